@@ -1,0 +1,501 @@
+"""Benchmark of the DeLS draft-scoring hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
+
+One JSON line (rank 0).  A *step* is one pass of the hot path over one batch:
+rank projection + fused long-logit / low-rank / prior scoring + argmax (+ for N > 1 the
+NCCL all-reduce(MAX) of the packed per-row keys and their decode).
+
+Workloads (seeded synthetic inputs, see dels_b200.workloads):
+  * N = 1 default: Qwen3-8B shape bf16, 32 x 16 = 512 rows, H = 4096, r = 256,
+    V = 151936 (the configuration the headline metric is quoted on);
+  * N > 1 default: the vocab-sharded large batch, 16384 rows, each rank owning a
+    contiguous vocabulary slice of W / Vr / prior (strong scaling: total work fixed);
+  * ``--workload cfg1|cfg2|cfg3|cfg4|cfg5`` selects any of the five explicitly.
+
+``value`` is device-timed (CUDA events, max over ranks) with inputs resident in HBM;
+``e2e`` is the same metric through the public API with the step's input rows copied
+from pinned host memory and the token ids copied back, inside the timed region.
+``roofline`` is the dominant kernel (the fused scorer) timed alone on its stream.
+``--impl reference`` times the reference formula (a torch restatement of
+code/kernel/dels.py:447-456 with the long logits of code/dflash.py:468) on the host
+cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "dels-spec_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "fused draft-score argmax rows/s @Qwen3-8B shape; % of TC/HBM roofline"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks() -> tuple[float, float, str]:
+    """(bf16 TFLOP/s burst, HBM GB/s, source)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"dels_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [x for x in sm if x > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- dist
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps: int, warmup: int, world: int, stream) -> float:
+    """ms for `steps` calls of fn, CUDA events on `stream`, barrier + sync both sides."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return start.elapsed_time(end)
+
+
+# ----------------------------------------------------------------------------- CPU reference
+def reference_rows_per_s(h, W, w_rank, Vr, prior, alpha_rows, beta_rows, reps: int) -> tuple[float, int]:
+    """Time the reference formula (torch on the host) on the given rows; returns rows/s."""
+    from oracle.reference_torch import score_rows
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    score_rows(h[:1], W, w_rank, Vr, prior, alpha_rows[:1], beta_rows[:1])  # warm caches
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        score_rows(h, W, w_rank, Vr, prior, alpha_rows, beta_rows)
+    dt = time.perf_counter() - t0
+    return h.shape[0] * reps / dt, torch.get_num_threads()
+
+
+def cpu_sample(wl, rows: int):
+    """The first `rows` rows of a dense workload, moved to the host (bounded CPU sample)."""
+    t = wl.tensors
+    pos = torch.arange(rows) % wl.n_pos
+    a = torch.tensor(wl.alpha, dtype=torch.float64)[pos]
+    b = torch.tensor(wl.beta, dtype=torch.float64)[pos]
+    h = t["h"][:rows].cpu()
+    return h, t["W"].cpu(), t["w_rank"].cpu(), t["Vr"].cpu(), t["prior"].cpu(), a, b
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args, rank, world, dev):
+    from dels_b200 import ops, workloads
+
+    pk_tflops, pk_gbs, pk_src = peaks()
+    stream = torch.cuda.current_stream(dev)
+    wname = args.workload if args.workload != "auto" else ("cfg2" if world == 1 else "cfg5")
+    sharded = world > 1
+    if wname in ("cfg1", "cfg2", "cfg5"):
+        V = workloads.VOCAB
+        v0, v1 = workloads.shard_range(V, world, rank) if sharded else (0, V)
+        gen = {"cfg1": workloads.cfg1, "cfg2": workloads.cfg2, "cfg5": workloads.cfg5}[wname]
+        wl = None if sharded else gen(device=dev)
+        if sharded:
+            base = {"cfg2": dict(rows=512, alpha=workloads.linspace(0.5, 0.1, 16), beta=workloads.linspace(0.3, 0.0, 16), seed=1),
+                    "cfg5": dict(rows=16384, alpha=[0.3], beta=[0.3], seed=4),
+                    "cfg1": None}[wname]
+            if base is None:
+                raise SystemExit("cfg1 (fp32, 16 rows) is single-GPU only")
+            wl = workloads.dense_workload(wname, H=4096, r=256, dtype=torch.bfloat16, device=dev, v_slice=(v0, v1),
+                                          **base)
+        t = wl.tensors
+        rows, H, r = wl.rows, wl.H, wl.r
+        Vloc = t["W"].shape[0]
+        fp32 = wl.dtype == torch.float32
+        out = ops.ScoreOut(tokens=torch.empty(rows, dtype=torch.int64, device=dev), scores=None,
+                           keys=torch.empty(rows, dtype=torch.int64, device=dev))
+        need = ops._lib.query("dels_score_f32_workspace_bytes" if fp32 else "dels_score_workspace_bytes",
+                              *((rows, r) if fp32 else (rows, H, r)))
+        ws = ops.Workspace(need, dev)
+        score = ops.draft_score_f32 if fp32 else ops.draft_score_bf16
+
+        def step(h=t["h"]):
+            score(h, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
+                  v_begin=v0, keys_only=sharded, out=out, ws=ws)
+            if sharded:
+                torch.distributed.all_reduce(out.keys, op=torch.distributed.ReduceOp.MAX)
+                ops.keys_decode(out.keys, tokens=out.tokens, with_scores=False)
+
+        launches_per_step = (3 if not fp32 else 2 + (rows + 15) // 16 + 1) + (1 if sharded else 0)
+        flops_main = 2.0 * rows * Vloc * (H + r)
+        bytes_main = (t["W"].numel() * t["W"].element_size() + t["Vr"].numel() * t["Vr"].element_size()
+                      + t["prior"].numel() * 4 + rows * (H + r) * t["h"].element_size() + rows * 8)
+        h_host = t["h"].cpu().pin_memory()
+        tok_host = torch.empty(rows, dtype=torch.int64).pin_memory()
+        h_dev = torch.empty_like(t["h"])
+        bi, bo = h_host.numel() * h_host.element_size(), tok_host.numel() * 8
+
+        def e2e_step():
+            h_dev.copy_(h_host, non_blocking=True)
+            step(h_dev)
+            tok_host.copy_(out.tokens, non_blocking=True)
+
+        # roofline: the scorer kernel alone (bf16: tcgen05 fused argmax; fp32: fp32 scorer pass)
+        if not fp32:
+            _, s_scaled = ops.rank_project_bf16(t["h"], t["w_rank"], t["alpha"], n_pos=wl.n_pos, want_state=False)
+            ks = ops.ScoreOut(tokens=torch.empty(rows, dtype=torch.int64, device=dev), scores=None,
+                              keys=torch.empty(rows, dtype=torch.int64, device=dev))
+            ops.keys_init(ks.keys)
+            mws = ops.Workspace(1 << 16, dev)
+
+            def main_kernel():
+                ops.fused_argmax_bf16(t["h"], t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=wl.n_pos,
+                                      v_begin=v0, keys_ready=True, out=ks, ws=mws)
+        else:
+            main_kernel = step
+    elif wname == "cfg3":
+        return run_ragged(args, rank, world, dev)
+    elif wname == "cfg4":
+        return run_rnn(args, rank, world, dev)
+    else:
+        raise SystemExit(f"unknown workload {wname}")
+
+    ops.init(dev)
+    clocks = ClockSampler(dev.index or 0)
+    clocks.start()
+    ms = timed(step, args.steps, args.warmup, world, stream)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, world, dev)
+    ms_e2e = max_over_ranks(timed(e2e_step, args.steps, args.warmup, world, stream), world, dev)
+    ms_main = timed(main_kernel, args.steps, args.warmup, 1, stream) / args.steps
+    ws.check()
+    bound = "hbm" if fp32 else "tensor"
+    if bound == "tensor":
+        achieved = flops_main / (ms_main * 1e-3) / 1e12
+        peak, unit = pk_tflops, "TFLOP/s"
+    else:
+        achieved = bytes_main / (ms_main * 1e-3) / 1e9
+        peak, unit = pk_gbs, "GB/s"
+    traffic = None
+    prof = ROOT / "profiles" / "traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get(wname if not sharded else f"{wname}_x{world}")
+    total_rows = wl.rows  # every rank scores all rows over its vocabulary slice
+    res = {
+        "metric": METRIC,
+        "value": total_rows * args.steps / (ms * 1e-3),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong" if sharded else "weak",
+        "vs_baseline": None,
+        "dtype": "f32" if fp32 else "bf16",
+        "data": "synthetic (seeded, shapes and distributions of the workload)",
+        "config": {
+            "workload": wl.name, "rows": rows, "H": H, "r": r, "V": workloads.VOCAB,
+            "vocab_per_rank": Vloc, "parallelism": f"vocab-shard x{world}" if sharded else "single",
+            "l2": "W alone is larger than L2 (streamed from HBM every step)",
+        },
+        "e2e": {"value": total_rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "traffic": traffic, "peak_source": f"{pk_src} (burst)",
+                     "kernel_ms": ms_main, "algorithmic": flops_main if bound == "tensor" else bytes_main},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        nrows = 16 if fp32 else 32
+        h, W, w_rank, Vr, prior, a, b = cpu_sample(wl, nrows)
+        rps, cores = reference_rows_per_s(h, W, w_rank, Vr, prior, a, b, reps=2)
+        res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
+                               "sample": f"{nrows} rows of the workload x 2 repetitions, full vocabulary, "
+                                         f"{str(wl.dtype).replace('torch.', '')} torch on the host"}
+    return res
+
+
+def run_ragged(args, rank, world, dev):
+    from dels_b200 import ops, workloads
+
+    if world > 1:
+        raise SystemExit("the ragged workload is single-GPU")
+    pk_tflops, _, pk_src = peaks()
+    wl = workloads.cfg3(device=dev)
+    t = wl.tensors
+    stream = torch.cuda.current_stream(dev)
+    n_seq, P = t["draft"].shape
+    acc = torch.empty(n_seq, dtype=torch.int32, device=dev)
+    off = torch.empty(n_seq + 1, dtype=torch.int32, device=dev)
+    packed = torch.empty(n_seq * P, wl.H, dtype=torch.bfloat16, device=dev)
+    row_pos = torch.zeros(n_seq * P, dtype=torch.int32, device=dev)
+    out = ops.ScoreOut(tokens=torch.empty(n_seq * P, dtype=torch.int64, device=dev), scores=None,
+                       keys=torch.empty(n_seq * P, dtype=torch.int64, device=dev))
+    ws = ops.Workspace(ops._lib.query("dels_score_workspace_bytes", n_seq * P, wl.H, wl.r), dev)
+
+    def step(draft=t["draft"], target=t["target"], hidden=t["hidden"]):
+        ops.accept_offsets(draft, target, accept=acc, offsets=off)
+        ops.pack_rows(hidden, acc, off, packed=packed, row_pos=row_pos)
+        ops.draft_score_bf16(packed, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=P,
+                             row_pos=row_pos, rows_dev=off[-1:], out=out, ws=ws)
+
+    ops.init(dev)
+    step()
+    torch.cuda.synchronize()
+    total = int(off[-1])
+    clocks = ClockSampler(dev.index or 0)
+    clocks.start()
+    ms = timed(step, args.steps, args.warmup, 1, stream)
+    clk = clocks.stop()
+    hh = {k: t[k].cpu().pin_memory() for k in ("draft", "target", "hidden")}
+    dd = {k: torch.empty_like(t[k]) for k in hh}
+    tok_host = torch.empty(n_seq * P, dtype=torch.int64).pin_memory()
+    acc_host = torch.empty(n_seq, dtype=torch.int32).pin_memory()
+
+    def e2e_step():
+        for k in hh:
+            dd[k].copy_(hh[k], non_blocking=True)
+        step(dd["draft"], dd["target"], dd["hidden"])
+        tok_host.copy_(out.tokens, non_blocking=True)
+        acc_host.copy_(acc, non_blocking=True)
+
+    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream)
+    flops = 2.0 * total * wl.V * (wl.H + wl.r)
+    _, s_scaled = ops.rank_project_bf16(packed[:total], t["w_rank"], t["alpha"], n_pos=P, row_pos=row_pos[:total],
+                                        want_state=False)
+    ks = ops.ScoreOut(tokens=torch.empty(total, dtype=torch.int64, device=dev), scores=None,
+                      keys=torch.empty(total, dtype=torch.int64, device=dev))
+    mws = ops.Workspace(1 << 16, dev)
+    main = lambda: ops.fused_argmax_bf16(packed[:total], t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=P,  # noqa: E731
+                                         row_pos=row_pos[:total], keys_ready=True, out=ks, ws=mws)
+    ops.keys_init(ks.keys)
+    ms_main = timed(main, args.steps, args.warmup, 1, stream) / args.steps
+    ws.check()
+    achieved = flops / (ms_main * 1e-3) / 1e12
+    return {
+        "metric": METRIC, "value": total * args.steps / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, shapes and distributions of the workload)",
+        "config": {"workload": wl.name, "sequences": n_seq, "draft": P, "accepted_rows": total, "H": wl.H, "r": wl.r,
+                   "V": wl.V, "l2": "W alone is larger than L2"},
+        "e2e": {"value": total * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in hh.values()),
+                "d2h_bytes_per_step": tok_host.numel() * 8 + acc_host.numel() * 4},
+        "gpu_launches": 5 * args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk_tflops, "unit": "TFLOP/s",
+                     "frac": achieved / pk_tflops, "traffic": None, "peak_source": f"{pk_src} (burst)",
+                     "kernel_ms": ms_main},
+        "clocks": clk,
+    }
+
+
+def run_rnn(args, rank, world, dev):
+    from dels_b200 import ops, workloads
+
+    if world > 1:
+        raise SystemExit("the RNN workload is single-GPU")
+    pk_tflops, _, pk_src = peaks()
+    wl = workloads.cfg4(device=dev)
+    t = wl.tensors
+    stream = torch.cuda.current_stream(dev)
+    rows = wl.rows
+    s_scaled = torch.empty(rows, wl.r, dtype=torch.bfloat16, device=dev)
+    out = ops.ScoreOut(tokens=torch.empty(rows, dtype=torch.int64, device=dev), scores=None,
+                       keys=torch.empty(rows, dtype=torch.int64, device=dev))
+    ws = ops.Workspace(ops._lib.query("dels_rnn_workspace_bytes", 512, 16, wl.H, wl.r), dev)
+    mws = ops.Workspace(1 << 16, dev)
+
+    def step(x=t["x"]):
+        ops.rnn_rank_states(x, t["w_in"], t["w_s"], t["bias"], t["alpha"], n_seq=512, T=16, s_scaled=s_scaled,
+                            keys=out.keys, ws=ws)
+        ops.fused_argmax_bf16(x, t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=16, keys_ready=True,
+                              out=out, ws=mws)
+
+    ops.init(dev)
+    clocks = ClockSampler(dev.index or 0)
+    clocks.start()
+    ms = timed(step, args.steps, args.warmup, 1, stream)
+    clk = clocks.stop()
+    x_host = t["x"].cpu().pin_memory()
+    x_dev = torch.empty_like(t["x"])
+    tok_host = torch.empty(rows, dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        step(x_dev)
+        tok_host.copy_(out.tokens, non_blocking=True)
+
+    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream)
+    ms_main = timed(lambda: ops.fused_argmax_bf16(t["x"], t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=16,
+                                                  keys_ready=True, out=out, ws=mws),
+                    args.steps, args.warmup, 1, stream) / args.steps
+    ws.check()
+    flops = 2.0 * rows * wl.V * (wl.H + wl.r)
+    achieved = flops / (ms_main * 1e-3) / 1e12
+    return {
+        "metric": METRIC, "value": rows * args.steps / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, shapes and distributions of the workload)",
+        "config": {"workload": wl.name, "rows": rows, "H": wl.H, "r": wl.r, "V": wl.V,
+                   "l2": "W alone is larger than L2"},
+        "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": rows * 8},
+        "gpu_launches": 3 * args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk_tflops, "unit": "TFLOP/s",
+                     "frac": achieved / pk_tflops, "traffic": None, "peak_source": f"{pk_src} (burst)",
+                     "kernel_ms": ms_main},
+        "clocks": clk,
+    }
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, dev):
+    """The reference's CPU formula on the host cores, same workload / metric / unit."""
+    from dels_b200 import workloads
+
+    wname = args.workload if args.workload != "auto" else "cfg2"
+    gen = {"cfg1": workloads.cfg1, "cfg2": workloads.cfg2, "cfg5": workloads.cfg5}.get(wname, workloads.cfg2)
+    gdev = dev if torch.cuda.is_available() else "cpu"
+    wl = gen(device=gdev)
+    nrows = 16 if wl.dtype == torch.float32 else 24
+    h, W, w_rank, Vr, prior, a, b = cpu_sample(wl, nrows)
+    del wl
+    torch.cuda.empty_cache() if torch.cuda.is_available() else None
+    rates = []
+    cores = 0
+    for i in range(args.warmup + args.steps):
+        rps, cores = reference_rows_per_s(h, W, w_rank, Vr, prior, a, b, reps=1)
+        if i >= args.warmup:
+            rates.append(rps)
+    rps = len(rates) / sum(1.0 / x for x in rates)
+    return {
+        "metric": METRIC, "value": rps, "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": nrows / rps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": str(h.dtype).replace("torch.", ""), "data": "synthetic (seeded)",
+        "config": {"workload": wname, "rows_per_step_sample": nrows},
+        "impl": "reference",
+        "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": f"{nrows} rows x full vocabulary per step, torch on the host"},
+        "e2e": {"value": rps, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="auto", choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = dist_env()
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+        print(json.dumps(run_reference(args, dev)), flush=True)
+        return
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        res = run_ours(args, rank, world, dev)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,689 @@
+// C ABI of the DeLS draft-scoring hot path: argument validation, tensor-map encoding,
+// grid sizing and kernel launches.  Declarations and the contract of every entry
+// point are in include/dels_b200.h.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "f32_score.cuh"
+#include "small_kernels.cuh"
+#include "tc_gemm.cuh"
+
+using namespace dels;
+
+namespace {
+
+constexpr int kVersion = 1;
+constexpr int kMaxDevices = 64;
+// Split-K sizing of the projection GEMMs aims at this many CTAs (one B200 wave).
+constexpr int kTargetCtas = 148;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DELS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define DELS_CHECK_LAUNCH(what)                    \
+  do {                                             \
+    cudaError_t e_ = cudaGetLastError();           \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+// ------------------------------------------------------------------ driver entry point
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_err = cudaSuccess;
+
+int ensure_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    g_encode_err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (g_encode_err == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr)
+    return fail(DELS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(g_encode_err));
+  return DELS_OK;
+}
+
+// 2-D bf16 tensor map over a row-major [outer, inner] matrix with leading dimension
+// `ld` elements, box = [box_outer rows, 64 elements], 128-byte swizzle, zero fill
+// outside the extents (so K, row and vocab tails need no special casing).
+int make_map_bf16(CUtensorMap* m, const void* ptr, long long inner, long long outer, long long ld, int box_outer) {
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DELS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for [%lld x %lld], ld %lld", (int)r, outer,
+                inner, ld);
+  return DELS_OK;
+}
+
+// ------------------------------------------------------------------ per-device state
+struct DeviceState {
+  bool ready = false;
+  int sm_count = 0;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+template <typename K>
+cudaError_t set_smem(K kernel, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes attr;
+  return cudaFuncGetAttributes(&attr, kernel);  // forces the module to load now
+}
+
+constexpr int kMaxSmem = 232448;
+
+int init_device(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(DELS_ERR_INVALID_ARG, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (g_dev[dev].ready) return DELS_OK;
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (prev != dev && (e = cudaSetDevice(dev)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  int major = 0, minor = 0, sms = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int rc = DELS_OK;
+  if (major != 10 || minor != 0) {
+    rc = fail(DELS_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev, major, minor);
+  } else {
+#define SET(k, b)                                            \
+  if (rc == DELS_OK && (e = set_smem(k, b)) != cudaSuccess) rc = cuda_fail(e, "kernel setup: " #k);
+    SET((tc_gemm_kernel<256, kArgmax, false>), TcConfig<256>::kSmemBytes);
+    SET((tc_gemm_kernel<256, kArgmax, true>), TcConfig<256>::kSmemBytes);
+    SET((tc_gemm_kernel<256, kStore, false>), TcConfig<256>::kSmemBytes);
+    SET((tc_gemm_kernel<128, kStore, false>), TcConfig<128>::kSmemBytes);
+    SET((tc_gemm_kernel<64, kStore, false>), TcConfig<64>::kSmemBytes);
+    SET((tc_gemm_kernel<32, kStore, false>), TcConfig<32>::kSmemBytes);
+    if (rc == DELS_OK && (e = f32_score_setup(kMaxSmem)) != cudaSuccess) rc = cuda_fail(e, "kernel setup: f32_score");
+    SET(rnn_recurrence_kernel, kMaxSmem);
+    SET(rank_finalize_kernel, 0);
+    SET(keys_init_kernel, 0);
+    SET(keys_decode_kernel, 0);
+    SET(accept_offsets_kernel, 0);
+    SET(pack_rows_kernel, 0);
+    SET(f32_rank_kernel, 0);
+#undef SET
+  }
+  if (rc == DELS_OK) {
+    g_dev[dev].sm_count = sms;
+    g_dev[dev].ready = true;
+  }
+  if (prev != dev) cudaSetDevice(prev);
+  return rc;
+}
+
+// Current device, initialised on first use.
+int current_device_state(DeviceState** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(DELS_ERR_INVALID_ARG, "device %d out of range", dev);
+  if (!g_dev[dev].ready) {
+    int rc = init_device(dev);
+    if (rc != DELS_OK) return rc;
+  }
+  *out = &g_dev[dev];
+  return DELS_OK;
+}
+
+struct WsHeader {
+  unsigned* counter;
+  int* status;
+};
+
+int ws_header(void* ws, size_t ws_bytes, size_t need, WsHeader* h) {
+  if (ws == nullptr || ws_bytes < need)
+    return fail(DELS_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", ws ? ws_bytes : (size_t)0, need);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(DELS_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  h->counter = reinterpret_cast<unsigned*>(ws);
+  h->status = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + 4);
+  return DELS_OK;
+}
+
+int check_bf16_matrix(const char* name, const void* p, long long ld, long long k) {
+  if (p == nullptr) return fail(DELS_ERR_INVALID_ARG, "%s is NULL", name);
+  if (!aligned16(p)) return fail(DELS_ERR_ALIGNMENT, "%s must be 16-byte aligned", name);
+  if (ld < k || (ld % 8) != 0)
+    return fail(DELS_ERR_ALIGNMENT, "%s: leading dimension %lld must be >= %lld and a multiple of 8", name, ld, k);
+  return DELS_OK;
+}
+
+// ------------------------------------------------------------------ tensor-core launches
+struct TcOperands {
+  const void* a0 = nullptr;
+  long long lda0 = 0;
+  const void* b0 = nullptr;
+  long long ldb0 = 0;
+  int K0 = 0;
+  const void* a1 = nullptr;
+  long long lda1 = 0;
+  const void* b1 = nullptr;
+  long long ldb1 = 0;
+  int K1 = 0;
+  int m_extent = 0;  // rows of A (capacity)
+  int n_extent = 0;  // rows of B
+};
+
+template <int BN, int MODE, bool VB>
+int launch_tc(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) {
+  int rc = ensure_encode();
+  if (rc != DELS_OK) return rc;
+  CUtensorMap ma0, mb0, ma1, mb1;
+  if (op.K1 > 0) {
+    if ((rc = make_map_bf16(&ma1, op.a1, op.K1, op.m_extent, op.lda1, kBM)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb1, op.b1, op.K1, op.n_extent, op.ldb1, BN)) != DELS_OK) return rc;
+  }
+  if (op.K0 > 0) {
+    if ((rc = make_map_bf16(&ma0, op.a0, op.K0, op.m_extent, op.lda0, kBM)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb0, op.b0, op.K0, op.n_extent, op.ldb0, BN)) != DELS_OK) return rc;
+  } else {
+    ma0 = ma1;
+    mb0 = mb1;
+  }
+  if (op.K1 == 0) {
+    ma1 = ma0;
+    mb1 = mb0;
+  }
+  args.kb0 = cdiv(op.K0, kBK);
+  args.kb1 = cdiv(op.K1, kBK);
+  const long long tiles = (long long)cdiv(op.m_extent, kBM) * cdiv(op.n_extent, BN) * args.k_splits;
+  const int grid = (int)(tiles < sm_count ? tiles : sm_count);
+  if (grid <= 0) return DELS_OK;
+  tc_gemm_kernel<BN, MODE, VB><<<grid, kTcThreads, TcConfig<BN>::kSmemBytes, st>>>(ma0, mb0, ma1, mb1, args);
+  DELS_CHECK_LAUNCH("tc_gemm_kernel launch");
+  return DELS_OK;
+}
+
+TcArgs blank_args() {
+  TcArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.k_splits = 1;
+  a.n_pos = 1;
+  return a;
+}
+
+// Split-K plan of a projection GEMM [rows, K] x [n, K]^T.
+struct SplitPlan {
+  int bn, splits, kb_per_split, ld_out;
+};
+
+SplitPlan plan_projection(int rows, int K, int n) {
+  SplitPlan p;
+  p.bn = n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : 256));
+  const int total_kb = cdiv(K, kBK);
+  const int base_tiles = cdiv(rows, kBM) * cdiv(n, p.bn);
+  int splits = cdiv(kTargetCtas, base_tiles);
+  const int max_splits = total_kb / 4 > 1 ? total_kb / 4 : 1;
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  p.kb_per_split = cdiv(total_kb, splits);
+  p.splits = cdiv(total_kb, p.kb_per_split);
+  p.ld_out = (n + 3) & ~3;
+  return p;
+}
+
+size_t projection_partials_bytes(int rows, int K, int n) {
+  const SplitPlan p = plan_projection(rows, K, n);
+  return align256((size_t)p.splits * rows * p.ld_out * sizeof(float));
+}
+
+// partial[split][row][n] = x[row, k-slice] . w[n, k-slice]
+int launch_projection(const void* x, long long ld_x, const void* w, long long ld_w, int rows, int K, int n,
+                      float* partials, int* status, int sm_count, cudaStream_t st, SplitPlan* plan_out) {
+  const SplitPlan p = plan_projection(rows, K, n);
+  TcOperands op;
+  op.a0 = x;
+  op.lda0 = ld_x;
+  op.b0 = w;
+  op.ldb0 = ld_w;
+  op.K0 = K;
+  op.m_extent = rows;
+  op.n_extent = n;
+  TcArgs a = blank_args();
+  a.m_rows = rows;
+  a.n_cols = n;
+  a.k_splits = p.splits;
+  a.kb_per_split = p.kb_per_split;
+  a.status = status;
+  a.out = partials;
+  a.ld_out = p.ld_out;
+  a.split_stride = (long long)rows * p.ld_out;
+  if (plan_out) *plan_out = p;
+  switch (p.bn) {
+    case 32: return launch_tc<32, kStore, false>(op, a, sm_count, st);
+    case 64: return launch_tc<64, kStore, false>(op, a, sm_count, st);
+    case 128: return launch_tc<128, kStore, false>(op, a, sm_count, st);
+    default: return launch_tc<256, kStore, false>(op, a, sm_count, st);
+  }
+}
+
+int check_common_score_args(int rows, int V, long long v_begin, const float* beta, const float* prior, int n_pos,
+                            const int* keys_present) {
+  if (rows < 0) return fail(DELS_ERR_INVALID_ARG, "rows must be >= 0 (got %d)", rows);
+  if (V <= 0) return fail(DELS_ERR_INVALID_ARG, "V must be > 0 (got %d)", V);
+  if (v_begin < 0 || v_begin + (long long)V > 0xFFFFFFFFll)
+    return fail(DELS_ERR_INVALID_ARG, "vocab range [%lld, %lld) exceeds the 32-bit index space", v_begin,
+                v_begin + V);
+  if (prior != nullptr && beta == nullptr) return fail(DELS_ERR_INVALID_ARG, "beta is NULL but prior is given");
+  if (n_pos <= 0) return fail(DELS_ERR_INVALID_ARG, "n_pos must be > 0 (got %d)", n_pos);
+  if (prior != nullptr && !aligned16(prior)) return fail(DELS_ERR_ALIGNMENT, "prior must be 16-byte aligned");
+  if (keys_present != nullptr && *keys_present == 0) return fail(DELS_ERR_INVALID_ARG, "keys is NULL");
+  return DELS_OK;
+}
+
+int fused_argmax_common(const void* h, long long ld_h, const void* W, long long ld_w, const void* base,
+                        long long ld_base, const void* s_scaled, long long ld_s, const void* Vr, long long ld_vr,
+                        const float* prior, const float* beta, int n_pos, const int32_t* row_pos, int rows,
+                        const int32_t* rows_dev, int H, int r, int V, long long v_begin, uint32_t flags,
+                        int64_t* keys, int64_t* idx_out, float* score_out, void* ws, size_t ws_bytes,
+                        cudaStream_t st) {
+  const int have_keys = keys != nullptr;
+  int rc = check_common_score_args(rows, V, v_begin, beta, prior, n_pos, &have_keys);
+  if (rc != DELS_OK) return rc;
+  if (H < 0 || r < 0 || (H == 0 && r == 0 && base == nullptr))
+    return fail(DELS_ERR_INVALID_ARG, "need H > 0 or r > 0 (H=%d, r=%d)", H, r);
+  if (H > 0) {
+    if ((rc = check_bf16_matrix("h", h, ld_h, H)) != DELS_OK) return rc;
+    if ((rc = check_bf16_matrix("W", W, ld_w, H)) != DELS_OK) return rc;
+  }
+  if (r > 0) {
+    if ((rc = check_bf16_matrix("s_scaled", s_scaled, ld_s, r)) != DELS_OK) return rc;
+    if ((rc = check_bf16_matrix("Vr", Vr, ld_vr, r)) != DELS_OK) return rc;
+  }
+  if (idx_out == nullptr && score_out != nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "score_out needs idx_out (use dels_keys_decode for keys-only calls)");
+  if (r == 0) return fail(DELS_ERR_UNSUPPORTED, "r must be > 0");
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, DELS_WS_HEADER_BYTES, &hdr)) != DELS_OK) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (rows == 0) return DELS_OK;
+
+  if ((flags & DELS_FLAG_KEYS_READY) == 0u) {
+    keys_init_kernel<<<cdiv(rows, 256) < 1024 ? cdiv(rows, 256) : 1024, 256, 0, st>>>(
+        reinterpret_cast<long long*>(keys), rows, hdr.counter);
+    DELS_CHECK_LAUNCH("keys_init_kernel launch");
+  }
+
+  TcOperands op;
+  op.a0 = h;
+  op.lda0 = ld_h;
+  op.b0 = W;
+  op.ldb0 = ld_w;
+  op.K0 = H;
+  op.a1 = s_scaled;
+  op.lda1 = ld_s;
+  op.b1 = Vr;
+  op.ldb1 = ld_vr;
+  op.K1 = r;
+  op.m_extent = rows;
+  op.n_extent = V;
+  TcArgs a = blank_args();
+  a.m_rows = rows;
+  a.m_rows_dev = rows_dev;
+  a.n_cols = V;
+  a.k_splits = 1;
+  a.kb_per_split = cdiv(H, kBK) + cdiv(r, kBK);
+  a.status = hdr.status;
+  a.v_begin = v_begin;
+  a.prior = prior;
+  a.beta = beta;
+  a.row_pos = row_pos;
+  a.n_pos = n_pos;
+  a.base = reinterpret_cast<const __nv_bfloat16*>(base);
+  a.ld_base = ld_base;
+  a.keys = reinterpret_cast<long long*>(keys);
+  a.idx_out = reinterpret_cast<long long*>(idx_out);
+  a.score_out = score_out;
+  a.counter = hdr.counter;
+  const bool vec_base = base != nullptr && aligned16(base) && (ld_base % 8) == 0;
+  if (vec_base) return launch_tc<256, kArgmax, true>(op, a, ds->sm_count, st);
+  return launch_tc<256, kArgmax, false>(op, a, ds->sm_count, st);
+}
+
+}  // namespace
+
+// ======================================================================== C ABI
+extern "C" {
+
+int dels_version(void) { return kVersion; }
+
+const char* dels_status_string(int status) {
+  switch (status) {
+    case DELS_OK: return "ok";
+    case DELS_ERR_INVALID_ARG: return "invalid argument";
+    case DELS_ERR_ALIGNMENT: return "misaligned pointer or leading dimension";
+    case DELS_ERR_WORKSPACE: return "workspace missing or too small";
+    case DELS_ERR_CUDA: return "CUDA error";
+    case DELS_ERR_UNSUPPORTED: return "unsupported configuration";
+    case DELS_ERR_DEVICE_TIMEOUT: return "a device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* dels_last_error(void) { return g_last_error.c_str(); }
+
+int dels_init(int device) { return init_device(device); }
+
+int dels_sm_count(int device) {
+  if (device < 0 || device >= kMaxDevices) return fail(DELS_ERR_INVALID_ARG, "device out of range");
+  int rc = init_device(device);
+  if (rc != DELS_OK) return rc;
+  return g_dev[device].sm_count;
+}
+
+size_t dels_rank_workspace_bytes(int rows, int K, int r) {
+  if (rows <= 0 || K <= 0 || r <= 0) return DELS_WS_HEADER_BYTES;
+  return DELS_WS_HEADER_BYTES + projection_partials_bytes(rows, K, r);
+}
+
+int dels_rank_project_bf16(const void* x, int64_t ld_x, const void* w_rank, int64_t ld_w, int rows, int K, int r,
+                           int activation, const float* alpha, int n_pos, const int32_t* row_pos, void* s_out,
+                           void* s_scaled, int64_t* keys, void* ws, size_t ws_bytes, void* stream) {
+  int rc;
+  if (rows < 0 || K <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape rows=%d K=%d r=%d", rows, K, r);
+  if (activation != DELS_ACT_IDENTITY && activation != DELS_ACT_SILU)
+    return fail(DELS_ERR_INVALID_ARG, "unsupported rank activation %d", activation);
+  if (n_pos <= 0) return fail(DELS_ERR_INVALID_ARG, "n_pos must be > 0");
+  if (s_scaled == nullptr) return fail(DELS_ERR_INVALID_ARG, "s_scaled is NULL");
+  if ((rc = check_bf16_matrix("x", x, ld_x, K)) != DELS_OK) return rc;
+  if ((rc = check_bf16_matrix("w_rank", w_rank, ld_w, K)) != DELS_OK) return rc;
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, dels_rank_workspace_bytes(rows, K, r), &hdr)) != DELS_OK) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (rows == 0) return DELS_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + DELS_WS_HEADER_BYTES);
+  SplitPlan plan;
+  if ((rc = launch_projection(x, ld_x, w_rank, ld_w, rows, K, r, partials, hdr.status, ds->sm_count, st, &plan)) !=
+      DELS_OK)
+    return rc;
+  const long long total = (long long)rows * r;
+  const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
+  rank_finalize_kernel<<<grid, 256, 0, st>>>(partials, plan.splits, (long long)rows * plan.ld_out, plan.ld_out, rows,
+                                             r, activation, alpha, n_pos, row_pos,
+                                             reinterpret_cast<__nv_bfloat16*>(s_out),
+                                             reinterpret_cast<__nv_bfloat16*>(s_scaled),
+                                             reinterpret_cast<long long*>(keys), hdr.counter);
+  DELS_CHECK_LAUNCH("rank_finalize_kernel launch");
+  return DELS_OK;
+}
+
+int dels_fused_argmax_bf16(const void* h, int64_t ld_h, const void* W, int64_t ld_w, const void* s_scaled,
+                           int64_t ld_s, const void* Vr, int64_t ld_vr, const float* prior, const float* beta,
+                           int n_pos, const int32_t* row_pos, int rows, const int32_t* rows_dev, int H, int r,
+                           int V, int64_t v_begin, uint32_t flags, int64_t* keys, int64_t* idx_out,
+                           float* score_out, void* ws, size_t ws_bytes, void* stream) {
+  if (H <= 0) return fail(DELS_ERR_INVALID_ARG, "H must be > 0 (use dels_fused_argmax_base_bf16 without W.h)");
+  return fused_argmax_common(h, ld_h, W, ld_w, nullptr, 0, s_scaled, ld_s, Vr, ld_vr, prior, beta, n_pos, row_pos,
+                             rows, rows_dev, H, r, V, v_begin, flags, keys, idx_out, score_out, ws, ws_bytes,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dels_fused_argmax_base_bf16(const void* base, int64_t ld_base, const void* s_scaled, int64_t ld_s,
+                                const void* Vr, int64_t ld_vr, const float* prior, const float* beta, int n_pos,
+                                const int32_t* row_pos, int rows, const int32_t* rows_dev, int r, int V,
+                                int64_t v_begin, uint32_t flags, int64_t* keys, int64_t* idx_out,
+                                float* score_out, void* ws, size_t ws_bytes, void* stream) {
+  if (base == nullptr) return fail(DELS_ERR_INVALID_ARG, "base is NULL");
+  if (ld_base < V) return fail(DELS_ERR_INVALID_ARG, "ld_base %lld < V %d", (long long)ld_base, V);
+  if (r <= 0) return fail(DELS_ERR_INVALID_ARG, "r must be > 0");
+  return fused_argmax_common(nullptr, 0, nullptr, 0, base, ld_base, s_scaled, ld_s, Vr, ld_vr, prior, beta, n_pos,
+                             row_pos, rows, rows_dev, 0, r, V, v_begin, flags, keys, idx_out, score_out, ws,
+                             ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dels_score_workspace_bytes(int rows, int H, int r) {
+  if (rows <= 0 || H <= 0 || r <= 0) return DELS_WS_HEADER_BYTES;
+  return DELS_WS_HEADER_BYTES + align256((size_t)rows * 8) + align256((size_t)rows * r * 2) +
+         projection_partials_bytes(rows, H, r);
+}
+
+int dels_draft_score_bf16(const void* h, int64_t ld_h, const void* W, int64_t ld_w, const void* w_rank,
+                          int64_t ld_wr, const void* Vr, int64_t ld_vr, const float* prior, const float* alpha,
+                          const float* beta, int n_pos, const int32_t* row_pos, int rows, const int32_t* rows_dev,
+                          int H, int r, int V, int64_t v_begin, int activation, int64_t* keys, int64_t* idx_out,
+                          float* score_out, void* ws, size_t ws_bytes, void* stream) {
+  int rc;
+  if (rows < 0 || H <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape rows=%d H=%d r=%d", rows, H, r);
+  const size_t need = dels_score_workspace_bytes(rows, H, r);
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, need, &hdr)) != DELS_OK) return rc;
+  if (rows == 0) return DELS_OK;
+  char* base = reinterpret_cast<char*>(ws);
+  int64_t* ws_keys = reinterpret_cast<int64_t*>(base + DELS_WS_HEADER_BYTES);
+  void* s_scaled = base + DELS_WS_HEADER_BYTES + align256((size_t)rows * 8);
+  // The rank projection's partials live after s_scaled; hand it a view of the
+  // workspace whose header is shared with this call.
+  const size_t part_off = DELS_WS_HEADER_BYTES + align256((size_t)rows * 8) + align256((size_t)rows * r * 2);
+  if (keys == nullptr) keys = ws_keys;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if ((rc = check_bf16_matrix("h", h, ld_h, H)) != DELS_OK) return rc;
+  if ((rc = check_bf16_matrix("w_rank", w_rank, ld_wr, H)) != DELS_OK) return rc;
+  if (activation != DELS_ACT_IDENTITY && activation != DELS_ACT_SILU)
+    return fail(DELS_ERR_INVALID_ARG, "unsupported rank activation %d", activation);
+  const int have_keys = 1;
+  if ((rc = check_common_score_args(rows, V, v_begin, beta, prior, n_pos, &have_keys)) != DELS_OK) return rc;
+  float* partials = reinterpret_cast<float*>(base + part_off);
+  SplitPlan plan;
+  if ((rc = launch_projection(h, ld_h, w_rank, ld_wr, rows, H, r, partials, hdr.status, ds->sm_count, st, &plan)) !=
+      DELS_OK)
+    return rc;
+  const long long total = (long long)rows * r;
+  const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
+  rank_finalize_kernel<<<grid, 256, 0, st>>>(partials, plan.splits, (long long)rows * plan.ld_out, plan.ld_out, rows,
+                                             r, activation, alpha, n_pos, row_pos, nullptr,
+                                             reinterpret_cast<__nv_bfloat16*>(s_scaled),
+                                             reinterpret_cast<long long*>(keys), hdr.counter);
+  DELS_CHECK_LAUNCH("rank_finalize_kernel launch");
+  return fused_argmax_common(h, ld_h, W, ld_w, nullptr, 0, s_scaled, r, Vr, ld_vr, prior, beta, n_pos, row_pos,
+                             rows, rows_dev, H, r, V, v_begin, DELS_FLAG_KEYS_READY, keys, idx_out, score_out, ws,
+                             ws_bytes, st);
+}
+
+size_t dels_score_f32_workspace_bytes(int rows, int r) {
+  if (rows <= 0 || r <= 0) return DELS_WS_HEADER_BYTES;
+  return DELS_WS_HEADER_BYTES + align256((size_t)rows * 8) + align256((size_t)rows * r * 4);
+}
+
+int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t ld_w, const float* w_rank,
+                         int64_t ld_wr, const float* Vr, int64_t ld_vr, const float* prior, const float* alpha,
+                         const float* beta, int n_pos, const int32_t* row_pos, int rows, int H, int r, int V,
+                         int64_t v_begin, int64_t* keys, int64_t* idx_out, float* score_out, void* ws,
+                         size_t ws_bytes, void* stream) {
+  int rc;
+  if (rows < 0 || H <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape rows=%d H=%d r=%d", rows, H, r);
+  if ((H % 4) != 0 || (r % 4) != 0)
+    return fail(DELS_ERR_UNSUPPORTED, "fp32 scorer needs H %% 4 == 0 and r %% 4 == 0 (H=%d, r=%d)", H, r);
+  if (h == nullptr || W == nullptr || w_rank == nullptr || Vr == nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "NULL operand");
+  if (!aligned16(W) || !aligned16(Vr) || (ld_w % 4) != 0 || (ld_vr % 4) != 0 || ld_w < H || ld_vr < r || ld_h < H ||
+      ld_wr < H)
+    return fail(DELS_ERR_ALIGNMENT, "fp32 W / Vr need 16-byte aligned rows (ld %% 4 == 0)");
+  const int have_keys = 1;
+  if ((rc = check_common_score_args(rows, V, v_begin, beta, prior, n_pos, &have_keys)) != DELS_OK) return rc;
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, dels_score_f32_workspace_bytes(rows, r), &hdr)) != DELS_OK) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (rows == 0) return DELS_OK;
+  if (idx_out == nullptr && score_out != nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "score_out needs idx_out (use dels_keys_decode for keys-only calls)");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* base = reinterpret_cast<char*>(ws);
+  if (keys == nullptr) keys = reinterpret_cast<int64_t*>(base + DELS_WS_HEADER_BYTES);
+  float* s_scaled = reinterpret_cast<float*>(base + DELS_WS_HEADER_BYTES + align256((size_t)rows * 8));
+
+  {
+    const int warps = rows * r;
+    const int grid = cdiv(warps, 8) < 8 * ds->sm_count ? cdiv(warps, 8) : 8 * ds->sm_count;
+    f32_rank_kernel<<<grid, 256, 0, st>>>(h, ld_h, w_rank, ld_wr, rows, H, r, alpha, n_pos, row_pos, s_scaled,
+                                          reinterpret_cast<long long*>(keys), hdr.counter);
+    DELS_CHECK_LAUNCH("f32_rank_kernel launch");
+  }
+  const int kp = f32_padded_k(H, r);
+  int rows_per_pass = 16;
+  while (rows_per_pass > 4 && (size_t)rows_per_pass * kp * 4 > (size_t)kMaxSmem) rows_per_pass /= 2;
+  if ((size_t)rows_per_pass * kp * 4 > (size_t)kMaxSmem)
+    return fail(DELS_ERR_UNSUPPORTED, "fp32 scorer: H + r = %d too large for shared memory", H + r);
+  const size_t smem = (size_t)rows_per_pass * kp * 4;
+  for (int row0 = 0; row0 < rows; row0 += rows_per_pass) {
+    const int nrows = rows - row0 < rows_per_pass ? rows - row0 : rows_per_pass;
+    const int grid = ds->sm_count;
+    cudaError_t e = f32_score_launch(rows_per_pass, grid, smem, st, h, ld_h, s_scaled, W, ld_w, Vr, ld_vr, prior, beta,
+                                     n_pos, row_pos, row0, nrows, H, r, V, v_begin, reinterpret_cast<long long*>(keys));
+    if (e != cudaSuccess) return cuda_fail(e, "f32_score_kernel launch");
+  }
+  if (idx_out != nullptr) {
+    keys_decode_kernel<<<cdiv(rows, 256), 256, 0, st>>>(reinterpret_cast<const long long*>(keys), rows, nullptr,
+                                                        reinterpret_cast<long long*>(idx_out), score_out);
+    DELS_CHECK_LAUNCH("keys_decode_kernel launch");
+  }
+  return DELS_OK;
+}
+
+int dels_keys_init(int64_t* keys, int rows, void* ws, void* stream) {
+  if (keys == nullptr || rows < 0) return fail(DELS_ERR_INVALID_ARG, "keys NULL or rows < 0");
+  unsigned* counter = nullptr;
+  if (ws != nullptr) {
+    if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(DELS_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    counter = reinterpret_cast<unsigned*>(ws);
+  }
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (rows == 0 && counter == nullptr) return DELS_OK;
+  const int grid = rows > 0 ? (cdiv(rows, 256) < 1024 ? cdiv(rows, 256) : 1024) : 1;
+  keys_init_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(reinterpret_cast<long long*>(keys),
+                                                                            rows, counter);
+  DELS_CHECK_LAUNCH("keys_init_kernel launch");
+  return DELS_OK;
+}
+
+int dels_keys_decode(const int64_t* keys, int rows, const int32_t* rows_dev, int64_t* idx_out, float* score_out,
+                     void* stream) {
+  if (keys == nullptr || rows < 0) return fail(DELS_ERR_INVALID_ARG, "keys NULL or rows < 0");
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (rows == 0) return DELS_OK;
+  const int grid = cdiv(rows, 256) < 1024 ? cdiv(rows, 256) : 1024;
+  keys_decode_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const long long*>(keys), rows, rows_dev, reinterpret_cast<long long*>(idx_out), score_out);
+  DELS_CHECK_LAUNCH("keys_decode_kernel launch");
+  return DELS_OK;
+}
+
+int dels_accept_offsets(const int64_t* draft, int64_t ld_draft, const int64_t* target, int64_t ld_target,
+                        int n_seq, int n_draft, int commit_extra, int32_t* accept, int32_t* offsets, void* stream) {
+  if (n_seq < 0 || n_draft < 0) return fail(DELS_ERR_INVALID_ARG, "n_seq and n_draft must be >= 0");
+  if (commit_extra != 0 && commit_extra != 1) return fail(DELS_ERR_INVALID_ARG, "commit_extra must be 0 or 1");
+  if (accept == nullptr || offsets == nullptr) return fail(DELS_ERR_INVALID_ARG, "accept / offsets is NULL");
+  if (n_seq > 0 && n_draft > 0 && (draft == nullptr || target == nullptr))
+    return fail(DELS_ERR_INVALID_ARG, "draft / target is NULL");
+  if (ld_draft < n_draft || ld_target < n_draft)
+    return fail(DELS_ERR_INVALID_ARG, "leading dimensions must be >= n_draft");
+  if ((long long)n_seq * (n_draft + commit_extra) > 0x7FFFFFFFll)
+    return fail(DELS_ERR_INVALID_ARG, "packed row count overflows int32");
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  accept_offsets_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const long long*>(draft), ld_draft, reinterpret_cast<const long long*>(target), ld_target,
+      n_seq, n_draft, commit_extra, accept, offsets);
+  DELS_CHECK_LAUNCH("accept_offsets_kernel launch");
+  return DELS_OK;
+}
+
+int dels_pack_rows_bf16(const void* hidden, int64_t ld_seq, int64_t ld_row, int n_seq, int P, int H,
+                        const int32_t* accept, const int32_t* offsets, void* packed, int64_t ld_packed,
+                        int32_t* row_pos, void* stream) {
+  if (n_seq < 0 || P <= 0 || H <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape n_seq=%d P=%d H=%d", n_seq, P, H);
+  if (hidden == nullptr || accept == nullptr || offsets == nullptr || packed == nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if (ld_row < H || ld_seq < (long long)P * ld_row - (ld_row - H) || ld_packed < H)
+    return fail(DELS_ERR_INVALID_ARG, "inconsistent strides");
+  if ((long long)n_seq * P > 0x7FFFFFFFll) return fail(DELS_ERR_INVALID_ARG, "too many rows");
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (n_seq == 0) return DELS_OK;
+  pack_rows_kernel<<<n_seq * P, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(hidden), ld_seq, ld_row, n_seq, P, H, accept, offsets,
+      reinterpret_cast<__nv_bfloat16*>(packed), ld_packed, row_pos);
+  DELS_CHECK_LAUNCH("pack_rows_kernel launch");
+  return DELS_OK;
+}
+
+size_t dels_rnn_workspace_bytes(int n_seq, int T, int H, int r) {
+  if (n_seq <= 0 || T <= 0 || H <= 0 || r <= 0) return DELS_WS_HEADER_BYTES;
+  return DELS_WS_HEADER_BYTES + projection_partials_bytes(n_seq * T, H, r);
+}
+
+int dels_rnn_rank_states_bf16(const void* x, int64_t ld_x, const void* w_in, int64_t ld_win, const void* w_s,
+                              const float* bias, const float* alpha, int n_seq, int T, int H, int r,
+                              void* s_scaled, void* s_out, int64_t* keys, void* ws, size_t ws_bytes,
+                              void* stream) {
+  int rc;
+  if (n_seq < 0 || T <= 0 || H <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape");
+  if (r > 256 || (r % 2) != 0) return fail(DELS_ERR_UNSUPPORTED, "RNN rank r must be even and <= 256 (got %d)", r);
+  if (w_s == nullptr || s_scaled == nullptr) return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if ((long long)n_seq * T > 0x7FFFFFFFll) return fail(DELS_ERR_INVALID_ARG, "too many rows");
+  if ((rc = check_bf16_matrix("x", x, ld_x, H)) != DELS_OK) return rc;
+  if ((rc = check_bf16_matrix("w_in", w_in, ld_win, H)) != DELS_OK) return rc;
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, dels_rnn_workspace_bytes(n_seq, T, H, r), &hdr)) != DELS_OK) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (n_seq == 0) return DELS_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int rows = n_seq * T;
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + DELS_WS_HEADER_BYTES);
+  SplitPlan plan;
+  if ((rc = launch_projection(x, ld_x, w_in, ld_win, rows, H, r, partials, hdr.status, ds->sm_count, st, &plan)) !=
+      DELS_OK)
+    return rc;
+  rnn_recurrence_kernel<<<cdiv(n_seq, kRnnSeqs), 256, rnn_smem_bytes(r), st>>>(
+      partials, plan.splits, (long long)rows * plan.ld_out, plan.ld_out,
+      reinterpret_cast<const __nv_bfloat16*>(w_s), bias, alpha, n_seq, T, r,
+      reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<__nv_bfloat16*>(s_out),
+      reinterpret_cast<long long*>(keys), hdr.counter);
+  DELS_CHECK_LAUNCH("rnn_recurrence_kernel launch");
+  return DELS_OK;
+}
+
+}  // extern "C"

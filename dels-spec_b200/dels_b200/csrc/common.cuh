@@ -1,0 +1,263 @@
+// Shared device helpers for the DeLS draft-scoring kernels (sm_100a only).
+//
+// Everything here is hand-written inline PTX for the Blackwell async machinery the
+// kernels use: mbarriers with bounded waits, TMA tile loads, and the tcgen05
+// tensor-core / tensor-memory instructions.  Also the packed (score, index) key that
+// turns "argmax with the lowest index on ties" into a single signed 64-bit max, which
+// both the in-kernel atomics and the cross-rank NCCL all-reduce(MAX) use.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../../include/dels_b200.h"
+
+namespace dels {
+
+// A single mbarrier wait gives up after this long (the whole kernel normally runs in
+// well under a millisecond per wave).  On expiry the kernel records
+// DELS_ERR_DEVICE_TIMEOUT in the caller's status word, tells the other roles of the CTA
+// to stop, and returns; the host reads the status after synchronising.
+constexpr unsigned long long kWaitLimitNs = 2000ull * 1000ull * 1000ull;
+
+// --------------------------------------------------------------------------------
+// Packed argmax keys.
+//
+// key = (ordered_i32(score) << 32) | (0xFFFFFFFF - index)
+//
+// ordered_i32 maps IEEE floats to int32 so that signed integer order equals float
+// order.  The low word is the complemented index, so among equal scores the lowest
+// index has the largest key: max(key) is torch.argmax's "first occurrence" rule
+// (reference: code/kernel/dels.py:134 strict '>' and torch.argmax in
+// code/kernel/dels.py:456).  NaN maps above +inf, so a NaN score wins like it does in
+// torch.argmax; -0.0 is folded onto +0.0 so that the two compare equal as in torch.
+// --------------------------------------------------------------------------------
+__host__ __device__ __forceinline__ int32_t ordered_i32(float f) {
+  if (f != f) return 0x7FFFFFFF;
+  if (f == 0.0f) f = 0.0f;
+#ifdef __CUDA_ARCH__
+  int32_t i = __float_as_int(f);
+#else
+  int32_t i;
+  __builtin_memcpy(&i, &f, 4);
+#endif
+  return i < 0 ? (i ^ 0x7FFFFFFF) : i;
+}
+
+__host__ __device__ __forceinline__ float ordered_to_float(int32_t o) {
+  int32_t i = o < 0 ? (o ^ 0x7FFFFFFF) : o;
+#ifdef __CUDA_ARCH__
+  return __int_as_float(i);
+#else
+  float f;
+  __builtin_memcpy(&f, &i, 4);
+  return f;
+#endif
+}
+
+__host__ __device__ __forceinline__ long long pack_key(float score, uint32_t index) {
+  return (long long)(((unsigned long long)(uint32_t)ordered_i32(score) << 32) |
+                     (unsigned long long)(0xFFFFFFFFu - index));
+}
+
+__host__ __device__ __forceinline__ uint32_t key_index(long long key) {
+  return 0xFFFFFFFFu - (uint32_t)((unsigned long long)key & 0xFFFFFFFFull);
+}
+
+__host__ __device__ __forceinline__ float key_score(long long key) {
+  return ordered_to_float((int32_t)((unsigned long long)key >> 32));
+}
+
+constexpr long long kKeyEmpty = (long long)0x8000000000000000ull;
+
+// "take" rule of a sequential scan in increasing index order: strictly greater wins,
+// a NaN beats any non-NaN, and the first NaN is kept.
+__device__ __forceinline__ bool scan_takes(float s, float best) {
+  return (s > best) || ((s != s) && (best == best));
+}
+
+// Row position (the draft-block slot that selects alpha_p / beta_p).
+__device__ __forceinline__ int row_position(const int* row_pos, int row, int n_pos) {
+  return row_pos != nullptr ? row_pos[row] : (row % n_pos);
+}
+
+// --------------------------------------------------------------------------------
+// Shared-memory addresses, timers
+// --------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// --------------------------------------------------------------------------------
+// mbarrier
+// --------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete.  Returns false if the CTA's
+// abort flag is raised or the wait runs past kWaitLimitNs; in the latter case this
+// thread raises the abort flag and records DELS_ERR_DEVICE_TIMEOUT in *status.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (status != nullptr) atomicCAS(status, 0, DELS_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------------
+// TMA (tensor tile copies global -> shared, completion counted on an mbarrier)
+// --------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x,
+                                            int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// --------------------------------------------------------------------------------
+// tcgen05: tensor memory, MMA, commit, loads
+// --------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Arrive (once) on an mbarrier when every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, fp32 accumulator.
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: bf16 A and B (both K-major),
+// fp32 accumulator, shape M x N.
+__host__ __device__ constexpr uint32_t make_idesc_bf16_f32(int M, int N) {
+  return (1u << 4)                        // accumulator format: f32
+         | (1u << 7)                      // A format: bf16
+         | (1u << 10)                     // B format: bf16
+         | ((uint32_t)(N >> 3) << 17)     // N / 8
+         | ((uint32_t)(M >> 4) << 24);    // M / 16
+}
+
+// Shared-memory matrix descriptor for a K-major bf16 tile written by TMA with the
+// 128-byte swizzle: rows of 64 elements (128 B), 8-row swizzle atoms 1024 B apart.
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);  // start address / 16
+  d |= (uint64_t)1 << 16;                         // leading byte offset (unused with swizzle)
+  d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset: 8 rows * 128 B
+  d |= (uint64_t)1 << 46;                         // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;                         // layout: 128-byte swizzle
+  return d;
+}
+
+// Load 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+
+// Wait for this thread's outstanding tcgen05.ld, then pin the loaded registers after
+// the wait so that no consumer is scheduled ahead of it.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&v)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(v[i]));
+}
+
+// --------------------------------------------------------------------------------
+// bf16 helpers
+// --------------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+}  // namespace dels

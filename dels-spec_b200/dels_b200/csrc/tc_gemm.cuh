@@ -1,0 +1,419 @@
+// Persistent warp-specialised tcgen05 GEMM with two epilogues (sm_100a).
+//
+//   D[m, n] = sum_k A[m, k] * B[n, k]        A, B bf16 K-major, D fp32 in TMEM
+//
+// The K range is the concatenation of two segments, each with its own pair of TMA
+// maps: segment 0 (A0, B0) for kb0 k-blocks, then segment 1 (A1, B1) for kb1
+// k-blocks.  The draft-scoring kernel uses this to fold both contractions of
+//
+//   score[row, v] = sum_k h[row, k] W[v, k]  +  alpha_p * sum_j s[row, j] Vr[v, j]
+//
+// into ONE accumulator: segment 0 is (h, W) over H, segment 1 is (alpha_p * s, Vr)
+// over r (the per-row alpha is folded into the bf16 rank state before the call).
+// Reference: code/kernel/dels.py:49-79 (the low-rank part) and code/dflash.py:468 (the
+// long-logit GEMM, which the reference materialises and this kernel does not).
+//
+// Tile: 128 rows (TMEM lanes) x BN columns (TMEM columns), 64-element K blocks staged
+// by TMA into 128-byte-swizzled shared memory, accumulators double-buffered in TMEM
+// so the epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA
+// issuer (one thread), warps 2..5 = epilogue (one thread per accumulator row).
+//
+// Epilogues:
+//   kArgmax : score = acc (+ base[row, v]) - beta_p * prior[v]; running (max, first
+//             index) over the tile's columns in registers, then one 64-bit atomicMax
+//             of the packed key per (row, tile).  The last CTA to finish decodes the
+//             keys into int64 token ids (optional).
+//   kStore  : write the fp32 accumulator tile to out[split][row][n] (split-K partial
+//             sums; used by the rank projection and the RNN input projection).
+#pragma once
+
+#include "common.cuh"
+
+namespace dels {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kTcThreads = 192;
+
+enum TcEpilogue { kArgmax = 0, kStore = 1 };
+
+struct TcArgs {
+  int m_rows;              // rows of A (capacity)
+  const int* m_rows_dev;   // optional device-side row count (clamped to m_rows)
+  int n_cols;              // rows of B (vocab slice length, or r for the projection)
+  int kb0, kb1;            // k-blocks in segment 0 and segment 1
+  int k_splits;            // split-K factor (kStore only; 1 for kArgmax)
+  int kb_per_split;
+  int* status;             // device error word (0 = ok)
+  // kArgmax
+  long long v_begin;       // global vocab index of column 0 of B
+  const float* prior;      // [n_cols] fp32 or null (beta term skipped)
+  const float* beta;       // [n_pos]
+  const int* row_pos;      // [m_rows] position of each row, or null (row % n_pos)
+  int n_pos;
+  const __nv_bfloat16* base;  // base logits: base[row * ld_base + v] or null
+  long long ld_base;
+  long long* keys;         // [m_rows] packed keys, pre-filled with kKeyEmpty
+  long long* idx_out;      // [m_rows] decoded token ids, or null (keys are left for a combine)
+  float* score_out;        // [m_rows] winning scores, or null
+  unsigned* counter;       // zero on entry; the last CTA resets it
+  // kStore
+  float* out;
+  long long ld_out;
+  long long split_stride;
+};
+
+template <int BN>
+struct TcConfig {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int kAccCols = 2 * BN;
+  static constexpr int kTmemCols =
+      kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kNumBars = 2 * kStages + 4;
+  static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct TileCoord {
+  int m_tile, n_tile, split;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int k_splits) {
+  TileCoord c;
+  c.m_tile = t % num_m;
+  const int rest = t / num_m;
+  c.split = rest % k_splits;
+  c.n_tile = rest / k_splits;
+  return c;
+}
+
+template <int BN, int MODE, bool VEC_BASE>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                   const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                   const TcArgs args) {
+  using Cfg = TcConfig<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_addr - raw_addr);
+  const uint32_t a_base = base_addr;
+  const uint32_t b_base = base_addr + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[S + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * S + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * S + 2 + a]); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  int m_rows = args.m_rows;
+  if (args.m_rows_dev != nullptr) {
+    const int d = *args.m_rows_dev;
+    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
+  }
+  const int num_m = (m_rows + kBM - 1) / kBM;
+  const int num_n = (args.n_cols + BN - 1) / BN;
+  const int total_kb = args.kb0 + args.kb1;
+  const int num_tiles = num_m * num_n * args.k_splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4 * 32);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&map_a0);
+    tma_prefetch_map(&map_b0);
+    tma_prefetch_map(&map_a1);
+    tma_prefetch_map(&map_b1);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = tile_coord(t, num_m, args.k_splits);
+        const int kb_begin = tc.split * args.kb_per_split;
+        const int kb_end = min(total_kb, kb_begin + args.kb_per_split);
+        const int m0 = tc.m_tile * kBM;
+        const int n0 = tc.n_tile * BN;
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
+          const uint32_t a_dst = a_base + stage * Cfg::kABytes;
+          const uint32_t b_dst = b_base + stage * Cfg::kBBytes;
+          if (kb < args.kb0) {
+            tma_load_2d(a_dst, &map_a0, full_bar(stage), kb * kBK, m0);
+            tma_load_2d(b_dst, &map_b0, full_bar(stage), kb * kBK, n0);
+          } else {
+            const int k1 = kb - args.kb0;
+            tma_load_2d(a_dst, &map_a1, full_bar(stage), k1 * kBK, m0);
+            tma_load_2d(b_dst, &map_b1, full_bar(stage), k1 * kBK, n0);
+          }
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Aborting: let the copies already in flight land before the CTA exits.
+        const int outstanding = issued < S ? issued : S;
+        int s = stage;
+        uint32_t p = phase;
+        for (int i = 0; i < outstanding; ++i) {
+          if (--s < 0) {
+            s = S - 1;
+            p ^= 1u;
+          }
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(full_bar(s), p) && globaltimer_ns() - t0 < kWaitLimitNs / 20) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = tile_coord(t, num_m, args.k_splits);
+        const int kb_begin = tc.split * args.kb_per_split;
+        const int kb_end = min(total_kb, kb_begin + args.kb_per_split);
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag, args.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_desc(a_base + stage * Cfg::kABytes);
+          const uint64_t bdesc = make_sw128_desc(b_base + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes per 16-element K step inside the 128-byte swizzled row.
+            tc_mma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                        (kb > kb_begin || k > 0) ? 1u : 0u);
+          }
+          tc_commit(empty_bar(stage));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(tfull_bar(acc));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Drain: wait until every MMA this thread issued has completed before TMEM is
+      // released (the normal path has already observed this through tfull).
+      if (!ok || *abort_flag) {
+        const uint32_t drain = tfull_bar(acc);
+        tc_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, acc_phase) && globaltimer_ns() - t0 < kWaitLimitNs / 20) {
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp can access
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const TileCoord tc = tile_coord(t, num_m, args.k_splits);
+      const int row = tc.m_tile * kBM + row_in_tile;
+      const bool row_ok = row < m_rows;
+      const int n0 = tc.n_tile * BN;
+      const int ncols = min(BN, args.n_cols - n0);
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+
+      if constexpr (MODE == kArgmax) {
+        float negb = 0.0f;
+        if (row_ok && args.prior != nullptr)
+          negb = -__ldg(&args.beta[row_position(args.row_pos, row, args.n_pos)]);
+        const __nv_bfloat16* brow =
+            (args.base != nullptr && row_ok) ? args.base + (long long)row * args.ld_base + n0 : nullptr;
+        const float* prow = args.prior != nullptr ? args.prior + n0 : nullptr;
+        float best = -INFINITY;
+        int best_c = 0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
+          tmem_ld_wait(v);
+          const int c0 = c * 32;
+          if (c0 < ncols) {
+            float sc[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(v[j]);
+            const bool full_chunk = (c0 + 32 <= ncols);
+            if (brow != nullptr) {
+              if (VEC_BASE && full_chunk) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint4 w = __ldg(reinterpret_cast<const uint4*>(brow + c0) + q);
+                  sc[8 * q + 0] += bf16_lo(w.x);
+                  sc[8 * q + 1] += bf16_hi(w.x);
+                  sc[8 * q + 2] += bf16_lo(w.y);
+                  sc[8 * q + 3] += bf16_hi(w.y);
+                  sc[8 * q + 4] += bf16_lo(w.z);
+                  sc[8 * q + 5] += bf16_hi(w.z);
+                  sc[8 * q + 6] += bf16_lo(w.w);
+                  sc[8 * q + 7] += bf16_hi(w.w);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (c0 + j < ncols) sc[j] += __bfloat162float(brow[c0 + j]);
+              }
+            }
+            if (prow != nullptr) {
+              if (full_chunk) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  const float4 p = __ldg(reinterpret_cast<const float4*>(prow + c0) + q);
+                  sc[4 * q + 0] = fmaf(negb, p.x, sc[4 * q + 0]);
+                  sc[4 * q + 1] = fmaf(negb, p.y, sc[4 * q + 1]);
+                  sc[4 * q + 2] = fmaf(negb, p.z, sc[4 * q + 2]);
+                  sc[4 * q + 3] = fmaf(negb, p.w, sc[4 * q + 3]);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (c0 + j < ncols) sc[j] = fmaf(negb, __ldg(prow + c0 + j), sc[j]);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (c0 + j < ncols && scan_takes(sc[j], best)) {
+                best = sc[j];
+                best_c = c0 + j;
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(tempty_bar(acc));
+        if (row_ok) {
+          atomicMax(&args.keys[row], pack_key(best, (uint32_t)(args.v_begin + n0 + best_c)));
+          __threadfence();
+        }
+      } else {
+        float* dst = args.out + (long long)tc.split * args.split_stride + (long long)row * args.ld_out + n0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
+          tmem_ld_wait(v);
+          const int c0 = c * 32;
+          if (row_ok && c0 < ncols) {
+            if (c0 + 32 <= ncols) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 f;
+                f.x = __uint_as_float(v[4 * q + 0]);
+                f.y = __uint_as_float(v[4 * q + 1]);
+                f.z = __uint_as_float(v[4 * q + 2]);
+                f.w = __uint_as_float(v[4 * q + 3]);
+                reinterpret_cast<float4*>(dst + c0)[q] = f;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (c0 + j < ncols) dst[c0 + j] = __uint_as_float(v[j]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(tempty_bar(acc));
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+
+  if constexpr (MODE == kArgmax) {
+    if (args.idx_out != nullptr) {
+      // The last CTA to finish turns the packed keys into token ids.
+      if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(args.counter, 1u);
+        *last_flag = (prev == gridDim.x - 1) ? 1 : 0;
+      }
+      __syncthreads();
+      if (*last_flag) {
+        __threadfence();
+        for (int row = threadIdx.x; row < m_rows; row += blockDim.x) {
+          const long long key = (long long)atomicAdd(reinterpret_cast<unsigned long long*>(&args.keys[row]), 0ull);
+          args.idx_out[row] = (long long)key_index(key);
+          if (args.score_out != nullptr) args.score_out[row] = key_score(key);
+        }
+        if (threadIdx.x == 0) atomicExch(args.counter, 0u);
+      }
+    }
+  }
+}
+
+}  // namespace dels

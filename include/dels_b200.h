@@ -1,0 +1,196 @@
+/*
+ * dels_b200.h — C ABI of the B200-native DeLS draft-scoring hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream handle; no framework types.  Every entry
+ * point only enqueues work on `stream` (a cudaStream_t passed as void*): none
+ * allocates device memory or synchronises the host, so all of them can be captured
+ * in a CUDA graph (call dels_init() for the device once, before any capture).
+ *
+ * Conventions
+ *   - bf16 tensors are row-major with a leading dimension `ld_*` in elements; it must
+ *     be a multiple of 8 and base pointers 16-byte aligned (tensor-memory-access tiles).
+ *   - fp32 tensors used by the fp32 scorer need 16-byte aligned rows (ld % 4 == 0).
+ *   - alpha / beta are fp32 device arrays of length n_pos; row `i` uses position
+ *     p = row_pos[i] when row_pos != NULL, else p = i % n_pos (rows laid out [B, P]).
+ *   - `prior` is the fp32 log-unigram prior (the bf16-rounded values of the reference
+ *     run are exactly representable); NULL skips the beta term, as the reference does
+ *     when it has no baseline or beta == 0 (code/kernel/dels.py:382, :454).
+ *   - Argmax ties go to the lowest vocabulary index (torch.argmax, and the strict '>'
+ *     of code/kernel/dels.py:134); a NaN score is treated as the largest value.
+ *   - Packed keys (int64): ((ordered score) << 32) | (0xFFFFFFFF - global index).  The
+ *     signed maximum of two keys is the argmax of the two candidates, so per-rank keys
+ *     combine with an all-reduce(MAX) on int64 (vocab sharding).
+ *   - Workspace `ws`: caller-owned device memory, zero-filled once before first use.
+ *     Bytes [0,4) are a completion counter (left at zero after every call), bytes [4,8)
+ *     an int32 device status word: a kernel that gives up on a bounded wait stores
+ *     DELS_ERR_DEVICE_TIMEOUT there; the status persists until the caller clears it.
+ *
+ * Return values: DELS_OK or a negative DELS_ERR_* code; dels_last_error() gives a
+ * message for the calling thread's most recent failure.
+ */
+#ifndef DELS_B200_H_
+#define DELS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DELS_API __attribute__((visibility("default")))
+#else
+#define DELS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DELS_OK 0
+#define DELS_ERR_INVALID_ARG (-1)
+#define DELS_ERR_ALIGNMENT (-2)
+#define DELS_ERR_WORKSPACE (-3)
+#define DELS_ERR_CUDA (-4)
+#define DELS_ERR_UNSUPPORTED (-5)
+#define DELS_ERR_DEVICE_TIMEOUT (-6)
+
+#define DELS_ACT_IDENTITY 0 /* code/dels.py:14 "identity" */
+#define DELS_ACT_SILU 1     /* code/dels.py:14 "silu"     */
+
+/* keys[] already hold the empty key (set by dels_rank_project_bf16 / dels_keys_init). */
+#define DELS_FLAG_KEYS_READY 1u
+
+#define DELS_WS_HEADER_BYTES 256
+
+DELS_API int dels_version(void);
+DELS_API const char* dels_status_string(int status);
+DELS_API const char* dels_last_error(void);
+
+/* Load every kernel of the library on `device` and set its launch attributes.  Call
+ * before the first CUDA-graph capture that contains a dels_* call. */
+DELS_API int dels_init(int device);
+
+/* Number of streaming multiprocessors the persistent kernels size their grids for. */
+DELS_API int dels_sm_count(int device);
+
+/* ---------------------------------------------------------------------------------
+ * Rank projection.  Replaces code/kernel/dels.py:437-439
+ *   rank_state = F.linear(h, W_rank); rank_state = F.silu(rank_state) (optional)
+ * and produces the scorer operand alpha_p * rank_state.
+ *   x        [rows, K] bf16 (ld_x)       w_rank [r, K] bf16 (ld_w), nn.Linear layout
+ *   s_out    [rows, r] bf16 or NULL      s = bf16(act(bf16(x . w_rank^T)))
+ *   s_scaled [rows, r] bf16              bf16(alpha_p * s)
+ *   keys     [rows] int64 or NULL        set to the empty key (saves an init launch)
+ * Tensor-core split-K GEMM + SIMT finalisation; ws >= dels_rank_workspace_bytes().
+ * --------------------------------------------------------------------------------- */
+DELS_API size_t dels_rank_workspace_bytes(int rows, int K, int r);
+DELS_API int dels_rank_project_bf16(const void* x, int64_t ld_x, const void* w_rank, int64_t ld_w, int rows, int K, int r,
+                           int activation, const float* alpha, int n_pos, const int32_t* row_pos, void* s_out,
+                           void* s_scaled, int64_t* keys, void* ws, size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Fused draft scorer, bf16 tensor cores.  Replaces
+ * _fused_low_rank_argmax_kernel + _reduce_argmax_kernel (code/kernel/dels.py:15-138,
+ * launched at :375-423) and the long-logit GEMM code/dflash.py:468, without ever
+ * materialising logits:
+ *   score[i, v] = h[i] . W[v] + s_scaled[i] . Vr[v] - beta_p * prior[v]
+ *   keys[i]     = max over v of pack(score[i, v], v_begin + v)     (atomicMax)
+ *   idx_out[i]  = argmax index (int64), score_out[i] = its score   (either may be NULL)
+ *   h [rows, H] bf16, W [V, H] bf16 (the target LM head, or this rank's vocab slice
+ *   starting at global index v_begin), s_scaled [rows, r] bf16, Vr [V, r] bf16
+ *   (low_rank_lm_head.weight), prior [V] fp32 or NULL.
+ * rows_dev (optional) holds the actual row count on the device (<= rows), so a ragged
+ * batch needs no host round trip.  With idx_out == NULL the keys are left for a
+ * cross-rank all-reduce(MAX) followed by dels_keys_decode().  H == 0 drops the W.h
+ * term.  ws >= DELS_WS_HEADER_BYTES.
+ * --------------------------------------------------------------------------------- */
+DELS_API int dels_fused_argmax_bf16(const void* h, int64_t ld_h, const void* W, int64_t ld_w, const void* s_scaled,
+                           int64_t ld_s, const void* Vr, int64_t ld_vr, const float* prior, const float* beta,
+                           int n_pos, const int32_t* row_pos, int rows, const int32_t* rows_dev, int H, int r,
+                           int V, int64_t v_begin, uint32_t flags, int64_t* keys, int64_t* idx_out,
+                           float* score_out, void* ws, size_t ws_bytes, void* stream);
+
+/* Base-logits variant: the exact DeLSGraphRunner step (code/kernel/dels.py:70-90),
+ *   score[i, v] = base[i, v] + s_scaled[i] . Vr[v] - beta_p * prior[v]
+ * with base [rows, V] bf16 (ld_base), e.g. static_base_logits[:, step, :]. */
+DELS_API int dels_fused_argmax_base_bf16(const void* base, int64_t ld_base, const void* s_scaled, int64_t ld_s,
+                                const void* Vr, int64_t ld_vr, const float* prior, const float* beta, int n_pos,
+                                const int32_t* row_pos, int rows, const int32_t* rows_dev, int r, int V,
+                                int64_t v_begin, uint32_t flags, int64_t* keys, int64_t* idx_out,
+                                float* score_out, void* ws, size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Whole draft-scoring step, bf16 (dense, ragged and vocab-sharded batches): rank projection
+ * s = act(h . w_rank^T) then the fused scorer.  Replaces one step of
+ * DeLSGraphRunner._forward_impl (code/kernel/dels.py:436-458) with the long logits of
+ * code/dflash.py:468 folded in; the eager twin is code/dflash.py:516-534.
+ * ws >= dels_score_workspace_bytes(rows, H, r).
+ * --------------------------------------------------------------------------------- */
+DELS_API size_t dels_score_workspace_bytes(int rows, int H, int r);
+DELS_API int dels_draft_score_bf16(const void* h, int64_t ld_h, const void* W, int64_t ld_w, const void* w_rank,
+                          int64_t ld_wr, const void* Vr, int64_t ld_vr, const float* prior, const float* alpha,
+                          const float* beta, int n_pos, const int32_t* row_pos, int rows, const int32_t* rows_dev,
+                          int H, int r, int V, int64_t v_begin, int activation, int64_t* keys, int64_t* idx_out,
+                          float* score_out, void* ws, size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * fp32 draft scorer on CUDA cores (fp32 workloads; scores within 1e-5).  Same
+ * formula as dels_draft_score_bf16 with every tensor fp32 and s kept in fp32:
+ *   s[i] = alpha_p * (h[i] . w_rank^T),  score = h.W[v] + s.Vr[v] - beta_p prior[v].
+ * H % 4 == 0, r % 4 == 0.  ws >= dels_score_f32_workspace_bytes(rows, r).
+ * --------------------------------------------------------------------------------- */
+DELS_API size_t dels_score_f32_workspace_bytes(int rows, int r);
+DELS_API int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t ld_w, const float* w_rank,
+                         int64_t ld_wr, const float* Vr, int64_t ld_vr, const float* prior, const float* alpha,
+                         const float* beta, int n_pos, const int32_t* row_pos, int rows, int H, int r, int V,
+                         int64_t v_begin, int64_t* keys, int64_t* idx_out, float* score_out, void* ws,
+                         size_t ws_bytes, void* stream);
+
+/* Set keys[0..rows) to the empty key and zero the workspace counter. */
+DELS_API int dels_keys_init(int64_t* keys, int rows, void* ws, void* stream);
+
+/* Decode packed keys (e.g. after a cross-rank all-reduce(MAX)) into int64 token ids
+ * and fp32 scores (either output may be NULL).  rows_dev as above. */
+DELS_API int dels_keys_decode(const int64_t* keys, int rows, const int32_t* rows_dev, int64_t* idx_out, float* score_out,
+                     void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Acceptance.  Replaces code/dflash.py:645-651
+ *   accept = (verify_ids[:, 1:] == posterior[:, :-1]).cumprod(1).sum(1)
+ * for a ragged continuous batch, without the host round trip of `.item()`:
+ *   draft [n_seq, n_draft] int64 (ld_draft), target [n_seq, >= n_draft] int64
+ *   accept[b]  = length of the prefix on which draft[b, j] == target[b, j]   (int32)
+ *   offsets[0] = 0, offsets[b+1] = offsets[b] + accept[b] + commit_extra     (int32)
+ * commit_extra = 1 counts the bonus target token the decode loop also commits
+ * (code/dflash.py:652-660).
+ * --------------------------------------------------------------------------------- */
+DELS_API int dels_accept_offsets(const int64_t* draft, int64_t ld_draft, const int64_t* target, int64_t ld_target,
+                        int n_seq, int n_draft, int commit_extra, int32_t* accept, int32_t* offsets, void* stream);
+
+/* Pack the accepted rows of hidden [n_seq, P, H] bf16 (strides ld_seq, ld_row in
+ * elements): packed[offsets[b] + j] = hidden[b, j] for j < accept[b], row_pos of that
+ * packed row = j.  Use offsets from dels_accept_offsets(commit_extra = 0); the total
+ * row count offsets[n_seq] can be passed to the scorer as rows_dev. */
+DELS_API int dels_pack_rows_bf16(const void* hidden, int64_t ld_seq, int64_t ld_row, int n_seq, int P, int H,
+                        const int32_t* accept, const int32_t* offsets, void* packed, int64_t ld_packed,
+                        int32_t* row_pos, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Input-projected RNN local head (a recurrence over the block positions; the reference only has the GRU
+ * form, code/kernel/dels.py:359-373, whose input projection is likewise precomputed
+ * at :265-268):
+ *   s_t = tanh(W_in x_t + W_s s_{t-1} + b), s_0 = 0, for t = 0..T-1 of each sequence
+ *   x [n_seq*T, H] bf16 (rows in [seq, t] order), w_in [r, H] bf16, w_s [r, r] bf16,
+ *   bias [r] fp32 or NULL, alpha [T] fp32.
+ *   s_scaled [n_seq*T, r] bf16 = bf16(alpha_t * s_t); s_out (optional) = bf16(s_t).
+ * r even and <= 256.  ws >= dels_rnn_workspace_bytes(n_seq, T, H, r).
+ * --------------------------------------------------------------------------------- */
+DELS_API size_t dels_rnn_workspace_bytes(int n_seq, int T, int H, int r);
+DELS_API int dels_rnn_rank_states_bf16(const void* x, int64_t ld_x, const void* w_in, int64_t ld_win, const void* w_s,
+                              const float* bias, const float* alpha, int n_seq, int T, int H, int r,
+                              void* s_scaled, void* s_out, int64_t* keys, void* ws, size_t ws_bytes,
+                              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DELS_B200_H_ */

@@ -1,0 +1,34 @@
+"""The reference's scoring formula as torch ops on the host — TEST / BASELINE ONLY.
+
+Restates, operation for operation and in the reference's own dtype, the CPU path the
+reference takes for one draft-scoring step: the long logits of the target LM head
+(code/dflash.py:468), the rank state and low-rank logits of the local head
+(code/kernel/dels.py:437 and :448), the mix with a Python-float alpha / beta per draft
+position (code/kernel/dels.py:449-455, eager twin code/dflash.py:523-527) and
+torch.argmax (:456).  ``bench.py`` times it on the host cores as the CPU baseline; it
+is never part of the product path.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+
+@torch.inference_mode()
+def score_rows(h, W, w_rank, Vr, prior, alpha_rows, beta_rows) -> torch.Tensor:
+    """Token ids [rows] for rows whose draft positions carry alpha_rows / beta_rows."""
+    long_logits = F.linear(h, W)
+    rank_state = F.linear(h, w_rank)
+    short_logits = F.linear(rank_state, Vr)
+    prior = None if prior is None else prior.to(long_logits.dtype).view(1, -1)
+    out = torch.empty(h.shape[0], dtype=torch.long)
+    a = [float(x) for x in alpha_rows]
+    b = [float(x) for x in beta_rows]
+    for key in sorted(set(zip(a, b))):
+        idx = torch.tensor([i for i in range(len(a)) if (a[i], b[i]) == key], dtype=torch.long)
+        logits = long_logits[idx] + key[0] * short_logits[idx]
+        if prior is not None and key[1] != 0.0:
+            logits = logits - key[1] * prior
+        out[idx] = torch.argmax(logits, dim=-1)
+    return out
