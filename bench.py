@@ -60,8 +60,11 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, dev: torch.device):
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:
+            self.index = str(dev.index or 0)
         self.proc = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"dels_clocks_{os.getpid()}.csv"
 
@@ -126,14 +129,27 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
-def timed(fn, steps: int, warmup: int, world: int, stream) -> float:
-    """ms for `steps` calls of fn, CUDA events on `stream`, barrier + sync both sides."""
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    barrier(world)
+def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None, hold_ms: float = 0.0) -> float:
+    """ms for exactly `steps` calls of fn: CUDA events on `stream`, barrier + synchronize on
+    both sides.  With `clocks`, the nvidia-smi sampler runs from before a load phase of
+    about `hold_ms` (same step count on every rank) until the timed region has ended, so
+    the clock record covers the timed region under steady load."""
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(warmup):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    hold_steps = 0
+    if clocks is not None and hold_ms > 0:
+        est = max_over_ranks(start.elapsed_time(end) / max(warmup, 1), world, dev)
+        hold_steps = int(min(5000, max(1, hold_ms / max(est, 1e-3))))
+        clocks.start()
+        for _ in range(hold_steps):
+            fn()
+        torch.cuda.synchronize()
+    barrier(world)
     start.record(stream)
     for _ in range(steps):
         fn()
@@ -242,9 +258,8 @@ def run_ours(args, rank, world, dev):
         raise SystemExit(f"unknown workload {wname}")
 
     ops.init(dev)
-    clocks = ClockSampler(dev.index or 0)
-    clocks.start()
-    ms = timed(step, args.steps, args.warmup, world, stream)
+    clocks = ClockSampler(dev)
+    ms = timed(step, args.steps, args.warmup, world, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
     ms = max_over_ranks(ms, world, dev)
     ms_e2e = max_over_ranks(timed(e2e_step, args.steps, args.warmup, world, stream), world, dev)
@@ -326,9 +341,8 @@ def run_ragged(args, rank, world, dev):
     step()
     torch.cuda.synchronize()
     total = int(off[-1])
-    clocks = ClockSampler(dev.index or 0)
-    clocks.start()
-    ms = timed(step, args.steps, args.warmup, 1, stream)
+    clocks = ClockSampler(dev)
+    ms = timed(step, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
     hh = {k: t[k].cpu().pin_memory() for k in ("draft", "target", "hidden")}
     dd = {k: torch.empty_like(t[k]) for k in hh}
@@ -396,9 +410,8 @@ def run_rnn(args, rank, world, dev):
                               out=out, ws=mws)
 
     ops.init(dev)
-    clocks = ClockSampler(dev.index or 0)
-    clocks.start()
-    ms = timed(step, args.steps, args.warmup, 1, stream)
+    clocks = ClockSampler(dev)
+    ms = timed(step, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
     x_host = t["x"].cpu().pin_memory()
     x_dev = torch.empty_like(t["x"])

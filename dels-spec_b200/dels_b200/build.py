@@ -21,7 +21,7 @@ INCLUDE_DIR = REPO_ROOT / "include"
 LIB_NAME = "libdels_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["api.cu", "small_kernels.cu", "f32_score.cu"]
+SOURCES = ["api.cu", "small_kernels.cu", "f32_score.cu", "runner_kernels.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

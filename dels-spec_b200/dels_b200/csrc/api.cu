@@ -10,6 +10,7 @@
 #include <string>
 
 #include "f32_score.cuh"
+#include "runner_kernels.cuh"
 #include "small_kernels.cuh"
 #include "tc_gemm.cuh"
 
@@ -21,6 +22,10 @@ constexpr int kVersion = 1;
 constexpr int kMaxDevices = 64;
 // Split-K sizing of the projection GEMMs aims at this many CTAs (one B200 wave).
 constexpr int kTargetCtas = 148;
+// Scorer schedule: 16 row tiles (2048 rows, a 17.8 MB A panel at H + r = 4352) sweep
+// the vocabulary together; the last partial wave's tiles are split 4 ways along N.
+constexpr int kScorerGroupM = 16;
+constexpr int kScorerTailSplit = 4;
 
 thread_local std::string g_last_error;
 
@@ -133,6 +138,9 @@ int init_device(int dev) {
     SET(accept_offsets_kernel, 0);
     SET(pack_rows_kernel, 0);
     SET(f32_rank_kernel, 0);
+    SET(gru_step_kernel, kMaxSmem);
+    SET(rank_gemv_kernel, kMaxSmem);
+    SET(gather_scaled_kernel, 0);
 #undef SET
   }
   if (rc == DELS_OK) {
@@ -199,28 +207,38 @@ template <int BN, int MODE, bool VB>
 int launch_tc(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) {
   int rc = ensure_encode();
   if (rc != DELS_OK) return rc;
-  CUtensorMap ma0, mb0, ma1, mb1;
+  // B maps come in two box heights: BN rows for whole tiles and BN / tail_split rows
+  // for the split tiles of the last partial wave.
+  const int tail_rows = BN / (args.tail_split > 1 ? args.tail_split : 1);
+  CUtensorMap ma0, mb0, ma1, mb1, mb0t, mb1t;
   if (op.K1 > 0) {
     if ((rc = make_map_bf16(&ma1, op.a1, op.K1, op.m_extent, op.lda1, kBM)) != DELS_OK) return rc;
     if ((rc = make_map_bf16(&mb1, op.b1, op.K1, op.n_extent, op.ldb1, BN)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb1t, op.b1, op.K1, op.n_extent, op.ldb1, tail_rows)) != DELS_OK) return rc;
   }
   if (op.K0 > 0) {
     if ((rc = make_map_bf16(&ma0, op.a0, op.K0, op.m_extent, op.lda0, kBM)) != DELS_OK) return rc;
     if ((rc = make_map_bf16(&mb0, op.b0, op.K0, op.n_extent, op.ldb0, BN)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb0t, op.b0, op.K0, op.n_extent, op.ldb0, tail_rows)) != DELS_OK) return rc;
   } else {
     ma0 = ma1;
     mb0 = mb1;
+    mb0t = mb1t;
   }
   if (op.K1 == 0) {
     ma1 = ma0;
     mb1 = mb0;
+    mb1t = mb0t;
   }
   args.kb0 = cdiv(op.K0, kBK);
   args.kb1 = cdiv(op.K1, kBK);
   const long long tiles = (long long)cdiv(op.m_extent, kBM) * cdiv(op.n_extent, BN) * args.k_splits;
-  const int grid = (int)(tiles < sm_count ? tiles : sm_count);
+  // With fewer tiles than SMs, split tiles (tail_split ways) so more SMs take part.
+  const long long want = tiles < sm_count ? tiles * (args.tail_split > 1 ? args.tail_split : 1) : tiles;
+  const int grid = (int)(want < sm_count ? want : sm_count);
   if (grid <= 0) return DELS_OK;
-  tc_gemm_kernel<BN, MODE, VB><<<grid, kTcThreads, TcConfig<BN>::kSmemBytes, st>>>(ma0, mb0, ma1, mb1, args);
+  tc_gemm_kernel<BN, MODE, VB><<<grid, kTcThreads, TcConfig<BN>::kSmemBytes, st>>>(ma0, mb0, ma1, mb1, mb0t, mb1t,
+                                                                                   args);
   DELS_CHECK_LAUNCH("tc_gemm_kernel launch");
   return DELS_OK;
 }
@@ -230,6 +248,8 @@ TcArgs blank_args() {
   std::memset(&a, 0, sizeof(a));
   a.k_splits = 1;
   a.n_pos = 1;
+  a.group_m = 1;
+  a.tail_split = 1;
   return a;
 }
 
@@ -355,6 +375,8 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
   a.n_cols = V;
   a.k_splits = 1;
   a.kb_per_split = cdiv(H, kBK) + cdiv(r, kBK);
+  a.group_m = kScorerGroupM;
+  a.tail_split = kScorerTailSplit;
   a.status = hdr.status;
   a.v_begin = v_begin;
   a.prior = prior;
@@ -612,7 +634,8 @@ int dels_accept_offsets(const int64_t* draft, int64_t ld_draft, const int64_t* t
                         int n_seq, int n_draft, int commit_extra, int32_t* accept, int32_t* offsets, void* stream) {
   if (n_seq < 0 || n_draft < 0) return fail(DELS_ERR_INVALID_ARG, "n_seq and n_draft must be >= 0");
   if (commit_extra != 0 && commit_extra != 1) return fail(DELS_ERR_INVALID_ARG, "commit_extra must be 0 or 1");
-  if (accept == nullptr || offsets == nullptr) return fail(DELS_ERR_INVALID_ARG, "accept / offsets is NULL");
+  if (offsets == nullptr || (n_seq > 0 && accept == nullptr))
+    return fail(DELS_ERR_INVALID_ARG, "accept / offsets is NULL");
   if (n_seq > 0 && n_draft > 0 && (draft == nullptr || target == nullptr))
     return fail(DELS_ERR_INVALID_ARG, "draft / target is NULL");
   if (ld_draft < n_draft || ld_target < n_draft)
@@ -683,6 +706,77 @@ int dels_rnn_rank_states_bf16(const void* x, int64_t ld_x, const void* w_in, int
       reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<__nv_bfloat16*>(s_out),
       reinterpret_cast<long long*>(keys), hdr.counter);
   DELS_CHECK_LAUNCH("rnn_recurrence_kernel launch");
+  return DELS_OK;
+}
+
+int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+                       const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G, int V,
+                       void* ws, void* stream) {
+  if (B < 0 || G <= 0 || V <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d V=%d", B, G, V);
+  if ((G % 8) != 0) return fail(DELS_ERR_UNSUPPORTED, "GRU hidden size %d must be a multiple of 8", G);
+  if (tokens == nullptr || gi_table == nullptr || w_hh == nullptr || h_out == nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if (!aligned16(w_hh) || (h_in != nullptr && !aligned16(h_in)) || !aligned16(h_out))
+    return fail(DELS_ERR_ALIGNMENT, "w_hh / h_in / h_out must be 16-byte aligned");
+  if (ld_table < 3LL * G) return fail(DELS_ERR_INVALID_ARG, "gi table leading dimension < 3G");
+  if (gru_smem_bytes(G) > (size_t)kMaxSmem) return fail(DELS_ERR_UNSUPPORTED, "GRU hidden size %d too large", G);
+  int* status = ws != nullptr ? reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + 4) : nullptr;
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (B == 0) return DELS_OK;
+  gru_step_kernel<<<cdiv(G, kGruCols), 256, gru_smem_bytes(G), reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const long long*>(tokens), tok_stride, reinterpret_cast<const __nv_bfloat16*>(gi_table),
+      ld_table, reinterpret_cast<const __nv_bfloat16*>(w_hh), reinterpret_cast<const __nv_bfloat16*>(b_hh),
+      reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V, status);
+  DELS_CHECK_LAUNCH("gru_step_kernel launch");
+  return DELS_OK;
+}
+
+int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias, int B, int K,
+                        int r, int activation, const float* alpha, int n_pos, const int32_t* row_pos, void* s_out,
+                        void* s_scaled, int64_t* keys, void* ws, void* stream) {
+  int rc;
+  if (B < 0 || K <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d K=%d r=%d", B, K, r);
+  if ((K % 8) != 0) return fail(DELS_ERR_UNSUPPORTED, "K = %d must be a multiple of 8", K);
+  if (activation != DELS_ACT_IDENTITY && activation != DELS_ACT_SILU)
+    return fail(DELS_ERR_INVALID_ARG, "unsupported rank activation %d", activation);
+  if (n_pos <= 0 || s_scaled == nullptr) return fail(DELS_ERR_INVALID_ARG, "n_pos <= 0 or s_scaled NULL");
+  if ((rc = check_bf16_matrix("x", x, ld_x, K)) != DELS_OK) return rc;
+  if ((rc = check_bf16_matrix("w_rank", w, ld_w, K)) != DELS_OK) return rc;
+  if (rank_gemv_smem_bytes(K) > (size_t)kMaxSmem) return fail(DELS_ERR_UNSUPPORTED, "K = %d too large", K);
+  unsigned* counter = ws != nullptr ? reinterpret_cast<unsigned*>(ws) : nullptr;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (B == 0) return DELS_OK;
+  const int grid = cdiv(r, 4) < ds->sm_count ? cdiv(r, 4) : ds->sm_count;
+  rank_gemv_kernel<<<grid, 128, rank_gemv_smem_bytes(K), reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ld_x, reinterpret_cast<const __nv_bfloat16*>(w), ld_w,
+      reinterpret_cast<const __nv_bfloat16*>(bias), B, K, r, activation, alpha, n_pos, row_pos,
+      reinterpret_cast<__nv_bfloat16*>(s_out), reinterpret_cast<__nv_bfloat16*>(s_scaled),
+      reinterpret_cast<long long*>(keys), counter);
+  DELS_CHECK_LAUNCH("rank_gemv_kernel launch");
+  return DELS_OK;
+}
+
+int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, const void* emb, int64_t ld_emb,
+                                 const float* alpha, int n_pos, int B, int r, int V, void* s_scaled, int64_t* keys,
+                                 void* ws, void* stream) {
+  if (B < 0 || r <= 0 || V <= 0 || n_pos <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape");
+  if (tokens == nullptr || emb == nullptr || s_scaled == nullptr) return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if (ld_emb < r) return fail(DELS_ERR_INVALID_ARG, "embedding leading dimension < r");
+  unsigned* counter = ws != nullptr ? reinterpret_cast<unsigned*>(ws) : nullptr;
+  int* status = ws != nullptr ? reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + 4) : nullptr;
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (B == 0) return DELS_OK;
+  const int grid = cdiv((long long)B * r, 256) < 1024 ? cdiv((long long)B * r, 256) : 1024;
+  gather_scaled_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const long long*>(tokens), tok_stride, reinterpret_cast<const __nv_bfloat16*>(emb), ld_emb,
+      alpha, n_pos, B, r, V, reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys), counter,
+      status);
+  DELS_CHECK_LAUNCH("gather_scaled_kernel launch");
   return DELS_OK;
 }
 

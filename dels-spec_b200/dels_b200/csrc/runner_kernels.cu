@@ -1,0 +1,193 @@
+// Small-batch kernels of the greedy suffix rollout that DeLSGraphRunner /
+// MarkovDeLSGraphRunner capture in a CUDA graph (B = 1 .. a few dozen rows):
+//
+//   * gru_step_kernel      — gi = table[token], gh = bf16(W_hh h + b_hh), then the GRU
+//                            gates in fp32 and h' stored as bf16, in one launch
+//                            (code/kernel/dels.py:359-373 + the Triton cell :140-211 +
+//                            the table gather :432, :461);
+//   * rank_gemv_kernel     — s = bf16(act(bf16(W_rank h + b))), s_scaled = bf16(alpha s),
+//                            and the packed keys reset (code/kernel/dels.py:437-443);
+//   * gather_scaled_kernel — Markov rank state s = embedding[token], s_scaled = bf16(alpha s)
+//                            (code/kernel/markov_dels.py:288).
+//
+// At these batch sizes every weight matrix is read once per step and each element is
+// used B times, so the kernels are memory-bound GEMVs: warps stream weight rows with
+// coalesced 16-byte loads (lane l owns elements 8l..8l+7 of every 256-element chunk),
+// the B input rows sit in shared memory, and a butterfly shuffle finishes each dot
+// product.
+#include "runner_kernels.cuh"
+
+namespace dels {
+
+namespace {
+
+// dot products of one weight row (bf16, length K) with `nb` bf16 rows staged in shared
+// memory (row stride ldx elements); the full sums end up in every lane.
+template <int MAXB>
+__device__ __forceinline__ void warp_row_dots(const __nv_bfloat16* __restrict__ wrow, const __nv_bfloat16* xs,
+                                              int ldx, int nb, int K, int lane, float (&acc)[MAXB]) {
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) acc[b] = 0.0f;
+  for (int k = lane * 8; k < K; k += 256) {
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(wrow + k));
+    const float w0 = bf16_lo(w.x), w1 = bf16_hi(w.x), w2 = bf16_lo(w.y), w3 = bf16_hi(w.y);
+    const float w4 = bf16_lo(w.z), w5 = bf16_hi(w.z), w6 = bf16_lo(w.w), w7 = bf16_hi(w.w);
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) {
+      if (b < nb) {
+        const uint4 x = *reinterpret_cast<const uint4*>(xs + b * ldx + k);
+        float a = acc[b];
+        a = fmaf(w0, bf16_lo(x.x), a);
+        a = fmaf(w1, bf16_hi(x.x), a);
+        a = fmaf(w2, bf16_lo(x.y), a);
+        a = fmaf(w3, bf16_hi(x.y), a);
+        a = fmaf(w4, bf16_lo(x.z), a);
+        a = fmaf(w5, bf16_hi(x.z), a);
+        a = fmaf(w6, bf16_lo(x.w), a);
+        a = fmaf(w7, bf16_hi(x.w), a);
+        acc[b] = a;
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) {
+    float a = acc[b];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+    acc[b] = a;
+  }
+}
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+}  // namespace
+
+// One CTA per kGruCols hidden units; B rows in chunks of kRunnerMaxB.
+__global__ void __launch_bounds__(256) gru_step_kernel(const long long* __restrict__ tokens, long long tok_stride,
+                                                       const __nv_bfloat16* __restrict__ table, long long ld_table,
+                                                       const __nv_bfloat16* __restrict__ w_hh,
+                                                       const __nv_bfloat16* __restrict__ b_hh,
+                                                       const __nv_bfloat16* h_in, __nv_bfloat16* h_out, int B, int G,
+                                                       int V, int* status) {
+  extern __shared__ uint4 smem4[];
+  __nv_bfloat16* hs = reinterpret_cast<__nv_bfloat16*>(smem4);     // [kRunnerMaxB][G]
+  float* gh_s = reinterpret_cast<float*>(hs + (size_t)kRunnerMaxB * G);  // [3][kGruCols][kRunnerMaxB]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int g0 = blockIdx.x * kGruCols;
+  for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
+    const int nb = min(kRunnerMaxB, B - b0);
+    __syncthreads();
+    // stage h_in rows (zeros when h_in is NULL: the rollout's initial state)
+    for (int e = threadIdx.x; e < nb * G / 8; e += blockDim.x) {
+      const int b = e / (G / 8), k8 = e % (G / 8);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (h_in != nullptr) v = *reinterpret_cast<const uint4*>(h_in + (long long)(b0 + b) * G + k8 * 8);
+      reinterpret_cast<uint4*>(hs + (size_t)b * G)[k8] = v;
+    }
+    __syncthreads();
+    // gh for the gate rows {g, G + g, 2G + g} of this CTA's columns
+    for (int rr = warp; rr < 3 * kGruCols; rr += nwarps) {
+      const int gate = rr / kGruCols, c = rr % kGruCols;
+      const int g = g0 + c;
+      float acc[kRunnerMaxB];
+      if (g < G) {
+        warp_row_dots<kRunnerMaxB>(w_hh + (long long)(gate * G + g) * G, hs, G, nb, G, lane, acc);
+        if (lane == 0) {
+          const float bias = b_hh != nullptr ? __bfloat162float(b_hh[gate * G + g]) : 0.0f;
+          for (int b = 0; b < nb; ++b) gh_s[(gate * kGruCols + c) * kRunnerMaxB + b] = bf16r(acc[b] + bias);
+        }
+      }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < nb * kGruCols; e += blockDim.x) {
+      const int b = e / kGruCols, c = e % kGruCols;
+      const int g = g0 + c;
+      if (g >= G) continue;
+      long long tok = tokens[(long long)(b0 + b) * tok_stride];
+      if (tok < 0 || tok >= V) {
+        if (status != nullptr) atomicCAS(status, 0, DELS_ERR_INVALID_ARG);
+        tok = tok < 0 ? 0 : V - 1;
+      }
+      const __nv_bfloat16* gi = table + tok * ld_table;
+      const float gi_r = __bfloat162float(gi[g]);
+      const float gi_z = __bfloat162float(gi[G + g]);
+      const float gi_n = __bfloat162float(gi[2 * G + g]);
+      const float gh_r = gh_s[(0 * kGruCols + c) * kRunnerMaxB + b];
+      const float gh_z = gh_s[(1 * kGruCols + c) * kRunnerMaxB + b];
+      const float gh_n = gh_s[(2 * kGruCols + c) * kRunnerMaxB + b];
+      const float h = __bfloat162float(hs[(size_t)b * G + g]);
+      const float rg = sigmoidf_(gi_r + gh_r);
+      const float zg = sigmoidf_(gi_z + gh_z);
+      const float ng = tanhf(gi_n + rg * gh_n);
+      h_out[(long long)(b0 + b) * G + g] = __float2bfloat16_rn((1.0f - zg) * ng + zg * h);
+    }
+  }
+}
+
+// One warp per output feature j (grid-stride), all B rows at once.
+__global__ void __launch_bounds__(256) rank_gemv_kernel(const __nv_bfloat16* __restrict__ x, long long ld_x,
+                                                        const __nv_bfloat16* __restrict__ w, long long ld_w,
+                                                        const __nv_bfloat16* __restrict__ bias, int B, int K, int r,
+                                                        int activation, const float* __restrict__ alpha, int n_pos,
+                                                        const int* __restrict__ row_pos, __nv_bfloat16* s_out,
+                                                        __nv_bfloat16* s_scaled, long long* keys, unsigned* counter) {
+  extern __shared__ uint4 smem4[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);  // [kRunnerMaxB][K]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
+    const int nb = min(kRunnerMaxB, B - b0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < nb * K / 8; e += blockDim.x) {
+      const int b = e / (K / 8), k8 = e % (K / 8);
+      reinterpret_cast<uint4*>(xs + (size_t)b * K)[k8] =
+          *reinterpret_cast<const uint4*>(x + (long long)(b0 + b) * ld_x + k8 * 8);
+    }
+    __syncthreads();
+    for (int j = gwarp; j < r; j += nwarps) {
+      float acc[kRunnerMaxB];
+      warp_row_dots<kRunnerMaxB>(w + (long long)j * ld_w, xs, K, nb, K, lane, acc);
+      if (lane < nb) {
+        float a = 0.0f;
+#pragma unroll
+        for (int b = 0; b < kRunnerMaxB; ++b)
+          if (b == lane) a = acc[b];
+        const int row = b0 + lane;
+        const float bj = bias != nullptr ? __bfloat162float(bias[j]) : 0.0f;
+        float s = bf16r(a + bj);
+        if (activation == DELS_ACT_SILU) s = bf16r(s / (1.0f + expf(-s)));
+        if (s_out != nullptr) s_out[(long long)row * r + j] = __float2bfloat16_rn(s);
+        const float al = alpha != nullptr ? alpha[row_position(row_pos, row, n_pos)] : 1.0f;
+        s_scaled[(long long)row * r + j] = __float2bfloat16_rn(al * s);
+      }
+    }
+  }
+  if (keys != nullptr && blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < B; i += blockDim.x) keys[i] = kKeyEmpty;
+  }
+  if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
+}
+
+__global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride,
+                                     const __nv_bfloat16* __restrict__ emb, long long ld_emb,
+                                     const float* __restrict__ alpha, int n_pos, int B, int r, int V,
+                                     __nv_bfloat16* s_scaled, long long* keys, unsigned* counter, int* status) {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < B * r; e += gridDim.x * blockDim.x) {
+    const int b = e / r, j = e % r;
+    long long tok = tokens[(long long)b * tok_stride];
+    if (tok < 0 || tok >= V) {
+      if (status != nullptr) atomicCAS(status, 0, DELS_ERR_INVALID_ARG);
+      tok = tok < 0 ? 0 : V - 1;
+    }
+    const float a = alpha != nullptr ? alpha[b % n_pos] : 1.0f;
+    s_scaled[e] = __float2bfloat16_rn(a * __bfloat162float(emb[tok * ld_emb + j]));
+    if (keys != nullptr && j == 0) keys[b] = kKeyEmpty;
+  }
+  if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
+}
+
+}  // namespace dels

@@ -46,6 +46,8 @@ struct TcArgs {
   int kb0, kb1;            // k-blocks in segment 0 and segment 1
   int k_splits;            // split-K factor (kStore only; 1 for kArgmax)
   int kb_per_split;
+  int group_m;             // rasterisation: row tiles that sweep the B operand together
+  int tail_split;          // the last partial wave's tiles are split this many ways along N
   int* status;             // device error word (0 = ok)
   // kArgmax
   long long v_begin;       // global vocab index of column 0 of B
@@ -85,19 +87,77 @@ struct TileCoord {
   int m_tile, n_tile, split;
 };
 
-__device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int k_splits) {
+// Tile t -> (row tile, column tile, K split).  Row tiles are taken in groups of
+// group_m: a group sweeps every column tile with its row tiles fastest, so the group's
+// A panel stays resident in L2 while the B operand (the LM head) streams through once
+// per group, and CTAs that run concurrently share each B tile.
+__device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n, int k_splits, int group_m) {
   TileCoord c;
-  c.m_tile = t % num_m;
-  const int rest = t / num_m;
-  c.split = rest % k_splits;
-  c.n_tile = rest / k_splits;
+  c.split = t % k_splits;
+  const int mn = t / k_splits;
+  const int per_group = group_m * num_n;
+  const int g = mn / per_group;
+  const int first_m = g * group_m;
+  const int gm = min(group_m, num_m - first_m);
+  const int local = mn - g * per_group;
+  c.m_tile = first_m + local % gm;
+  c.n_tile = local / gm;
   return c;
+}
+
+// Work unit u of the persistent schedule.  The first `main_units` units are whole
+// tiles; the remaining tiles of the last, partial wave are split `tail_split` ways
+// along N so that the wave's work spreads over all CTAs instead of a handful.
+struct WorkUnit {
+  TileCoord c;
+  int n0;   // first B row (column of D) of the unit
+  int bn;   // columns in this unit (BN or BN / tail_split)
+  bool tail;
+};
+
+struct Schedule {
+  int num_m, num_n, k_splits, group_m;
+  int main_units, tail_split, total_units;
+};
+
+__device__ __forceinline__ Schedule make_schedule(int num_m, int num_n, int k_splits, int group_m, int tail_split,
+                                                  int grid) {
+  Schedule s;
+  s.num_m = num_m;
+  s.num_n = num_n;
+  s.k_splits = k_splits;
+  s.group_m = group_m < 1 ? 1 : group_m;
+  const int tiles = num_m * num_n * k_splits;
+  const int rem = grid > 0 ? tiles % grid : 0;
+  s.tail_split = (tail_split > 1 && rem > 0) ? tail_split : 1;
+  s.main_units = tiles - (s.tail_split > 1 ? rem : 0);
+  s.total_units = s.main_units + (tiles - s.main_units) * s.tail_split;
+  return s;
+}
+
+template <int BN>
+__device__ __forceinline__ WorkUnit work_unit(int u, const Schedule& s) {
+  WorkUnit w;
+  if (u < s.main_units) {
+    w.c = tile_coord(u, s.num_m, s.num_n, s.k_splits, s.group_m);
+    w.n0 = w.c.n_tile * BN;
+    w.bn = BN;
+    w.tail = false;
+  } else {
+    const int q = u - s.main_units;
+    w.c = tile_coord(s.main_units + q / s.tail_split, s.num_m, s.num_n, s.k_splits, s.group_m);
+    w.bn = BN / s.tail_split;
+    w.n0 = w.c.n_tile * BN + (q % s.tail_split) * w.bn;
+    w.tail = true;
+  }
+  return w;
 }
 
 template <int BN, int MODE, bool VEC_BASE>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                    const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                   const __grid_constant__ CUtensorMap map_b0t, const __grid_constant__ CUtensorMap map_b1t,
                    const TcArgs args) {
   using Cfg = TcConfig<BN>;
   constexpr int S = Cfg::kStages;
@@ -129,7 +189,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int num_m = (m_rows + kBM - 1) / kBM;
   const int num_n = (args.n_cols + BN - 1) / BN;
   const int total_kb = args.kb0 + args.kb1;
-  const int num_tiles = num_m * num_n * args.k_splits;
+  const Schedule sched = make_schedule(num_m, num_n, args.k_splits, args.group_m, args.tail_split, gridDim.x);
+  const int num_units = sched.total_units;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -149,6 +210,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tma_prefetch_map(&map_b0);
     tma_prefetch_map(&map_a1);
     tma_prefetch_map(&map_b1);
+    if (sched.tail_split > 1) {
+      tma_prefetch_map(&map_b0t);
+      tma_prefetch_map(&map_b1t);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -166,27 +231,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord(t, num_m, args.k_splits);
-        const int kb_begin = tc.split * args.kb_per_split;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const WorkUnit wu = work_unit<BN>(u, sched);
+        const int kb_begin = wu.c.split * args.kb_per_split;
         const int kb_end = min(total_kb, kb_begin + args.kb_per_split);
-        const int m0 = tc.m_tile * kBM;
-        const int n0 = tc.n_tile * BN;
+        const int m0 = wu.c.m_tile * kBM;
+        const int n0 = wu.n0;
+        const uint32_t tx = (uint32_t)Cfg::kABytes + (uint32_t)wu.bn * kBK * 2u;
+        const CUtensorMap* mb0 = wu.tail ? &map_b0t : &map_b0;
+        const CUtensorMap* mb1 = wu.tail ? &map_b1t : &map_b1;
         for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
+          mbar_arrive_expect_tx(full_bar(stage), tx);
           const uint32_t a_dst = a_base + stage * Cfg::kABytes;
           const uint32_t b_dst = b_base + stage * Cfg::kBBytes;
           if (kb < args.kb0) {
             tma_load_2d(a_dst, &map_a0, full_bar(stage), kb * kBK, m0);
-            tma_load_2d(b_dst, &map_b0, full_bar(stage), kb * kBK, n0);
+            tma_load_2d(b_dst, mb0, full_bar(stage), kb * kBK, n0);
           } else {
             const int k1 = kb - args.kb0;
             tma_load_2d(a_dst, &map_a1, full_bar(stage), k1 * kBK, m0);
-            tma_load_2d(b_dst, &map_b1, full_bar(stage), k1 * kBK, n0);
+            tma_load_2d(b_dst, mb1, full_bar(stage), k1 * kBK, n0);
           }
           ++issued;
           if (++stage == S) {
@@ -214,14 +282,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, BN);
+      constexpr uint32_t idesc_full = make_idesc_bf16_f32(kBM, BN);
+      const uint32_t idesc_tail = make_idesc_bf16_f32(kBM, BN / (sched.tail_split > 1 ? sched.tail_split : 1));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord(t, num_m, args.k_splits);
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const WorkUnit wu = work_unit<BN>(u, sched);
+        const TileCoord tc = wu.c;
+        const uint32_t idesc = wu.tail ? idesc_tail : idesc_full;
         const int kb_begin = tc.split * args.kb_per_split;
         const int kb_end = min(total_kb, kb_begin + args.kb_per_split);
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag, args.status)) break;
@@ -269,12 +340,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const TileCoord tc = tile_coord(t, num_m, args.k_splits);
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      const WorkUnit wu = work_unit<BN>(u, sched);
+      const TileCoord tc = wu.c;
       const int row = tc.m_tile * kBM + row_in_tile;
       const bool row_ok = row < m_rows;
-      const int n0 = tc.n_tile * BN;
-      const int ncols = min(BN, args.n_cols - n0);
+      const int n0 = wu.n0;
+      const int ncols = min(wu.bn, args.n_cols - n0);
+      const int nchunks = wu.bn / 32;
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
@@ -289,7 +362,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float best = -INFINITY;
         int best_c = 0;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < nchunks; ++c) {
           uint32_t v[32];
           tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
           tmem_ld_wait(v);
@@ -353,7 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else {
         float* dst = args.out + (long long)tc.split * args.split_stride + (long long)row * args.ld_out + n0;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < nchunks; ++c) {
           uint32_t v[32];
           tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
           tmem_ld_wait(v);

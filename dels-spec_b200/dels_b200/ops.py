@@ -39,9 +39,13 @@ def _require_cuda(name: str, t: torch.Tensor, dtype: torch.dtype, ndim: int | No
 
 def _row_major(name: str, t: torch.Tensor) -> int:
     """Leading dimension (elements) of a 2-D tensor with unit column stride."""
-    if t.dim() != 2 or t.stride(1) != 1:
-        raise ValueError(f"{name} must be 2-D with contiguous rows (stride {tuple(t.stride())})")
-    return t.stride(0)
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D (got shape {tuple(t.shape)})")
+    if t.numel() == 0:
+        return max(int(t.shape[1]), 1)
+    if t.stride(1) != 1 and t.shape[1] > 1:
+        raise ValueError(f"{name} must have contiguous rows (stride {tuple(t.stride())})")
+    return t.stride(0) if t.shape[0] > 1 else max(t.stride(0), int(t.shape[1]))
 
 
 def _f32_vec(name: str, t: torch.Tensor | None, device: torch.device) -> torch.Tensor | None:
@@ -489,3 +493,84 @@ def rnn_rank_states(
               _ptr(w_s), _ptr(bias), _ptr(alpha), n_seq, T, H, r, _ptr(s_scaled), _ptr(s_out), _ptr(keys), ws.ptr,
               ws.nbytes, _stream(dev))
     return s_scaled, s_out
+
+
+# --------------------------------------------------------------------------- rollout kernels
+def gru_step(
+    tokens: torch.Tensor,
+    gi_table: torch.Tensor,
+    w_hh: torch.Tensor,
+    h_in: torch.Tensor | None,
+    h_out: torch.Tensor,
+    *,
+    b_hh: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """h_out = GRU(gi_table[tokens], h_in) with gh = W_hh h_in (+ b_hh); h_in None = zeros."""
+    _require_cuda("tokens", tokens, torch.int64)
+    _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
+    _require_cuda("w_hh", w_hh, torch.bfloat16, 2)
+    _require_cuda("h_out", h_out, torch.bfloat16, 2)
+    B, G = h_out.shape
+    V = gi_table.shape[0]
+    if w_hh.shape != (3 * G, G) or not w_hh.is_contiguous() or gi_table.shape[1] != 3 * G:
+        raise ValueError("GRU weights do not match the hidden size")
+    if h_in is not None and (h_in.shape != (B, G) or not h_in.is_contiguous()):
+        raise ValueError("h_in must be a contiguous [B, G] tensor")
+    if not h_out.is_contiguous():
+        raise ValueError("h_out must be contiguous")
+    tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
+    _lib.call("dels_gru_step_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+              _ptr(w_hh), _ptr(b_hh), _ptr(h_in), _ptr(h_out), B, G, V, None if ws is None else ws.ptr,
+              _stream(h_out.device))
+    return h_out
+
+
+def rank_gemv(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    alpha: torch.Tensor | None,
+    s_scaled: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    n_pos: int = 1,
+    row_pos: torch.Tensor | None = None,
+    activation: str = "identity",
+    s_out: torch.Tensor | None = None,
+    keys: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """Small-batch rank projection: s_scaled = bf16(alpha * act(x . w^T + bias))."""
+    _require_cuda("x", x, torch.bfloat16, 2)
+    _require_cuda("w", w, torch.bfloat16, 2)
+    B, K = x.shape
+    r = w.shape[0]
+    if w.shape[1] != K or s_scaled.shape != (B, r) or not s_scaled.is_contiguous():
+        raise ValueError("rank projection shapes do not match")
+    _lib.call("dels_rank_gemv_bf16", _ptr(x), _row_major("x", x), _ptr(w), _row_major("w", w), _ptr(bias), B, K, r,
+              ACTIVATIONS[activation], _ptr(alpha), int(n_pos), _ptr(_i32_vec("row_pos", row_pos)), _ptr(s_out),
+              _ptr(s_scaled), _ptr(keys), None if ws is None else ws.ptr, _stream(x.device))
+    return s_scaled
+
+
+def gather_scaled_rows(
+    tokens: torch.Tensor,
+    emb: torch.Tensor,
+    alpha: torch.Tensor | None,
+    s_scaled: torch.Tensor,
+    *,
+    n_pos: int = 1,
+    keys: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """s_scaled[b] = bf16(alpha * emb[tokens[b]]) (Markov rank state)."""
+    _require_cuda("tokens", tokens, torch.int64)
+    _require_cuda("emb", emb, torch.bfloat16, 2)
+    B, r = s_scaled.shape
+    if emb.shape[1] != r or not s_scaled.is_contiguous():
+        raise ValueError("embedding / output shapes do not match")
+    tok_stride = tokens.stride(0) if tokens.numel() > 1 else 1
+    _lib.call("dels_gather_scaled_rows_bf16", _ptr(tokens), tok_stride, _ptr(emb), _row_major("emb", emb),
+              _ptr(alpha), int(n_pos), B, r, emb.shape[0], _ptr(s_scaled), _ptr(keys),
+              None if ws is None else ws.ptr, _stream(s_scaled.device))
+    return s_scaled

@@ -1,0 +1,179 @@
+"""CUDA-graph runner for block-prefix DeLS greedy correction, on the B200 kernels.
+
+Drop-in for ``kernel.dels.DeLSGraphRunner`` of the reference (code/kernel/dels.py:214-478):
+same constructor keywords, same ``ValueError`` checks, same ``__call__(prefix_ids,
+base_logits) -> LongTensor[B, steps]`` returning a fresh tensor, same static buffers
+(``static_prefix_ids``, ``static_base_logits``, ``static_out``), warm-up on a side
+stream and capture into ``self.graph``.  Each captured step is three kernels of
+``libdels_b200.so``:
+
+  1. GRU step: token -> input-table row, W_hh h, gates (``dels_gru_step_bf16``);
+  2. rank projection + activation + alpha_step scaling, keys reset (``dels_rank_gemv_bf16``);
+  3. fused scorer on tcgen05 tensor cores: base logits + low-rank logits - beta * prior,
+     argmax with the lowest index on ties, written straight into the step's token slot
+     (``dels_fused_argmax_base_bf16``).
+
+alpha / beta live in device arrays indexed by step, so one graph serves a schedule;
+the reference instead bakes them into the Triton kernels as constexprs (:404-409).
+The local head must be bf16 (the reference benchmark always loads it in bf16,
+code/benchmark.py:303-309); other dtypes raise ``ValueError``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from dels_b200 import ops
+
+
+class DeLSGraphRunner:
+    """
+    CUDA Graph runner for block-prefix DeLS greedy correction.
+
+    Captures the fixed-shape suffix rollout used by the HF benchmark; every step runs
+    on hand-written sm_100a kernels (GRU step, rank projection, fused low-rank
+    LM-head mix + argmax).
+    """
+
+    def __init__(
+        self,
+        *,
+        local_head,
+        batch_size: int,
+        steps: int,
+        vocab_size: int,
+        alpha_values: list[float],
+        beta_values: list[float],
+        baseline_logits: torch.Tensor | None,
+        device: torch.device,
+    ):
+        if steps <= 0:
+            raise ValueError(f"DeLSGraphRunner requires steps > 0, got {steps}.")
+        if len(alpha_values) != steps or len(beta_values) != steps:
+            raise ValueError(
+                "DeLS graph alpha/beta schedules must match steps: "
+                f"steps={steps}, alpha={len(alpha_values)}, beta={len(beta_values)}."
+            )
+        if any(float(beta) != 0.0 for beta in beta_values) and baseline_logits is None:
+            raise ValueError("DeLS graph requires baseline_logits when any beta is nonzero.")
+
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("DeLSGraphRunner runs on a CUDA device (sm_100a kernels only).")
+        self.local_head = local_head
+        self.batch_size = int(batch_size)
+        self.steps = int(steps)
+        self.vocab_size = int(vocab_size)
+        self.alpha_values = [float(x) for x in alpha_values]
+        self.beta_values = [float(x) for x in beta_values]
+
+        dtype = local_head.rank_proj.weight.dtype
+        if dtype != torch.bfloat16:
+            raise ValueError(f"DeLSGraphRunner kernels are bf16; the local head is {dtype}.")
+        self.rank_dim = int(local_head.low_rank_lm_head.weight.shape[1])
+        # Kept for the reference's log line (code/benchmark.py:481-484): the fused path
+        # is always used here.
+        self._can_triton_fuse = True
+        activation = getattr(local_head, "rank_activation", "identity")
+        if activation not in ops.ACTIVATIONS:
+            raise ValueError(f"Unsupported DeLS rank_activation={activation!r}.")
+        self._activation = activation
+
+        gru = local_head.prefix_gru
+        if gru.num_layers != 1 or gru.bidirectional:
+            raise ValueError("DeLS graph runner supports only a single unidirectional GRU.")
+        self.gru_hidden_dim = int(gru.hidden_size)
+        with torch.no_grad():
+            self.gru_w_ih = gru.weight_ih_l0.detach().to(device).contiguous()
+            self.gru_w_hh = gru.weight_hh_l0.detach().to(device).contiguous()
+            self.gru_b_ih = gru.bias_ih_l0.detach().to(device).contiguous() if gru.bias else None
+            self.gru_b_hh = gru.bias_hh_l0.detach().to(device).contiguous() if gru.bias else None
+
+            embed_weight = local_head.embed_tokens.weight.detach().to(device).contiguous()
+            if self.gru_b_ih is None:
+                # gi table = F.linear(embed, W_ih) (code/kernel/dels.py:265-268) on the
+                # tensor-core projection kernel: bf16 output of an fp32 accumulation.
+                table, _ = ops.rank_project_bf16(embed_weight, self.gru_w_ih, None, n_pos=1)
+            else:
+                table = torch.nn.functional.linear(embed_weight, self.gru_w_ih, self.gru_b_ih)
+            self._gru_input_proj_table = table.contiguous()
+
+            self.rank_weight = local_head.rank_proj.weight.detach().to(device).contiguous()
+            self.rank_bias = (
+                local_head.rank_proj.bias.detach().to(device).contiguous()
+                if local_head.rank_proj.bias is not None
+                else None
+            )
+            self.lm_head_weight = local_head.low_rank_lm_head.weight.detach().to(device).contiguous()
+
+            baseline_flat = torch.zeros(self.vocab_size, dtype=dtype, device=device)
+            if baseline_logits is not None:
+                baseline_numel = int(baseline_logits.numel())
+                if baseline_numel != self.vocab_size:
+                    raise ValueError(
+                        "DeLS graph baseline vocab size mismatch: "
+                        f"baseline={baseline_numel}, vocab={self.vocab_size}."
+                    )
+                baseline_flat.copy_(baseline_logits.to(device=device, dtype=dtype).reshape(-1))
+        self.baseline_logits = baseline_flat.contiguous()
+        self.has_baseline = baseline_logits is not None
+        # the scorer reads the prior in fp32 (exactly the bf16 values above)
+        self._prior_f32 = self.baseline_logits.to(torch.float32) if self.has_baseline else None
+
+        B, G, r, S = self.batch_size, self.gru_hidden_dim, self.rank_dim, self.steps
+        self.static_prefix_ids = torch.zeros(B, 1, dtype=torch.long, device=device)
+        self.static_base_logits = torch.zeros(B, S, self.vocab_size, dtype=dtype, device=device)
+        self.static_out = torch.zeros(B, S, dtype=torch.long, device=device)
+
+        self._alpha = torch.tensor(self.alpha_values, dtype=torch.float32, device=device)
+        # beta == 0 at a step skips the prior like the reference (:382); a zero beta
+        # contributes nothing, so the device array simply holds the schedule.
+        self._beta = torch.tensor(self.beta_values, dtype=torch.float32, device=device)
+        self._tokens = torch.zeros(S, B, dtype=torch.long, device=device)  # step-major token slots
+        self._h = [torch.zeros(B, G, dtype=dtype, device=device) for _ in range(2)]
+        self._s_scaled = torch.zeros(B, r, dtype=dtype, device=device)
+        self._keys = torch.empty(B, dtype=torch.int64, device=device)
+        self._ws = ops.Workspace(1 << 12, device)
+        self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
+
+        ops.init(device)
+        stream = torch.cuda.Stream(device=device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.inference_mode(), torch.cuda.stream(stream):
+            for _ in range(3):
+                self._forward_impl()
+        torch.cuda.current_stream(device).wait_stream(stream)
+
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.inference_mode(), torch.cuda.graph(self.graph):
+            self._forward_impl()
+
+    def _forward_impl(self):
+        prefix = self.static_prefix_ids[:, 0]
+        h_cur = ops.gru_step(prefix, self._gru_input_proj_table, self.gru_w_hh, None, self._h[0],
+                             b_hh=self.gru_b_hh, ws=self._ws)
+        nxt = 1
+        for step in range(self.steps):
+            ops.rank_gemv(h_cur, self.rank_weight, self._alpha[step : step + 1], self._s_scaled,
+                          bias=self.rank_bias, activation=self._activation, keys=self._keys, ws=self._ws)
+            ops.fused_argmax_base_bf16(
+                self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight,
+                self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],
+                ws=self._ws,
+            )
+            if step + 1 < self.steps:
+                h_cur = ops.gru_step(self._tokens[step], self._gru_input_proj_table, self.gru_w_hh, h_cur,
+                                     self._h[nxt], b_hh=self.gru_b_hh, ws=self._ws)
+                nxt ^= 1
+        self.static_out.copy_(self._tokens.t())
+
+    @torch.inference_mode()
+    def __call__(
+        self,
+        prefix_ids: torch.Tensor,
+        base_logits: torch.Tensor,
+    ) -> torch.Tensor:
+        self.static_prefix_ids.copy_(prefix_ids)
+        self.static_base_logits.copy_(base_logits)
+        self.graph.replay()
+        return self.static_out.clone()

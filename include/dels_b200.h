@@ -189,6 +189,38 @@ DELS_API int dels_rnn_rank_states_bf16(const void* x, int64_t ld_x, const void* 
                               void* s_scaled, void* s_out, int64_t* keys, void* ws, size_t ws_bytes,
                               void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Small-batch kernels of the greedy suffix rollout captured by DeLSGraphRunner /
+ * MarkovDeLSGraphRunner (B rows, typically 1..64).
+ *
+ * GRU step — replaces DeLSGraphRunner._gru_cell + the input-table gather
+ * (code/kernel/dels.py:359-373, :432, :461; Triton cell :140-211):
+ *   gi = gi_table[tokens[b * tok_stride]]   ([V, 3G] bf16 = F.linear(embed, W_ih, b_ih))
+ *   gh = bf16(W_hh . h_in[b] + b_hh)        (W_hh [3G, G] bf16, b_hh [3G] bf16 or NULL)
+ *   r, z = sigmoid(gi + gh) (first two G-blocks), n = tanh(gi_n + r * gh_n)
+ *   h_out[b] = bf16((1 - z) * n + z * h_in[b])      (h_in NULL = zero state)
+ * G % 8 == 0.  Out-of-range token ids are clamped and flagged in the ws status word
+ * (DELS_ERR_INVALID_ARG) when ws is given. */
+DELS_API int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+                                const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G,
+                                int V, void* ws, void* stream);
+
+/* Rank projection for small batches (code/kernel/dels.py:437-443):
+ *   s = bf16(act(bf16(x . w^T + bias))), s_scaled = bf16(alpha_p * s), keys[0..B) reset,
+ * one warp per output feature.  K % 8 == 0.  ws (optional) supplies the counter that
+ * the following scorer call expects at zero. */
+DELS_API int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias, int B,
+                                 int K, int r, int activation, const float* alpha, int n_pos,
+                                 const int32_t* row_pos, void* s_out, void* s_scaled, int64_t* keys, void* ws,
+                                 void* stream);
+
+/* Markov rank state (code/kernel/markov_dels.py:288):
+ *   s_scaled[b] = bf16(alpha_p * emb[tokens[b * tok_stride]]),  emb [V, r] bf16,
+ * keys[0..B) reset.  Out-of-range ids are clamped and flagged as above. */
+DELS_API int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, const void* emb, int64_t ld_emb,
+                                          const float* alpha, int n_pos, int B, int r, int V, void* s_scaled,
+                                          int64_t* keys, void* ws, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

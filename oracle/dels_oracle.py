@@ -341,6 +341,7 @@ def dels_runner_rollout(
     beta: Sequence[float],
     activation: str = "identity",
     bf16: bool = False,
+    table: np.ndarray | None = None,
 ) -> tuple[np.ndarray, np.ndarray]:
     """Greedy DeLS suffix rollout of DeLSGraphRunner._forward_impl
     (code/kernel/dels.py:425-467): h = GRU(embed[prefix]); for each step: rank state,
@@ -348,13 +349,15 @@ def dels_runner_rollout(
 
     With ``bf16=True`` the values the reference stores in bf16 tensors are rounded
     (gi table, gh, GRU state, rank state) while the mix is exact — the Triton path's
-    semantics (fp32 math on bf16 storage, :47-88 and :164-211).  Returns tokens
-    [B, steps] and per-step top-2 gaps [B, steps]."""
+    semantics (fp32 math on bf16 storage, :47-88 and :164-211).  ``table`` may pass a
+    precomputed input table embed . w_ih^T.  Returns tokens [B, steps] and per-step
+    top-2 gaps [B, steps]."""
     rnd = bf16_round if bf16 else (lambda a: np.asarray(a, np.float64))
     B = prefix_ids.shape[0]
     steps = base_logits.shape[1]
     G = w_hh.shape[1]
-    table = rnd((np.asarray(embed, np.float64) @ np.asarray(w_ih, np.float64).T).astype(np.float32))
+    if table is None:
+        table = rnd((np.asarray(embed, np.float64) @ np.asarray(w_ih, np.float64).T).astype(np.float32))
     h = np.zeros((B, G))
 
     def advance(tok, h):

@@ -1,0 +1,148 @@
+"""The drop-in graph runners (kernel/dels.py, kernel/markov_dels.py) against the
+reference's own runner outputs (tests/golden/runners.npz) and the oracle rollout.
+Needs a B200.  After a step whose exact top-2 gap is below the tolerance the greedy
+rollouts may legitimately diverge, so each row is compared up to that step."""
+
+from __future__ import annotations
+
+import json
+import types
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from oracle import dels_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _head(dev, V, E, G, r, act, weights):
+    import dels as D
+
+    target = types.SimpleNamespace(model=types.SimpleNamespace(embed_tokens=nn.Embedding(V, E)),
+                                   lm_head=nn.Linear(G, V, bias=False))
+    head = D.DeLSLocalHead(target_model=target, vocab_size=V, embed_dim=E, gru_hidden_dim=G, low_rank_dim=r,
+                           lm_head_mode="low_rank", rank_activation=act, dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        head.embed_tokens.weight.copy_(torch.from_numpy(weights["embed"]).to(dev))
+        head.prefix_gru.weight_ih_l0.copy_(torch.from_numpy(weights["w_ih"]).to(dev))
+        head.prefix_gru.weight_hh_l0.copy_(torch.from_numpy(weights["w_hh"]).to(dev))
+        head.rank_proj.weight.copy_(torch.from_numpy(weights["w_rank"]).to(dev))
+        head.low_rank_lm_head.weight.copy_(torch.from_numpy(weights["Vr"]).to(dev))
+    return head
+
+
+def _compare(ours, gaps, ref, thresh):
+    n = 0
+    for b in range(ours.shape[0]):
+        for t in range(ours.shape[1]):
+            if gaps[b, t] <= thresh:
+                break
+            assert ours[b, t] == ref[b, t], (b, t, ours[b], ref[b])
+            n += 1
+    return n
+
+
+def test_dels_runner_matches_reference_fixture(cuda_device, golden_dir):
+    from kernel.dels import DeLSGraphRunner
+
+    g = np.load(golden_dir / "runners.npz")
+    total = 0
+    for c in json.loads(str(g["meta"])):
+        n = c["name"]
+        w = {k: g[f"{n}_{k}"] for k in ("embed", "w_ih", "w_hh", "w_rank", "Vr")}
+        head = _head(cuda_device, c["V"], c["E"], c["G"], c["r"], c["activation"], w)
+        prior = torch.from_numpy(g[f"{n}_prior_bf16"]).to(cuda_device) if c["prior"] else None
+        runner = DeLSGraphRunner(local_head=head, batch_size=c["B"], steps=c["steps"], vocab_size=c["V"],
+                                 alpha_values=list(g[f"{n}_alpha"]), beta_values=list(g[f"{n}_beta"]),
+                                 baseline_logits=prior, device=cuda_device)
+        base = torch.from_numpy(g[f"{n}_base"]).to(cuda_device).to(torch.bfloat16)
+        prefix = torch.from_numpy(g[f"{n}_prefix"]).to(cuda_device)
+        out = runner(prefix, base).cpu().numpy()
+        assert out.shape == (c["B"], c["steps"])
+        toks, gaps = O.dels_runner_rollout(
+            g[f"{n}_prefix"], g[f"{n}_base"], embed=w["embed"], w_ih=w["w_ih"], w_hh=w["w_hh"], w_rank=w["w_rank"],
+            Vr=w["Vr"], prior=None if prior is None else g[f"{n}_prior_bf16"], alpha=g[f"{n}_alpha"],
+            beta=g[f"{n}_beta"], activation=c["activation"], bf16=True,
+        )
+        # the oracle's bf16-storage rollout (the reference's Triton-path semantics) ...
+        total += _compare(out, gaps, toks, 1e-2)
+        # ... and the reference runner's own bf16 output, away from its rounding noise
+        _compare(out, gaps, g[f"{n}_tokens_bf16"], 0.05)
+        # replay with other inputs: static buffers are refreshed on every call
+        out2 = runner(torch.flip(prefix, [0]), torch.flip(base, [0])).cpu().numpy()
+        toks2, gaps2 = O.dels_runner_rollout(
+            np.flip(g[f"{n}_prefix"], 0), np.flip(g[f"{n}_base"], 0), embed=w["embed"], w_ih=w["w_ih"],
+            w_hh=w["w_hh"], w_rank=w["w_rank"], Vr=w["Vr"], prior=None if prior is None else g[f"{n}_prior_bf16"],
+            alpha=g[f"{n}_alpha"], beta=g[f"{n}_beta"], activation=c["activation"], bf16=True,
+        )
+        _compare(out2, gaps2, toks2, 1e-2)
+    assert total >= 15
+
+
+def test_markov_runner_matches_reference_fixture(cuda_device, golden_dir):
+    import dels as D
+    from kernel.markov_dels import MarkovDeLSGraphRunner
+
+    g = np.load(golden_dir / "runners.npz")
+    for c in json.loads(str(g["meta"])):
+        n = c["name"]
+        emb = torch.from_numpy(g[f"{n}_markov_embedding"])
+        head = D.MarkovDeLSLocalHead(embedding_weight=emb, lm_head_weight=torch.from_numpy(g[f"{n}_Vr"]),
+                                     dtype=torch.bfloat16, device=cuda_device)
+        prior = torch.from_numpy(g[f"{n}_prior_bf16"]).to(cuda_device) if c["prior"] else None
+        runner = MarkovDeLSGraphRunner(local_head=head, batch_size=c["B"], steps=c["steps"], vocab_size=c["V"],
+                                       alpha_values=list(g[f"{n}_alpha"]), beta_values=list(g[f"{n}_beta"]),
+                                       baseline_logits=prior, device=cuda_device)
+        out = runner(torch.from_numpy(g[f"{n}_prefix"]).to(cuda_device),
+                     torch.from_numpy(g[f"{n}_base"]).to(cuda_device).to(torch.bfloat16)).cpu().numpy()
+        toks, gaps = O.markov_runner_rollout(g[f"{n}_prefix"], g[f"{n}_base"], embedding=g[f"{n}_markov_embedding"],
+                                             lm_head=g[f"{n}_Vr"], prior=None if prior is None else
+                                             g[f"{n}_prior_bf16"], alpha=g[f"{n}_alpha"], beta=g[f"{n}_beta"])
+        _compare(out, gaps, toks, 1e-2)
+        _compare(out, gaps, g[f"{n}_markov_tokens_bf16"], 0.05)
+
+
+def test_runner_validation_errors(cuda_device):
+    from kernel.dels import DeLSGraphRunner
+
+    with pytest.raises(ValueError, match="steps > 0"):
+        DeLSGraphRunner(local_head=None, batch_size=1, steps=0, vocab_size=10, alpha_values=[], beta_values=[],
+                        baseline_logits=None, device=cuda_device)
+    with pytest.raises(ValueError, match="must match steps"):
+        DeLSGraphRunner(local_head=None, batch_size=1, steps=2, vocab_size=10, alpha_values=[1.0], beta_values=[1, 1],
+                        baseline_logits=None, device=cuda_device)
+    with pytest.raises(ValueError, match="requires baseline_logits"):
+        DeLSGraphRunner(local_head=None, batch_size=1, steps=1, vocab_size=10, alpha_values=[1.0], beta_values=[0.5],
+                        baseline_logits=None, device=cuda_device)
+
+
+def test_runner_full_vocab_b1(cuda_device):
+    """Released head shapes (V=151936, E=256, G=1024, r=256), batch 1, 14 steps."""
+    from kernel.dels import DeLSGraphRunner
+
+    rng = np.random.default_rng(21)
+    V, E, G, r, steps = 151936, 256, 1024, 256, 14
+    w = {
+        "embed": O.bf16_round((rng.standard_normal((V, E)) * 0.5).astype(np.float32)),
+        "w_ih": O.bf16_round((rng.standard_normal((3 * G, E)) * 0.05).astype(np.float32)),
+        "w_hh": O.bf16_round((rng.standard_normal((3 * G, G)) * 0.03).astype(np.float32)),
+        "w_rank": O.bf16_round((rng.standard_normal((r, G)) * 0.05).astype(np.float32)),
+        "Vr": O.bf16_round((rng.standard_normal((V, r)) * 0.05).astype(np.float32)),
+    }
+    head = _head(cuda_device, V, E, G, r, "identity", w)
+    prior = O.bf16_round(O.zipf_log_prior(V).astype(np.float32))
+    alpha = list(np.linspace(0.9, 0.3, steps))
+    beta = list(np.linspace(0.3, 0.1, steps))
+    runner = DeLSGraphRunner(local_head=head, batch_size=1, steps=steps, vocab_size=V, alpha_values=alpha,
+                             beta_values=beta, baseline_logits=torch.from_numpy(prior).to(cuda_device),
+                             device=cuda_device)
+    base = O.bf16_round(rng.standard_normal((1, steps, V)).astype(np.float32))
+    prefix = np.array([[12345]])
+    out = runner(torch.from_numpy(prefix).to(cuda_device), torch.from_numpy(base).to(cuda_device).to(torch.bfloat16))
+    table = runner._gru_input_proj_table.float().cpu().numpy()  # bf16 F.linear(embed, W_ih) on the GPU
+    toks, gaps = O.dels_runner_rollout(prefix, base, embed=None, w_ih=None, w_hh=w["w_hh"], w_rank=w["w_rank"],
+                                       Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta, bf16=True, table=table)
+    assert _compare(out.cpu().numpy(), gaps, toks, 1e-2) >= 3
