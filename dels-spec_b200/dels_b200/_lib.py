@@ -25,6 +25,7 @@ DELS_ACT_IDENTITY = 0
 DELS_ACT_SILU = 1
 DELS_FLAG_KEYS_READY = 1
 DELS_WS_HEADER_BYTES = 256
+DELS_NOALLOC_SCRATCH_BYTES = 12 * 1024 * 1024
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -77,6 +78,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dels_gru_step_bf16": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "dels_rank_gemv_bf16": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "dels_gather_scaled_rows_bf16": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "dels_draft_score_bf16_noalloc": (
+        _I,
+        [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _I64, _I, _P, _P, _P, _P],
+    ),
 }
 
 

@@ -781,3 +781,77 @@ int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, cons
 }
 
 }  // extern "C"
+
+// ======================================================================== allocation-free entry
+//
+// Some hosts cannot give this library device scratch memory: a service that binds the C
+// ABI directly through an FFI layer (cgo, JNI, plain ctypes) has no device allocator of
+// its own, and a serving engine that has already reserved nearly all of device memory
+// for its KV-cache pool would see cudaMalloc fail, or pay for a device-wide
+// synchronisation at the worst moment.  dels_draft_score_bf16_noalloc serves those
+// callers: it runs exactly the dels_draft_score_bf16 kernels, with the scratch they
+// need (packed keys, the scaled rank state, the split-K partial sums, the completion
+// counter and the status word) placed in the fixed array below, which the module
+// reserves on every device that loads the library and keeps until the process exits.
+//
+// The array holds only the state of the call in flight: every call rewrites the keys,
+// the rank state and the partials, and its rank-projection finalisation zeroes the
+// completion counter before the scorer runs, so nothing carries over between calls.
+// Calls that can overlap on the device (different streams, or different host threads
+// without ordering) share the one array and race; serialise them.
+namespace {
+
+constexpr size_t kStaticScratchBytes = (size_t)DELS_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+struct StaticScratch {
+  void* ptr = nullptr;
+};
+StaticScratch g_static_scratch_dev[kMaxDevices];
+std::mutex g_static_scratch_mu;
+
+// Device address of g_static_scratch on the current device, looked up once per device
+// (the symbol's host-side name is not a device pointer and must never reach a kernel).
+int static_scratch_for_current_device(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(DELS_ERR_INVALID_ARG, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (g_static_scratch_dev[dev].ptr == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255u) != 0)
+      return fail(DELS_ERR_CUDA, "static scratch address is NULL or not 256-byte aligned");
+    g_static_scratch_dev[dev].ptr = p;
+  }
+  *out = g_static_scratch_dev[dev].ptr;
+  return DELS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dels_draft_score_bf16_noalloc(const void* h, int64_t ld_h, const void* W, int64_t ld_w, const void* w_rank,
+                                  int64_t ld_wr, const void* Vr, int64_t ld_vr, const float* prior,
+                                  const float* alpha, const float* beta, int n_pos, const int32_t* row_pos, int rows,
+                                  const int32_t* rows_dev, int H, int r, int V, int64_t v_begin, int activation,
+                                  int64_t* keys, int64_t* idx_out, float* score_out, void* stream) {
+  if (rows < 0 || H <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape rows=%d H=%d r=%d", rows, H, r);
+  const size_t need = dels_score_workspace_bytes(rows, H, r);
+  if (need > kStaticScratchBytes)
+    return fail(DELS_ERR_WORKSPACE,
+                "rows=%d, H=%d, r=%d need %zu bytes of scratch; the allocation-free entry point has %zu "
+                "(use dels_draft_score_bf16 with a caller-provided workspace)",
+                rows, H, r, need, kStaticScratchBytes);
+  void* scratch = nullptr;
+  int rc = static_scratch_for_current_device(&scratch);
+  if (rc != DELS_OK) return rc;
+  return dels_draft_score_bf16(h, ld_h, W, ld_w, w_rank, ld_wr, Vr, ld_vr, prior, alpha, beta, n_pos, row_pos, rows,
+                               rows_dev, H, r, V, v_begin, activation, keys, idx_out, score_out, scratch,
+                               kStaticScratchBytes, stream);
+}
+
+}  // extern "C"

@@ -221,6 +221,27 @@ DELS_API int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_str
                                           const float* alpha, int n_pos, int B, int r, int V, void* s_scaled,
                                           int64_t* keys, void* ws, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Allocation-free variant of dels_draft_score_bf16 (no counterpart in the reference).
+ * For callers that cannot hand the library device memory — an FFI host without a
+ * device allocator, or a serving engine whose memory pool already owns the device —
+ * the scratch lives in a fixed array of DELS_NOALLOC_SCRATCH_BYTES that the library
+ * reserves on each device it is loaded on, for the life of the process.  Same
+ * arguments and results as dels_draft_score_bf16 without ws / ws_bytes; shapes whose
+ * dels_score_workspace_bytes(rows, H, r) exceeds the array are rejected with
+ * DELS_ERR_WORKSPACE (the Qwen3-8B block batch, 512 x 4096 x 256, fits).  The first
+ * call on a device looks up the array's device address; make that first call before
+ * any stream capture.  All calls share the one array: calls that may overlap on the
+ * device race, so serialise them.  Never calls cudaMalloc / cudaFree.
+ * --------------------------------------------------------------------------------- */
+#define DELS_NOALLOC_SCRATCH_BYTES (12u * 1024u * 1024u)
+DELS_API int dels_draft_score_bf16_noalloc(const void* h, int64_t ld_h, const void* W, int64_t ld_w,
+                                           const void* w_rank, int64_t ld_wr, const void* Vr, int64_t ld_vr,
+                                           const float* prior, const float* alpha, const float* beta, int n_pos,
+                                           const int32_t* row_pos, int rows, const int32_t* rows_dev, int H, int r,
+                                           int V, int64_t v_begin, int activation, int64_t* keys, int64_t* idx_out,
+                                           float* score_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
