@@ -54,6 +54,16 @@ def peaks() -> tuple[float, float, str]:
     return 1590.0, 6650.0, "fallback"
 
 
+def peaks_sustained() -> float:
+    """bf16 TFLOP/s sustained under the power cap (seconds-long GEMM loop)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"])
+    return 1400.0
+
+
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -142,10 +152,11 @@ def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None
     end.record(stream)
     torch.cuda.synchronize()
     hold_steps = 0
-    if clocks is not None and hold_ms > 0:
+    if hold_ms > 0:
         est = max_over_ranks(start.elapsed_time(end) / max(warmup, 1), world, dev)
         hold_steps = int(min(5000, max(1, hold_ms / max(est, 1e-3))))
-        clocks.start()
+        if clocks is not None:
+            clocks.start()
         for _ in range(hold_steps):
             fn()
         torch.cuda.synchronize()
@@ -262,13 +273,16 @@ def run_ours(args, rank, world, dev):
     ms = timed(step, args.steps, args.warmup, world, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
     ms = max_over_ranks(ms, world, dev)
-    ms_e2e = max_over_ranks(timed(e2e_step, args.steps, args.warmup, world, stream), world, dev)
-    ms_main = timed(main_kernel, args.steps, args.warmup, 1, stream) / args.steps
+    # e2e and the scorer-alone timing run under the same sustained load as `value`
+    ms_e2e = max_over_ranks(timed(e2e_step, args.steps, args.warmup, world, stream, dev, hold_ms=500.0), world, dev)
+    ms_main = timed(main_kernel, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0) / args.steps
     ws.check()
     bound = "hbm" if fp32 else "tensor"
     if bound == "tensor":
         achieved = flops_main / (ms_main * 1e-3) / 1e12
-        peak, unit = pk_tflops, "TFLOP/s"
+        # the scorer is timed after a 0.5 s load phase, at the power-capped clocks of a
+        # long run: its denominator is the sustained bf16 peak (burst given beside it)
+        peak, unit = peaks_sustained(), "TFLOP/s"
     else:
         achieved = bytes_main / (ms_main * 1e-3) / 1e9
         peak, unit = pk_gbs, "GB/s"
@@ -299,7 +313,9 @@ def run_ours(args, rank, world, dev):
                 "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                     "frac": achieved / peak, "traffic": traffic, "peak_source": f"{pk_src} (burst)",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{pk_src} ({'sustained' if bound == 'tensor' else 'copy'})",
+                     "frac_of_burst_peak": achieved / pk_tflops if bound == "tensor" else None,
                      "kernel_ms": ms_main, "algorithmic": flops_main if bound == "tensor" else bytes_main},
         "clocks": clk,
     }
@@ -356,7 +372,7 @@ def run_ragged(args, rank, world, dev):
         tok_host.copy_(out.tokens, non_blocking=True)
         acc_host.copy_(acc, non_blocking=True)
 
-    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream)
+    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0)
     flops = 2.0 * total * wl.V * (wl.H + wl.r)
     _, s_scaled = ops.rank_project_bf16(packed[:total], t["w_rank"], t["alpha"], n_pos=P, row_pos=row_pos[:total],
                                         want_state=False)
@@ -366,7 +382,7 @@ def run_ragged(args, rank, world, dev):
     main = lambda: ops.fused_argmax_bf16(packed[:total], t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=P,  # noqa: E731
                                          row_pos=row_pos[:total], keys_ready=True, out=ks, ws=mws)
     ops.keys_init(ks.keys)
-    ms_main = timed(main, args.steps, args.warmup, 1, stream) / args.steps
+    ms_main = timed(main, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0) / args.steps
     ws.check()
     achieved = flops / (ms_main * 1e-3) / 1e12
     return {
@@ -380,9 +396,9 @@ def run_ragged(args, rank, world, dev):
                 "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in hh.values()),
                 "d2h_bytes_per_step": tok_host.numel() * 8 + acc_host.numel() * 4},
         "gpu_launches": 5 * args.steps,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk_tflops, "unit": "TFLOP/s",
-                     "frac": achieved / pk_tflops, "traffic": None, "peak_source": f"{pk_src} (burst)",
-                     "kernel_ms": ms_main},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks_sustained(), "unit": "TFLOP/s",
+                     "frac": achieved / peaks_sustained(), "traffic": None, "peak_source": f"{pk_src} (sustained)",
+                     "frac_of_burst_peak": achieved / pk_tflops, "kernel_ms": ms_main},
         "clocks": clk,
     }
 
@@ -422,10 +438,10 @@ def run_rnn(args, rank, world, dev):
         step(x_dev)
         tok_host.copy_(out.tokens, non_blocking=True)
 
-    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream)
+    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0)
     ms_main = timed(lambda: ops.fused_argmax_bf16(t["x"], t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=16,
                                                   keys_ready=True, out=out, ws=mws),
-                    args.steps, args.warmup, 1, stream) / args.steps
+                    args.steps, args.warmup, 1, stream, dev, hold_ms=500.0) / args.steps
     ws.check()
     flops = 2.0 * rows * wl.V * (wl.H + wl.r)
     achieved = flops / (ms_main * 1e-3) / 1e12
@@ -439,9 +455,9 @@ def run_rnn(args, rank, world, dev):
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": rows * 8},
         "gpu_launches": 3 * args.steps,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk_tflops, "unit": "TFLOP/s",
-                     "frac": achieved / pk_tflops, "traffic": None, "peak_source": f"{pk_src} (burst)",
-                     "kernel_ms": ms_main},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks_sustained(), "unit": "TFLOP/s",
+                     "frac": achieved / peaks_sustained(), "traffic": None, "peak_source": f"{pk_src} (sustained)",
+                     "frac_of_burst_peak": achieved / pk_tflops, "kernel_ms": ms_main},
         "clocks": clk,
     }
 
