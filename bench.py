@@ -139,7 +139,53 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
-def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None, hold_ms: float = 0.0) -> float:
+class PipelinedE2E:
+    """Serving-style end-to-end loop through the public API.
+
+    Every step copies its input rows host -> device (pinned memory) on an H2D stream,
+    scores them on the compute stream once they have landed, and copies the token ids
+    back on a D2H stream.  Two device input / output slots let the copy of step i+1
+    overlap the scoring of step i, as a serving loop would; all copies stay inside the
+    timed region (``drain`` makes the compute stream wait for the last read-back)."""
+
+    def __init__(self, host_in: torch.Tensor, score, rows: int, dev, stream):
+        self.host_in = host_in
+        self.score = score
+        self.stream = stream
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.dev_in = [torch.empty_like(host_in, device=dev) for _ in range(2)]
+        self.tokens = [torch.empty(rows, dtype=torch.int64, device=dev) for _ in range(2)]
+        self.host_out = [torch.empty(rows, dtype=torch.int64).pin_memory() for _ in range(2)]
+        self.in_ready = [torch.cuda.Event() for _ in range(2)]
+        self.done = [torch.cuda.Event() for _ in range(2)]
+        self.read = [torch.cuda.Event() for _ in range(2)]
+        for e in self.done + self.read:
+            e.record(stream)
+        self.i = 0
+
+    def step(self):
+        slot = self.i & 1
+        self.i += 1
+        with torch.cuda.stream(self.h2d):
+            self.h2d.wait_event(self.done[slot])  # the slot's previous scoring has consumed it
+            self.dev_in[slot].copy_(self.host_in, non_blocking=True)
+            self.in_ready[slot].record(self.h2d)
+        self.stream.wait_event(self.in_ready[slot])
+        self.stream.wait_event(self.read[slot])  # the slot's previous tokens were read back
+        self.score(self.dev_in[slot], self.tokens[slot])
+        self.done[slot].record(self.stream)
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(self.done[slot])
+            self.host_out[slot].copy_(self.tokens[slot], non_blocking=True)
+            self.read[slot].record(self.d2h)
+
+    def drain(self):
+        self.stream.wait_stream(self.d2h)
+
+
+def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None, hold_ms: float = 0.0,
+          drain=None) -> float:
     """ms for exactly `steps` calls of fn: CUDA events on `stream`, barrier + synchronize on
     both sides.  With `clocks`, the nvidia-smi sampler runs from before a load phase of
     about `hold_ms` (same step count on every rank) until the timed region has ended, so
@@ -160,10 +206,14 @@ def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None
         for _ in range(hold_steps):
             fn()
         torch.cuda.synchronize()
+    if drain is not None:
+        drain()
     barrier(world)
     start.record(stream)
     for _ in range(steps):
         fn()
+    if drain is not None:
+        drain()
     end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
@@ -239,14 +289,23 @@ def run_ours(args, rank, world, dev):
         bytes_main = (t["W"].numel() * t["W"].element_size() + t["Vr"].numel() * t["Vr"].element_size()
                       + t["prior"].numel() * 4 + rows * (H + r) * t["h"].element_size() + rows * 8)
         h_host = t["h"].cpu().pin_memory()
-        tok_host = torch.empty(rows, dtype=torch.int64).pin_memory()
-        h_dev = torch.empty_like(t["h"])
-        bi, bo = h_host.numel() * h_host.element_size(), tok_host.numel() * 8
+        bi, bo = h_host.numel() * h_host.element_size(), rows * 8
+        e2e_outs = [ops.ScoreOut(tokens=None, scores=None, keys=torch.empty(rows, dtype=torch.int64, device=dev))
+                    for _ in range(2)]
+        e2e_ws = [ops.Workspace(need, dev) for _ in range(2)]
 
-        def e2e_step():
-            h_dev.copy_(h_host, non_blocking=True)
-            step(h_dev)
-            tok_host.copy_(out.tokens, non_blocking=True)
+        def e2e_score(h_in, tokens, _slot=[0]):
+            o, w = e2e_outs[_slot[0]], e2e_ws[_slot[0]]
+            _slot[0] ^= 1
+            o.tokens = tokens
+            score(h_in, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
+                  v_begin=v0, keys_only=sharded, out=o, ws=w)
+            if sharded:
+                torch.distributed.all_reduce(o.keys, op=torch.distributed.ReduceOp.MAX)
+                ops.keys_decode(o.keys, tokens=tokens, with_scores=False)
+
+        pipe = PipelinedE2E(h_host, e2e_score, rows, dev, stream)
+        e2e_step = pipe.step
 
         # roofline: the scorer kernel alone (bf16: tcgen05 fused argmax; fp32: fp32 scorer pass)
         if not fp32:
@@ -274,7 +333,8 @@ def run_ours(args, rank, world, dev):
     clk = clocks.stop()
     ms = max_over_ranks(ms, world, dev)
     # e2e and the scorer-alone timing run under the same sustained load as `value`
-    ms_e2e = max_over_ranks(timed(e2e_step, args.steps, args.warmup, world, stream, dev, hold_ms=500.0), world, dev)
+    ms_e2e = max_over_ranks(timed(e2e_step, args.steps, args.warmup, world, stream, dev, hold_ms=500.0,
+                                  drain=pipe.drain), world, dev)
     ms_main = timed(main_kernel, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0) / args.steps
     ws.check()
     bound = "hbm" if fp32 else "tensor"

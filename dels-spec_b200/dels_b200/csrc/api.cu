@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -13,6 +14,7 @@
 #include "runner_kernels.cuh"
 #include "small_kernels.cuh"
 #include "tc_gemm.cuh"
+#include "tc_scorer_pair.cuh"
 
 using namespace dels;
 
@@ -26,6 +28,9 @@ constexpr int kTargetCtas = 148;
 // the vocabulary together; the last partial wave's tiles are split 4 ways along N.
 constexpr int kScorerGroupM = 16;
 constexpr int kScorerTailSplit = 4;
+// Paired scorer enabled (DELS_SCORER_PAIRS=0 in the environment selects the
+// single-CTA scorer for every shape, e.g. to compare the two).
+bool g_use_pairs = true;
 
 thread_local std::string g_last_error;
 
@@ -88,10 +93,28 @@ int make_map_bf16(CUtensorMap* m, const void* ptr, long long inner, long long ou
   return DELS_OK;
 }
 
+// 2-D fp32 tensor map, box = [box_outer rows, 32 elements] (128 bytes), optional
+// 128-byte swizzle, zero fill outside the extents.
+int make_map_f32(CUtensorMap* m, const void* ptr, long long inner, long long outer, long long ld, int box_outer,
+                 bool swizzle) {
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {32u, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DELS_ERR_CUDA, "cuTensorMapEncodeTiled (fp32) failed (%d) for [%lld x %lld], ld %lld", (int)r, outer,
+                inner, ld);
+  return DELS_OK;
+}
+
 // ------------------------------------------------------------------ per-device state
 struct DeviceState {
   bool ready = false;
   int sm_count = 0;
+  int max_pairs = 0;  // co-resident 2-CTA clusters of the paired scorer
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -110,6 +133,7 @@ int init_device(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return fail(DELS_ERR_INVALID_ARG, "device %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_dev_mu);
   if (g_dev[dev].ready) return DELS_OK;
+  if (const char* env = getenv("DELS_SCORER_PAIRS")) g_use_pairs = env[0] != '0';
   int prev = -1;
   cudaError_t e = cudaGetDevice(&prev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -131,6 +155,8 @@ int init_device(int dev) {
     SET((tc_gemm_kernel<64, kStore, false>), TcConfig<64>::kSmemBytes);
     SET((tc_gemm_kernel<32, kStore, false>), TcConfig<32>::kSmemBytes);
     if (rc == DELS_OK && (e = f32_score_setup(kMaxSmem)) != cudaSuccess) rc = cuda_fail(e, "kernel setup: f32_score");
+    SET((tc_scorer_pair_kernel<false>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<true>), PairConfig::kSmemBytes);
     SET(rnn_recurrence_kernel, kMaxSmem);
     SET(rank_finalize_kernel, 0);
     SET(keys_init_kernel, 0);
@@ -144,6 +170,19 @@ int init_device(int dev) {
 #undef SET
   }
   if (rc == DELS_OK) {
+    // A persistent grid of CTA pairs must fit on the device at once: ask the occupancy
+    // calculator how many 2-CTA clusters can be resident (SMs pair up within a GPC).
+    int pairs = 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = PairConfig::kSmemBytes;
+    e = cudaOccupancyMaxActiveClusters(&pairs, (const void*)tc_scorer_pair_kernel<false>, &cfg);
+    if (e != cudaSuccess || pairs <= 0) {
+      cudaGetLastError();
+      pairs = 0;  // the paired scorer is not used on this device
+    }
+    g_dev[dev].max_pairs = pairs < sms / 2 ? pairs : sms / 2;
     g_dev[dev].sm_count = sms;
     g_dev[dev].ready = true;
   }
@@ -240,6 +279,46 @@ int launch_tc(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) 
   tc_gemm_kernel<BN, MODE, VB><<<grid, kTcThreads, TcConfig<BN>::kSmemBytes, st>>>(ma0, mb0, ma1, mb1, mb0t, mb1t,
                                                                                    args);
   DELS_CHECK_LAUNCH("tc_gemm_kernel launch");
+  return DELS_OK;
+}
+
+// The paired (cta_group::2) scorer: 256-row pair tiles, each CTA stages 128 rows of A
+// and half of the 256-token B tile (128 rows; 32 rows for the split tail units).
+template <bool VB>
+int launch_scorer_pair(const TcOperands& op, TcArgs args, int max_pairs, cudaStream_t st) {
+  int rc = ensure_encode();
+  if (rc != DELS_OK) return rc;
+  constexpr int half = PairConfig::kHalfBN;
+  const int tail_half = PairConfig::BN / (args.tail_split > 1 ? args.tail_split : 1) / 2;
+  CUtensorMap ma0, mb0, ma1, mb1, mb0t, mb1t;
+  if (op.K1 > 0) {
+    if ((rc = make_map_bf16(&ma1, op.a1, op.K1, op.m_extent, op.lda1, kBM)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb1, op.b1, op.K1, op.n_extent, op.ldb1, half)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb1t, op.b1, op.K1, op.n_extent, op.ldb1, tail_half)) != DELS_OK) return rc;
+  }
+  if (op.K0 > 0) {
+    if ((rc = make_map_bf16(&ma0, op.a0, op.K0, op.m_extent, op.lda0, kBM)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb0, op.b0, op.K0, op.n_extent, op.ldb0, half)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&mb0t, op.b0, op.K0, op.n_extent, op.ldb0, tail_half)) != DELS_OK) return rc;
+  } else {
+    ma0 = ma1;
+    mb0 = mb1;
+    mb0t = mb1t;
+  }
+  if (op.K1 == 0) {
+    ma1 = ma0;
+    mb1 = mb0;
+    mb1t = mb0t;
+  }
+  args.kb0 = cdiv(op.K0, kBK);
+  args.kb1 = cdiv(op.K1, kBK);
+  const long long tiles = (long long)cdiv(op.m_extent, 2 * kBM) * cdiv(op.n_extent, PairConfig::BN);
+  const long long want = tiles < max_pairs ? tiles * (args.tail_split > 1 ? args.tail_split : 1) : tiles;
+  const int pairs = (int)(want < max_pairs ? want : max_pairs);
+  if (pairs <= 0) return DELS_OK;
+  tc_scorer_pair_kernel<VB><<<2 * pairs, kTcThreads, PairConfig::kSmemBytes, st>>>(ma0, mb0, ma1, mb1, mb0t, mb1t,
+                                                                                   args);
+  DELS_CHECK_LAUNCH("tc_scorer_pair_kernel launch");
   return DELS_OK;
 }
 
@@ -390,6 +469,12 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
   a.score_out = score_out;
   a.counter = hdr.counter;
   const bool vec_base = base != nullptr && aligned16(base) && (ld_base % 8) == 0;
+  if (rows > kBM && ds->max_pairs > 0 && g_use_pairs) {
+    // More than one 128-row tile: CTA pairs share each LM-head tile across two SMs.
+    a.group_m = kScorerGroupM / 2;
+    if (vec_base) return launch_scorer_pair<true>(op, a, ds->max_pairs, st);
+    return launch_scorer_pair<false>(op, a, ds->max_pairs, st);
+  }
   if (vec_base) return launch_tc<256, kArgmax, true>(op, a, ds->sm_count, st);
   return launch_tc<256, kArgmax, false>(op, a, ds->sm_count, st);
 }
@@ -553,9 +638,9 @@ int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t l
     return fail(DELS_ERR_UNSUPPORTED, "fp32 scorer needs H %% 4 == 0 and r %% 4 == 0 (H=%d, r=%d)", H, r);
   if (h == nullptr || W == nullptr || w_rank == nullptr || Vr == nullptr)
     return fail(DELS_ERR_INVALID_ARG, "NULL operand");
-  if (!aligned16(W) || !aligned16(Vr) || (ld_w % 4) != 0 || (ld_vr % 4) != 0 || ld_w < H || ld_vr < r || ld_h < H ||
-      ld_wr < H)
-    return fail(DELS_ERR_ALIGNMENT, "fp32 W / Vr need 16-byte aligned rows (ld %% 4 == 0)");
+  if (!aligned16(W) || !aligned16(Vr) || !aligned16(h) || (ld_w % 4) != 0 || (ld_vr % 4) != 0 || (ld_h % 4) != 0 ||
+      ld_w < H || ld_vr < r || ld_h < H || ld_wr < H)
+    return fail(DELS_ERR_ALIGNMENT, "fp32 h / W / Vr need 16-byte aligned rows (ld %% 4 == 0)");
   const int have_keys = 1;
   if ((rc = check_common_score_args(rows, V, v_begin, beta, prior, n_pos, &have_keys)) != DELS_OK) return rc;
   WsHeader hdr;
@@ -577,17 +662,19 @@ int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t l
                                           reinterpret_cast<long long*>(keys), hdr.counter);
     DELS_CHECK_LAUNCH("f32_rank_kernel launch");
   }
-  const int kp = f32_padded_k(H, r);
-  int rows_per_pass = 16;
-  while (rows_per_pass > 4 && (size_t)rows_per_pass * kp * 4 > (size_t)kMaxSmem) rows_per_pass /= 2;
-  if ((size_t)rows_per_pass * kp * 4 > (size_t)kMaxSmem)
-    return fail(DELS_ERR_UNSUPPORTED, "fp32 scorer: H + r = %d too large for shared memory", H + r);
-  const size_t smem = (size_t)rows_per_pass * kp * 4;
-  for (int row0 = 0; row0 < rows; row0 += rows_per_pass) {
-    const int nrows = rows - row0 < rows_per_pass ? rows - row0 : rows_per_pass;
-    const int grid = ds->sm_count;
-    cudaError_t e = f32_score_launch(rows_per_pass, grid, smem, st, h, ld_h, s_scaled, W, ld_w, Vr, ld_vr, prior, beta,
-                                     n_pos, row_pos, row0, nrows, H, r, V, v_begin, reinterpret_cast<long long*>(keys));
+  if ((rc = ensure_encode()) != DELS_OK) return rc;
+  // W / Vr: 32-float x 64-row boxes, 128-byte swizzle (the kernel reads 32 rows at one k)
+  CUtensorMap mw, mvr;
+  if ((rc = make_map_f32(&mw, W, H, V, ld_w, 64, true)) != DELS_OK) return rc;
+  if ((rc = make_map_f32(&mvr, Vr, r, V, ld_vr, 64, true)) != DELS_OK) return rc;
+  const int kb0 = cdiv(H, 64), kb1 = cdiv(r, 64);
+  for (int row0 = 0; row0 < rows; row0 += 16) {
+    const int nrows = rows - row0 < 16 ? rows - row0 : 16;
+    CUtensorMap mh, ms;
+    if ((rc = make_map_f32(&mh, h + (long long)row0 * ld_h, H, nrows, ld_h, 16, false)) != DELS_OK) return rc;
+    if ((rc = make_map_f32(&ms, s_scaled + (long long)row0 * r, r, nrows, r, 16, false)) != DELS_OK) return rc;
+    cudaError_t e = f32_score_launch(ds->sm_count, st, mw, mh, mvr, ms, kb0, kb1, prior, beta, n_pos, row_pos, row0,
+                                     nrows, V, v_begin, reinterpret_cast<long long*>(keys), hdr.status);
     if (e != cudaSuccess) return cuda_fail(e, "f32_score_kernel launch");
   }
   if (idx_out != nullptr) {

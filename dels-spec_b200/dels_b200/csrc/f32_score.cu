@@ -54,153 +54,217 @@ __global__ void f32_rank_kernel(const float* __restrict__ h, long long ld_h, con
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
 }
 
-template <int ROWS>
-__global__ void __launch_bounds__(kF32Threads, 1)
-    f32_score_kernel(const float* __restrict__ h, long long ld_h, const float* __restrict__ s_scaled,
-                     const float* __restrict__ W, long long ld_w, const float* __restrict__ vr, long long ld_vr,
-                     const float* __restrict__ prior, const float* __restrict__ beta, int n_pos,
-                     const int* __restrict__ row_pos, int row0, int nrows, int H, int r, int V, long long v_begin,
-                     long long* keys) {
-  constexpr int NV = ROWS >= 16 ? 4 : 8;  // vocabulary rows per warp iteration
-  constexpr int N = ROWS * NV;  // partial sums per lane
-  constexpr int PER_LANE = N / 32;
-  constexpr int LANES_PER_ROW = NV / PER_LANE;
-  static_assert(N >= 32 && (N % 32) == 0, "ROWS * NV must be a multiple of 32");
-  extern __shared__ float4 a_s4[];
-  float* a_s = reinterpret_cast<float*>(a_s4);
+// ------------------------------------------------------------------------------------
+// fp32 scorer.  Persistent: CTA c owns a contiguous run of 64-token vocabulary tiles.
+// Each K block of 64 is staged by TMA: the tile's 64 W rows (two 32-float boxes, 128-B
+// swizzle, so a warp reading 32 different rows at one k hits 8 distinct 16-B banks
+// groups per wavefront) and the pass's 16 [h | s'] rows (two boxes, read as shared-
+// memory broadcasts).  Compute warp w owns the 4-wide K slice [4w, 4w+4) of every block
+// (one 16-byte chunk of a 128-byte row) and keeps, per lane, 2 vocabulary rows x 16 data
+// rows of partial sums in registers; after the last K block the 16 slices are summed
+// through shared memory, the prior term applied, and each thread keeps a running packed
+// (score, index) key for one data row.  Sixteen compute warps give the SM enough warps
+// to hide shared-memory latency; a seventeenth issues the TMA loads (6-stage mbarrier
+// ring, bounded waits).
+// ------------------------------------------------------------------------------------
+namespace {
+constexpr int kF32TileV = 64;                       // vocabulary rows per tile
+constexpr int kF32Rows = 16;                        // data rows per pass
+constexpr int kF32KB = 64;                          // K per stage
+constexpr int kF32WBox = 32 * kF32TileV * 4;        // one 32-float x 64-row box: 8 KB
+constexpr int kF32HBox = 32 * kF32Rows * 4;         // one 32-float x 16-row box: 2 KB
+constexpr int kF32StageBytes = 2 * kF32WBox + 2 * kF32HBox;  // 20 KB
+constexpr int kF32Stages = 6;
+constexpr int kF32ComputeWarps = 16;
+constexpr int kF32RedBytes = kF32ComputeWarps * kF32TileV * kF32Rows * 4;  // 32 KB
+}  // namespace
 
-  const int kp = f32_padded_k(H, r);  // padded K' = H + r rounded up to 128
-  // Stage [h | s' | 0] for the pass's rows in shared memory.
-  for (int e = threadIdx.x; e < ROWS * kp; e += blockDim.x) {
-    const int rr = e / kp, k = e % kp;
-    float x = 0.0f;
-    if (rr < nrows) {
-      if (k < H)
-        x = h[(long long)(row0 + rr) * ld_h + k];
-      else if (k - H < r)
-        x = s_scaled[(long long)(row0 + rr) * r + (k - H)];
+int f32_score_smem_bytes() { return kF32Stages * kF32StageBytes + kF32RedBytes + 256 + 1024; }
+
+__global__ void __launch_bounds__(kF32Threads, 1)
+    f32_score_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_h,
+                     const __grid_constant__ CUtensorMap map_vr, const __grid_constant__ CUtensorMap map_s,
+                     int kb0, int kb1, const float* __restrict__ prior, const float* __restrict__ beta, int n_pos,
+                     const int* __restrict__ row_pos, int row0, int nrows, int V, long long v_begin,
+                     long long* keys, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_addr - raw_addr);
+  float* red = reinterpret_cast<float*>(smem + kF32Stages * kF32StageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kF32Stages * kF32StageBytes + kF32RedBytes);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kF32Stages);
+  auto full_bar = [&](int st) { return smem_u32(&bars[st]); };
+  auto empty_bar = [&](int st) { return smem_u32(&bars[kF32Stages + st]); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = (V + kF32TileV - 1) / kF32TileV;
+  const int t_lo = (int)((long long)tiles * blockIdx.x / gridDim.x);
+  const int t_hi = (int)((long long)tiles * (blockIdx.x + 1) / gridDim.x);
+  const int nkb = kb0 + kb1;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kF32Stages; ++st) {
+      mbar_init(full_bar(st), 1);
+      mbar_init(empty_bar(st), kF32ComputeWarps);
     }
-    a_s[e] = x;
+    *abort_flag = 0;
+    mbar_fence_init();
   }
   __syncthreads();
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gwarp = blockIdx.x * (kF32Threads / 32) + warp;
-  const int nwarps = gridDim.x * (kF32Threads / 32);
-  const int ngroups = (V + NV - 1) / NV;
-  const int nchunks = kp / 128;
+  if (warp == kF32ComputeWarps) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int st = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = t_lo; t < t_hi && ok; ++t) {
+        const int v0 = t * kF32TileV;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(empty_bar(st), phase ^ 1u, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = base_addr + st * kF32StageBytes;
+          mbar_arrive_expect_tx(full_bar(st), kF32StageBytes);
+          const bool seg0 = kb < kb0;
+          const int k = (seg0 ? kb : kb - kb0) * kF32KB;
+          const CUtensorMap* mw = seg0 ? &map_w : &map_vr;
+          const CUtensorMap* mh = seg0 ? &map_h : &map_s;
+          tma_load_2d(dst, mw, full_bar(st), k, v0);
+          tma_load_2d(dst + kF32WBox, mw, full_bar(st), k + 32, v0);
+          tma_load_2d(dst + 2 * kF32WBox, mh, full_bar(st), k, 0);
+          tma_load_2d(dst + 2 * kF32WBox + kF32HBox, mh, full_bar(st), k + 32, 0);
+          if (++st == kF32Stages) {
+            st = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    return;  // the producer takes no part in the reduction barriers below
+  }
 
-  const int my_row = (lane * PER_LANE) / NV;
-  const int my_vi0 = (lane * PER_LANE) % NV;
+  // -------------------------------------------------------------- compute warps
+  const int box = warp >> 3;            // which 32-wide half of the K block
+  const int c = warp & 7;               // this warp's 16-byte chunk of each 128-byte row
+  // epilogue ownership: data row r_own, vocabulary rows v_own + 32 i
+  const int r_own = threadIdx.x & 15;
+  const int v_own = threadIdx.x >> 4;   // 0..31
   float negb = 0.0f;
-  if (my_row < nrows && prior != nullptr) negb = -beta[row_position(row_pos, row0 + my_row, n_pos)];
+  if (r_own < nrows && prior != nullptr) negb = -beta[row_position(row_pos, row0 + r_own, n_pos)];
   long long best_key = kKeyEmpty;
+  int st = 0;
+  uint32_t phase = 0;
+  bool ok = true;
 
-  for (int g = gwarp; g < ngroups; g += nwarps) {
-    const int v0 = g * NV;
-    float acc[N];
+  for (int t = t_lo; t < t_hi && ok; ++t) {
+    const int v0 = t * kF32TileV;
+    float acc[2][kF32Rows];
 #pragma unroll
-    for (int i = 0; i < N; ++i) acc[i] = 0.0f;
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int r = 0; r < kF32Rows; ++r) acc[j][r] = 0.0f;
 
-#pragma unroll 1
-    for (int c = 0; c < nchunks; ++c) {
-      const int k = c * 128 + 4 * lane;
-      float4 w[NV];
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (!mbar_wait(full_bar(st), phase, abort_flag, status)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* stage = smem + st * kF32StageBytes;
+      const uint8_t* wbox = stage + box * kF32WBox;
+      const float* hbox = reinterpret_cast<const float*>(stage + 2 * kF32WBox + box * kF32HBox);
+      {
+        float4 w[2];
 #pragma unroll
-      for (int vi = 0; vi < NV; ++vi) {
-        const int v = v0 + vi;
-        w[vi] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (v < V) {
-          if (k < H)
-            w[vi] = __ldg(reinterpret_cast<const float4*>(W + (long long)v * ld_w + k));
-          else if (k - H < r)
-            w[vi] = __ldg(reinterpret_cast<const float4*>(vr + (long long)v * ld_vr + (k - H)));
+        for (int j = 0; j < 2; ++j) {
+          const int v = lane + 32 * j;
+          w[j] = *reinterpret_cast<const float4*>(wbox + v * 128 + ((c ^ (v & 7)) << 4));
+        }
+#pragma unroll
+        for (int r = 0; r < kF32Rows; ++r) {
+          const float4 hv = *reinterpret_cast<const float4*>(hbox + r * 32 + c * 4);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            float a = acc[j][r];
+            a = fmaf(w[j].x, hv.x, a);
+            a = fmaf(w[j].y, hv.y, a);
+            a = fmaf(w[j].z, hv.z, a);
+            a = fmaf(w[j].w, hv.w, a);
+            acc[j][r] = a;
+          }
         }
       }
-#pragma unroll
-      for (int rr = 0; rr < ROWS; ++rr) {
-        const float4 a = a_s4[(rr * kp + k) >> 2];
-#pragma unroll
-        for (int vi = 0; vi < NV; ++vi) {
-          float t = acc[rr * NV + vi];
-          t = fmaf(a.x, w[vi].x, t);
-          t = fmaf(a.y, w[vi].y, t);
-          t = fmaf(a.z, w[vi].z, t);
-          t = fmaf(a.w, w[vi].w, t);
-          acc[rr * NV + vi] = t;
-        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(st));
+      if (++st == kF32Stages) {
+        st = 0;
+        phase ^= 1u;
       }
     }
+    if (!ok) break;
 
-    // Recursive-halving reduce-scatter: afterwards lane l holds the complete sums of
-    // partial-index l*PER_LANE + j, j < PER_LANE (index = row * NV + vi).
+    // sum the 8 K slices: red[warp][v][r]
 #pragma unroll
-    for (int st = 0; st < 5; ++st) {
-      const int o = 16 >> st;
-      const int half = N >> (st + 1);
-      const bool upper = (lane & o) != 0;
+    for (int j = 0; j < 2; ++j) {
+      float4* dst = reinterpret_cast<float4*>(red + (warp * kF32TileV + lane + 32 * j) * kF32Rows);
 #pragma unroll
-      for (int j = 0; j < half; ++j) {
-        const float lo = acc[j], hi = acc[j + half];
-        const float send = select_f32(upper, lo, hi);
-        const float keep = select_f32(upper, hi, lo);
-        acc[j] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
-      }
+      for (int q = 0; q < kF32Rows / 4; ++q)
+        dst[q] = make_float4(acc[j][4 * q], acc[j][4 * q + 1], acc[j][4 * q + 2], acc[j][4 * q + 3]);
     }
-
-    if (my_row < nrows) {
+    asm volatile("bar.sync 1, %0;" ::"r"(kF32ComputeWarps * 32) : "memory");
+    if (r_own < nrows) {
 #pragma unroll
-      for (int j = 0; j < PER_LANE; ++j) {
-        const int v = v0 + my_vi0 + j;
-        if (v < V) {
-          float s = acc[j];
-          if (prior != nullptr) s = fmaf(negb, __ldg(prior + v), s);
-          const long long key = pack_key(s, (uint32_t)(v_begin + v));
+      for (int i = 0; i < kF32TileV / 32; ++i) {
+        const int v = v_own + 32 * i;
+        if (v0 + v < V) {
+          float s = 0.0f;
+#pragma unroll
+          for (int w8 = 0; w8 < kF32ComputeWarps; ++w8) s += red[(w8 * kF32TileV + v) * kF32Rows + r_own];
+          if (prior != nullptr) s = fmaf(negb, __ldg(prior + v0 + v), s);
+          const long long key = pack_key(s, (uint32_t)(v_begin + v0 + v));
           best_key = key > best_key ? key : best_key;
         }
       }
     }
+    asm volatile("bar.sync 1, %0;" ::"r"(kF32ComputeWarps * 32) : "memory");
   }
 
-  // Lanes that share a row combine, then one atomic per (row, warp).
-#pragma unroll
-  for (int o = 1; o < LANES_PER_ROW; o <<= 1) {
-    const long long other = __shfl_xor_sync(0xFFFFFFFFu, best_key, o);
-    best_key = other > best_key ? other : best_key;
+  if (!ok) {
+    // Aborted: give the producer's copies in flight time to land before leaving.
+    const unsigned long long t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < kWaitLimitNs / 40) {
+    }
   }
-  if ((lane % LANES_PER_ROW) == 0 && my_row < nrows && best_key != kKeyEmpty)
-    atomicMax(&keys[row0 + my_row], best_key);
+  // combine the 16 threads that own each data row, one atomic per (row, CTA)
+  const long long other = __shfl_xor_sync(0xFFFFFFFFu, best_key, 16);
+  best_key = other > best_key ? other : best_key;
+  __shared__ long long row_best[kF32ComputeWarps][kF32Rows];
+  if (lane < 16) row_best[warp][lane] = best_key;
+  asm volatile("bar.sync 1, %0;" ::"r"(kF32ComputeWarps * 32) : "memory");
+  if (threadIdx.x < kF32Rows && threadIdx.x < nrows) {
+    long long k = row_best[0][threadIdx.x];
+    for (int w8 = 1; w8 < kF32ComputeWarps; ++w8) k = row_best[w8][threadIdx.x] > k ? row_best[w8][threadIdx.x] : k;
+    if (k != kKeyEmpty) atomicMax(&keys[row0 + threadIdx.x], k);
+  }
 }
 
-cudaError_t f32_score_setup(int max_smem) {
-  cudaError_t e;
+cudaError_t f32_score_setup(int /*max_smem*/) {
+  cudaError_t e = cudaFuncSetAttribute(f32_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       f32_score_smem_bytes());
+  if (e != cudaSuccess) return e;
   cudaFuncAttributes attr;
-  if ((e = cudaFuncSetAttribute(f32_score_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(f32_score_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(f32_score_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncGetAttributes(&attr, f32_score_kernel<16>)) != cudaSuccess) return e;
-  if ((e = cudaFuncGetAttributes(&attr, f32_score_kernel<8>)) != cudaSuccess) return e;
-  return cudaFuncGetAttributes(&attr, f32_score_kernel<4>);
+  return cudaFuncGetAttributes(&attr, f32_score_kernel);
 }
 
-cudaError_t f32_score_launch(int rows_per_pass, int grid, size_t smem, cudaStream_t st, const float* h, long long ld_h,
-                             const float* s_scaled, const float* W, long long ld_w, const float* vr, long long ld_vr,
+cudaError_t f32_score_launch(int grid, cudaStream_t st, const CUtensorMap& map_w, const CUtensorMap& map_h,
+                             const CUtensorMap& map_vr, const CUtensorMap& map_s, int kb0, int kb1,
                              const float* prior, const float* beta, int n_pos, const int* row_pos, int row0,
-                             int nrows, int H, int r, int V, long long v_begin, long long* keys) {
-  switch (rows_per_pass) {
-    case 16:
-      f32_score_kernel<16><<<grid, kF32Threads, smem, st>>>(h, ld_h, s_scaled, W, ld_w, vr, ld_vr, prior, beta, n_pos,
-                                                            row_pos, row0, nrows, H, r, V, v_begin, keys);
-      break;
-    case 8:
-      f32_score_kernel<8><<<grid, kF32Threads, smem, st>>>(h, ld_h, s_scaled, W, ld_w, vr, ld_vr, prior, beta, n_pos,
-                                                           row_pos, row0, nrows, H, r, V, v_begin, keys);
-      break;
-    default:
-      f32_score_kernel<4><<<grid, kF32Threads, smem, st>>>(h, ld_h, s_scaled, W, ld_w, vr, ld_vr, prior, beta, n_pos,
-                                                           row_pos, row0, nrows, H, r, V, v_begin, keys);
-      break;
-  }
+                             int nrows, int V, long long v_begin, long long* keys, int* status) {
+  f32_score_kernel<<<grid, kF32Threads, f32_score_smem_bytes(), st>>>(map_w, map_h, map_vr, map_s, kb0, kb1, prior,
+                                                                      beta, n_pos, row_pos, row0, nrows, V, v_begin,
+                                                                      keys, status);
   return cudaGetLastError();
 }
 
