@@ -19,7 +19,11 @@ What runs, and from where in the reference:
     that run the captured function eagerly, and the Triton kernels are disabled, so the
     runners execute their own torch fallback path (code/kernel/dels.py:447-456);
   * the acceptance expression of code/dflash.py:645-651, evaluated with torch exactly as
-    written there.
+    written there;
+  * the checkpoint loaders of code/dels.py (``detect_local_head_checkpoint_kind``,
+    ``DeLSLocalHead.from_checkpoint`` incl. target-LM-head fusion and merged heads,
+    ``MarkovDeLSLocalHead.from_checkpoint``, ``PositionMixJointHead.from_checkpoint``) on
+    small synthetic SpecForge-style checkpoints written to ``ckpt/``.
 """
 
 from __future__ import annotations
@@ -284,6 +288,136 @@ def gen_accept() -> None:
     )
 
 
+# ------------------------------------------------------------------------------ checkpoints
+def _target(V, E, Hd, seed):
+    g = torch.Generator().manual_seed(seed)
+    emb = torch.randn(V, E, generator=g)
+    head = torch.randn(V, Hd, generator=g) * 0.1
+    target = stub_target(V, E, Hd, torch.float32)
+    with torch.no_grad():
+        target.model.embed_tokens.weight.copy_(emb)
+        target.lm_head.weight.copy_(head)
+    return target, emb, head
+
+
+def gen_checkpoints(ref) -> None:
+    """Small SpecForge-style local-head checkpoints of every kind the reference loads,
+    the reference's verdict on each (kind, parsed attributes, fused weights, forward
+    outputs or the error message) — the pin for the drop-in ``dels.py``."""
+    out_dir = HERE / "ckpt"
+    out_dir.mkdir(exist_ok=True)
+    V, E, G, r, Hd = 64, 8, 16, 4, 12
+    target, emb, head = _target(V, E, Hd, 42)
+    torch.save({"embed": emb, "lm_head": head}, out_dir / "target.pt")
+    g = torch.Generator().manual_seed(7)
+
+    def rnd(*shape, scale=0.3):
+        return torch.randn(*shape, generator=g) * scale
+
+    gru = {"prefix_gru.weight_ih_l0": rnd(3 * G, E), "prefix_gru.weight_hh_l0": rnd(3 * G, G)}
+    cases = {}
+    # (a) direct-vocab RNN head with its own embedding, SiLU rank activation
+    cases["direct_vocab"] = {
+        "model_config": {"rnn_parameterization": "direct_vocab", "vocab_size": V, "embed_dim": E,
+                         "gru_hidden_dim": G, "low_rank_dim": r, "rank_activation": "silu", "shift_label": True},
+        "model_state_dict": {**gru, "embed_tokens.weight": rnd(V, E), "rank_proj.weight": rnd(r, G),
+                             "low_rank_lm_head.weight": rnd(V, r)},
+    }
+    # (b) target-factorised head: low-rank head = target lm_head . rank_to_hidden (fused at load)
+    cases["target_factorized"] = {
+        "model_config": {"local_head_parameterization": "target_factorized", "vocab_size": V, "embed_dim": E,
+                         "gru_hidden_dim": G, "low_rank_dim": r, "lm_head_mode": "target_lm_head",
+                         "pure_draft_prefix_len": 1},
+        "model_state_dict": {**gru, "rank_proj.weight": rnd(r, G), "rank_to_hidden.weight": rnd(Hd, r),
+                             "embed_tokens.weight": emb.clone(), "target_lm_head.weight": head.clone()},
+    }
+    # (c) low-rank head whose weight comes from a separate merged file
+    cases["merged_head"] = {
+        "model_config": {"vocab_size": V, "embed_dim": E, "gru_hidden_dim": G, "low_rank_dim": r},
+        "model_state_dict": {**gru, "rank_proj.weight": rnd(r, G), "rank_to_hidden.weight": rnd(Hd, r)},
+    }
+    torch.save({"weight": rnd(V, r)}, out_dir / "merged_head_weight.pt")
+    # (c') the same with the target-LM-head mode recorded in the config: loads, and the
+    # merged weight replaces the factorised head
+    cases["merged_head_target"] = {
+        "model_config": {"vocab_size": V, "embed_dim": E, "gru_hidden_dim": G, "low_rank_dim": r,
+                         "lm_head_mode": "target_lm_head"},
+        "model_state_dict": {**gru, "rank_proj.weight": rnd(r, G), "rank_to_hidden.weight": rnd(Hd, r)},
+    }
+    # (d) errors: an un-merged input projection; an unexpected tensor
+    cases["input_projection"] = {
+        "model_config": {"vocab_size": V, "embed_dim": E, "gru_hidden_dim": G, "low_rank_dim": r},
+        "model_state_dict": {**gru, "embed_down_proj.weight": rnd(E, E)},
+    }
+    cases["unexpected_tensor"] = {
+        "model_config": {"vocab_size": V, "embed_dim": E, "gru_hidden_dim": G, "low_rank_dim": r},
+        "model_state_dict": {**gru, "rank_proj.weight": rnd(r, G), "low_rank_lm_head.weight": rnd(V, r),
+                             "mystery.weight": rnd(3)},
+    }
+    # (e) Markov heads, merged and factorised
+    cases["markov_merged"] = {"embedding_weight": rnd(V, r), "lm_head_weight": rnd(V, r)}
+    cases["markov_factorized"] = {"model_config": {"rank": r},
+                                  "model_state_dict": {"down_proj": rnd(E, r), "up_proj": rnd(r, Hd)}}
+    # (f) block-prefix position-mix joint head (suffix gates + its own baseline)
+    pm_state = {f"local_head_model.{k}": v for k, v in gru.items()}
+    pm_state.update({"local_head_model.rank_proj.weight": rnd(r, G), "local_head_model.rank_to_hidden.weight": rnd(Hd, r),
+                     "local_head_model.embed_tokens.weight": emb.clone(), "position_gates": rnd(14, 2),
+                     "baseline_logits": rnd(1, V), "optimizer_step": torch.tensor(3)})
+    cases["position_mix"] = {
+        "model_config": {"method": "block_prefix_position_mix_joint", "dflash_shift_label": False,
+                         "local_head_config": {"vocab_size": V, "embed_dim": E, "gru_hidden_dim": G,
+                                               "low_rank_dim": r, "rank_activation": "identity",
+                                               "lm_head_mode": "target_lm_head"}},
+        "model_state_dict": pm_state,
+    }
+    cases["unknown"] = {"something": 1}
+
+    hidden = rnd(1, 3, G, scale=1.0)
+    tokens = torch.tensor([[5], [17], [63]])
+    prev = torch.tensor([[1], [2], [40]])
+    expected = {}
+    arrays = {"hidden": hidden.numpy(), "tokens": tokens.numpy(), "prev": prev.numpy()}
+    cpu = torch.device("cpu")
+    for name, payload in cases.items():
+        path = out_dir / f"{name}.pt"
+        torch.save(payload, path)
+        rec = {}
+        try:
+            rec["kind"] = ref.dels.detect_local_head_checkpoint_kind(str(path))
+        except ValueError as exc:
+            rec["kind_error"] = str(exc)
+        try:
+            if name.startswith("markov"):
+                m = ref.dels.MarkovDeLSLocalHead.from_checkpoint(checkpoint_path=str(path), target_model=target,
+                                                                 dtype=torch.float32, device=cpu)
+                arrays[f"{name}_logits"] = m.logits_from_token(prev).numpy()
+                rec.update(vocab_size=m.vocab_size, rank=m.rank)
+            elif name == "position_mix":
+                m = ref.dels.PositionMixJointHead.from_checkpoint(checkpoint_path=str(path), target_model=target,
+                                                                  block_size=16, dtype=torch.float32, device=cpu)
+                a, b = m.alpha_beta_schedules()
+                rec.update(alpha=a, beta=b, shift_label=m.shift_label, pure=m.pure_draft_prefix_len)
+                arrays[f"{name}_baseline"] = m.baseline_logits.numpy()
+                arrays[f"{name}_logits"] = m.logits_from_hidden(hidden).numpy()
+                arrays[f"{name}_advance"] = m.advance(tokens, hidden).numpy()
+            elif name != "unknown":
+                kw = ({"merged_lm_head_path": str(out_dir / "merged_head_weight.pt")}
+                      if name.startswith("merged_head") else {})
+                m = ref.dels.DeLSLocalHead.from_checkpoint(checkpoint_path=str(path), target_model=target,
+                                                           dtype=torch.float32, device=cpu, **kw)
+                rec.update(lm_head_mode=m.lm_head_mode, pure=m.pure_draft_prefix_len, shift_label=m.shift_label,
+                           rank_activation=m.rank_activation)
+                arrays[f"{name}_low_rank_lm_head"] = m.low_rank_lm_head.weight.detach().numpy()
+                arrays[f"{name}_logits"] = m.logits_from_hidden(hidden).numpy()
+                arrays[f"{name}_advance"] = m.advance(tokens, hidden).numpy()
+                arrays[f"{name}_empty_hidden"] = m.init_empty_hidden(3, device=cpu).numpy()
+        except ValueError as exc:
+            rec["load_error"] = str(exc)
+        expected[name] = rec
+    (out_dir / "expected.json").write_text(json.dumps(expected, indent=1, sort_keys=True) + "\n")
+    np.savez_compressed(out_dir / "outputs.npz", **arrays)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="the reference checkout's code/ directory")
@@ -302,7 +436,8 @@ def main() -> None:
     gen_scorer(ref)
     gen_runners(ref)
     gen_accept()
-    for p in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
+    gen_checkpoints(ref)
+    for p in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")) + sorted((HERE / "ckpt").glob("*")):
         print(f"{p.name}: {p.stat().st_size} bytes")
 
 
