@@ -288,7 +288,13 @@ def run_ours(args, rank, world, dev):
         flops_main = 2.0 * rows * Vloc * (H + r)
         bytes_main = (t["W"].numel() * t["W"].element_size() + t["Vr"].numel() * t["Vr"].element_size()
                       + t["prior"].numel() * 4 + rows * (H + r) * t["h"].element_size() + rows * 8)
-        h_host = t["h"].cpu().pin_memory()
+        # With vocab sharding every rank needs all rows: each rank copies only its 1/N
+        # slice from the host and an NCCL all-gather over NVLink rebuilds the batch, so
+        # the box moves each input byte over PCIe once instead of N times.
+        gather = sharded and rows % world == 0
+        rows_in = rows // world if gather else rows
+        h_host = t["h"][rank * rows_in:(rank + 1) * rows_in].cpu().pin_memory() if gather else t["h"].cpu().pin_memory()
+        h_full = torch.empty_like(t["h"]) if gather else None
         bi, bo = h_host.numel() * h_host.element_size(), rows * 8
         e2e_outs = [ops.ScoreOut(tokens=None, scores=None, keys=torch.empty(rows, dtype=torch.int64, device=dev))
                     for _ in range(2)]
@@ -298,6 +304,9 @@ def run_ours(args, rank, world, dev):
             o, w = e2e_outs[_slot[0]], e2e_ws[_slot[0]]
             _slot[0] ^= 1
             o.tokens = tokens
+            if gather:
+                torch.distributed.all_gather_into_tensor(h_full, h_in)
+                h_in = h_full
             score(h_in, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
                   v_begin=v0, keys_only=sharded, out=o, ws=w)
             if sharded:
@@ -305,6 +314,8 @@ def run_ours(args, rank, world, dev):
                 ops.keys_decode(o.keys, tokens=tokens, with_scores=False)
 
         pipe = PipelinedE2E(h_host, e2e_score, rows, dev, stream)
+        e2e_note = ("per rank: this rank's 1/N row slice (all-gathered over NVLink)" if gather else
+                    "per rank: all rows")
         e2e_step = pipe.step
 
         # roofline: the scorer kernel alone (bf16: tcgen05 fused argmax; fp32: fp32 scorer pass)
@@ -324,6 +335,8 @@ def run_ours(args, rank, world, dev):
         return run_ragged(args, rank, world, dev)
     elif wname == "cfg4":
         return run_rnn(args, rank, world, dev)
+    elif wname == "runner":
+        return run_runner(args, rank, world, dev)
     else:
         raise SystemExit(f"unknown workload {wname}")
 
@@ -370,7 +383,7 @@ def run_ours(args, rank, world, dev):
             "l2": "W alone is larger than L2 (streamed from HBM every step)",
         },
         "e2e": {"value": total_rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
-                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo},
+                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "note": e2e_note},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "traffic": traffic,
@@ -522,6 +535,92 @@ def run_rnn(args, rank, world, dev):
     }
 
 
+def run_runner(args, rank, world, dev):
+    """The drop-in DeLSGraphRunner (kernel/dels.py) at the released local-head shapes
+    (V = 151936, E = 256, G = 1024, r = 256), batch B, 14 suffix steps: one call =
+    copy-in of prefix ids and base logits, CUDA-graph replay, clone of the tokens —
+    exactly the reference runner's __call__ (code/kernel/dels.py:469-478)."""
+    import torch.nn as nn
+
+    import dels as D
+    from kernel.dels import DeLSGraphRunner
+    from dels_b200 import workloads
+
+    if world > 1:
+        raise SystemExit("the runner workload is single-GPU")
+    V, E, G, r, steps, B = workloads.VOCAB, 256, 1024, 256, 14, args.runner_batch
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    stub = type("T", (), {})()
+    stub.model = type("M", (), {})()
+    stub.model.embed_tokens = nn.Embedding(V, E).to(device=dev, dtype=torch.bfloat16)
+    head = D.DeLSLocalHead(target_model=stub, vocab_size=V, embed_dim=E, gru_hidden_dim=G, low_rank_dim=r,
+                           lm_head_mode="low_rank", dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        for p, std in ((head.embed_tokens.weight, 0.5), (head.prefix_gru.weight_ih_l0, 0.05),
+                       (head.prefix_gru.weight_hh_l0, 0.03), (head.rank_proj.weight, 0.05),
+                       (head.low_rank_lm_head.weight, 0.05)):
+            p.copy_(torch.randn(p.shape, generator=g, device=dev) * std)
+    prior = workloads.zipf_log_prior(V, device=dev).to(torch.bfloat16)
+    alpha = workloads.linspace(0.9, 0.3, steps)
+    beta = workloads.linspace(0.3, 0.1, steps)
+    runner = DeLSGraphRunner(local_head=head, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha,
+                             beta_values=beta, baseline_logits=prior, device=dev)
+    base = (torch.randn(B, steps, V, generator=g, device=dev)).to(torch.bfloat16)
+    prefix = torch.randint(0, V, (B, 1), generator=g, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    call = lambda: runner(prefix, base)  # noqa: E731
+    clocks = ClockSampler(dev)
+    ms = timed(call, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
+    clk = clocks.stop()
+    base_host = base.cpu().pin_memory()
+    prefix_host = prefix.cpu().pin_memory()
+    tok_host = torch.empty(B, steps, dtype=torch.int64).pin_memory()
+
+    def e2e_call():
+        out = runner(prefix_host.to(dev, non_blocking=True), base_host.to(dev, non_blocking=True))
+        tok_host.copy_(out, non_blocking=True)
+
+    ms_e2e = timed(e2e_call, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0)
+    _, pk_gbs, pk_src = peaks()
+    per_step = (r * V + 3 * G * G + r * G + B * V + B * 3 * G) * 2  # Vr, W_hh, W_rank, base row, table rows
+    bytes_call = steps * per_step + B * steps * V * 2 * 2  # + copy-in of the base logits (read + write)
+    achieved = bytes_call / (ms / args.steps * 1e-3) / 1e9
+    rows = B * steps
+    res = {
+        "metric": METRIC, "value": rows * args.steps / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, random-init local head at the released shapes)",
+        "config": {"workload": f"runner_b{B}_steps{steps}", "V": V, "E": E, "G": G, "r": r,
+                   "note": "one step = one DeLSGraphRunner call (14 scored positions per sequence)"},
+        "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": base_host.numel() * 2 + B * 8, "d2h_bytes_per_step": B * steps * 8},
+        "gpu_launches": (1 + 3 * steps - 1) * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
+                     "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call,
+                     "note": "Vr (77.8 MB) can stay L2-resident across the 14 steps, so this bound can be beaten"},
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        from oracle.reference_torch import runner_rollout
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        table = torch.nn.functional.linear(head.embed_tokens.weight, head.prefix_gru.weight_ih_l0).cpu()
+        cpu_args = (prefix[:1].cpu(), base[:1].cpu(), table, head.prefix_gru.weight_hh_l0.detach().cpu(),
+                    head.rank_proj.weight.detach().cpu(), head.low_rank_lm_head.weight.detach().cpu(), prior.cpu(),
+                    alpha, beta)
+        runner_rollout(*cpu_args)
+        t0 = time.perf_counter()
+        reps = 2
+        for _ in range(reps):
+            runner_rollout(*cpu_args)
+        dt = (time.perf_counter() - t0) / reps
+        res["cpu_baseline"] = {"value": steps / dt, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+                               "sample": "one batch-1 rollout of 14 steps x 2 repetitions, bf16 torch on the host"}
+    return res
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, dev):
     """The reference's CPU formula on the host cores, same workload / metric / unit."""
@@ -560,7 +659,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="auto", choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "runner"])
+    ap.add_argument("--runner-batch", type=int, default=1, help="batch of the runner workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -167,6 +167,7 @@ int init_device(int dev) {
     SET(gru_step_kernel, kMaxSmem);
     SET(rank_gemv_kernel, kMaxSmem);
     SET(gather_scaled_kernel, 0);
+    SET(wait_selftest_kernel, 0);
 #undef SET
   }
   if (rc == DELS_OK) {
@@ -758,6 +759,19 @@ int dels_pack_rows_bf16(const void* hidden, int64_t ld_seq, int64_t ld_row, int 
   DELS_CHECK_LAUNCH("pack_rows_kernel launch");
   return DELS_OK;
 }
+
+int dels_selftest_bounded_wait(int* status, uint64_t* waited_ns, double limit_ms, void* stream) {
+  if (status == nullptr || waited_ns == nullptr) return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if (!(limit_ms > 0.0 && limit_ms <= 1000.0)) return fail(DELS_ERR_INVALID_ARG, "limit_ms must be in (0, 1000]");
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  wait_selftest_kernel<<<1, 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      status, (unsigned long long)(limit_ms * 1e6), reinterpret_cast<unsigned long long*>(waited_ns));
+  DELS_CHECK_LAUNCH("wait_selftest_kernel launch");
+  return DELS_OK;
+}
+
 
 size_t dels_rnn_workspace_bytes(int n_seq, int T, int H, int r) {
   if (n_seq <= 0 || T <= 0 || H <= 0 || r <= 0) return DELS_WS_HEADER_BYTES;

@@ -131,16 +131,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false if the CTA's
-// abort flag is raised or the wait runs past kWaitLimitNs; in the latter case this
-// thread raises the abort flag and records DELS_ERR_DEVICE_TIMEOUT in *status.
+// abort flag is raised or the wait runs past limit_ns (kWaitLimitNs unless given); in
+// the latter case this thread raises the abort flag and records
+// DELS_ERR_DEVICE_TIMEOUT in *status.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status) {
+                                          int* status, unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       if (status != nullptr) atomicCAS(status, 0, DELS_ERR_DEVICE_TIMEOUT);
       return false;

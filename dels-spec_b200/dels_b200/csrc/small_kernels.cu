@@ -235,4 +235,31 @@ __global__ void __launch_bounds__(256) rnn_recurrence_kernel(
   }
 }
 
+// -----------------------------------------------------------------------------------
+// Self-test of the bounded wait that every tensor-core kernel uses.  Thread 0 waits on
+// an mbarrier that nothing ever completes, with a short limit: the wait must give up,
+// raise the CTA's abort flag and record DELS_ERR_DEVICE_TIMEOUT.  Thread 32 (another
+// warp) waits on a second such barrier with the full limit and must leave as soon as
+// it sees the abort flag — the path the producer / MMA / epilogue roles take when one
+// of them times out.  Both report how long they waited.
+// -----------------------------------------------------------------------------------
+__global__ void wait_selftest_kernel(int* status, unsigned long long limit_ns, unsigned long long* waited_ns) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars[0]), 1);
+    mbar_init(smem_u32(&bars[1]), 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 || threadIdx.x == 32) {
+    const int which = threadIdx.x == 0 ? 0 : 1;
+    const unsigned long long t0 = globaltimer_ns();
+    const bool ok = mbar_wait(smem_u32(&bars[which]), 0u, &abort_flag, status,
+                              which == 0 ? limit_ns : kWaitLimitNs);
+    waited_ns[which] = ok ? 0ull : (globaltimer_ns() - t0);
+  }
+}
+
 }  // namespace dels

@@ -32,6 +32,8 @@ __global__ void rnn_recurrence_kernel(const float* __restrict__ pre, int splits,
                                       __nv_bfloat16* s_scaled, __nv_bfloat16* s_out, long long* keys,
                                       unsigned* counter);
 
+__global__ void wait_selftest_kernel(int* status, unsigned long long limit_ns, unsigned long long* waited_ns);
+
 inline size_t rnn_smem_bytes(int r) { return (size_t)(r / 2) * r * 4 + (size_t)kRnnSeqs * r * 4; }
 
 }  // namespace dels

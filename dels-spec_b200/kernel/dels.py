@@ -122,7 +122,7 @@ class DeLSGraphRunner:
 
         B, G, r, S = self.batch_size, self.gru_hidden_dim, self.rank_dim, self.steps
         self.static_prefix_ids = torch.zeros(B, 1, dtype=torch.long, device=device)
-        self.static_base_logits = torch.zeros(B, S, self.vocab_size, dtype=dtype, device=device)
+        self._alloc_step_inputs(dtype, device)
         self.static_out = torch.zeros(B, S, dtype=torch.long, device=device)
 
         self._alpha = torch.tensor(self.alpha_values, dtype=torch.float32, device=device)
@@ -156,16 +156,24 @@ class DeLSGraphRunner:
         for step in range(self.steps):
             ops.rank_gemv(h_cur, self.rank_weight, self._alpha[step : step + 1], self._s_scaled,
                           bias=self.rank_bias, activation=self._activation, keys=self._keys, ws=self._ws)
-            ops.fused_argmax_base_bf16(
-                self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight,
-                self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],
-                ws=self._ws,
-            )
+            self._score(step)
             if step + 1 < self.steps:
                 h_cur = ops.gru_step(self._tokens[step], self._gru_input_proj_table, self.gru_w_hh, h_cur,
                                      self._h[nxt], b_hh=self.gru_b_hh, ws=self._ws)
                 nxt ^= 1
         self.static_out.copy_(self._tokens.t())
+
+    # -- the per-step inputs and scorer; DeLSFusedGraphRunner swaps these two ----------
+    def _alloc_step_inputs(self, dtype, device):
+        self.static_base_logits = torch.zeros(self.batch_size, self.steps, self.vocab_size, dtype=dtype,
+                                              device=device)
+
+    def _score(self, step: int):
+        ops.fused_argmax_base_bf16(
+            self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight,
+            self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],
+            ws=self._ws,
+        )
 
     @torch.inference_mode()
     def __call__(
@@ -175,5 +183,49 @@ class DeLSGraphRunner:
     ) -> torch.Tensor:
         self.static_prefix_ids.copy_(prefix_ids)
         self.static_base_logits.copy_(base_logits)
+        self.graph.replay()
+        return self.static_out.clone()
+
+
+class DeLSFusedGraphRunner(DeLSGraphRunner):
+    """DeLS rollout that takes the DFlash draft hidden states instead of the long logits.
+
+    The reference materialises ``base_logits = target.lm_head(parallel_hiddens)``
+    ([B, 15, V], code/dflash.py:468) and copies positions 1..steps into the runner
+    (:482-485).  Here every step scores
+        h_t . W_lm + alpha_t * act(W_rank g_t) . Vr - beta_t * prior
+    inside the tensor-core scorer (``dels_fused_argmax_bf16``), so the long logits are
+    never written.  Each step streams the LM head once, so this pays off when B x (one
+    step's rows) is large enough for the scorer to be tensor-bound (a few hundred rows);
+    at batch 1 the materialising runner above is cheaper.
+
+    ``__call__(prefix_ids [B, 1], parallel_hiddens [B, steps, H])`` with the hidden
+    states of the same positions the reference feeds as base logits."""
+
+    def __init__(self, *, target_lm_head_weight: torch.Tensor, **kwargs):
+        w = target_lm_head_weight.detach()
+        if w.dim() != 2 or int(w.shape[0]) != int(kwargs["vocab_size"]):
+            raise ValueError(
+                f"target LM head weight {tuple(w.shape)} does not match vocab_size={kwargs['vocab_size']}."
+            )
+        self._lm_weight = w.to(device=kwargs["device"], dtype=torch.bfloat16).contiguous()
+        self.hidden_size = int(w.shape[1])
+        super().__init__(**kwargs)
+
+    def _alloc_step_inputs(self, dtype, device):
+        self.static_parallel_hiddens = torch.zeros(self.batch_size, self.steps, self.hidden_size, dtype=dtype,
+                                                   device=device)
+
+    def _score(self, step: int):
+        ops.fused_argmax_bf16(
+            self.static_parallel_hiddens[:, step, :], self._lm_weight, self._s_scaled, self.lm_head_weight,
+            self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],
+            ws=self._ws,
+        )
+
+    @torch.inference_mode()
+    def __call__(self, prefix_ids: torch.Tensor, parallel_hiddens: torch.Tensor) -> torch.Tensor:
+        self.static_prefix_ids.copy_(prefix_ids)
+        self.static_parallel_hiddens.copy_(parallel_hiddens)
         self.graph.replay()
         return self.static_out.clone()

@@ -152,6 +152,15 @@ DELS_API int dels_keys_init(int64_t* keys, int rows, void* ws, void* stream);
 DELS_API int dels_keys_decode(const int64_t* keys, int rows, const int32_t* rows_dev, int64_t* idx_out, float* score_out,
                      void* stream);
 
+/* Health check of the device-side bounded waits (no counterpart in the reference).
+ * Launches one CTA in which one thread waits on an mbarrier that nothing completes,
+ * giving up after limit_ms (0 < limit_ms <= 1000), and a second thread on another such
+ * barrier that must leave as soon as the first raises the CTA's abort flag.  Afterwards
+ * *status (device int, zero before the call) holds DELS_ERR_DEVICE_TIMEOUT and
+ * waited_ns[0..1] (device uint64) how long each waited.  No fault, trap or hang: the
+ * context stays usable. */
+DELS_API int dels_selftest_bounded_wait(int* status, uint64_t* waited_ns, double limit_ms, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Acceptance.  Replaces code/dflash.py:645-651
  *   accept = (verify_ids[:, 1:] == posterior[:, :-1]).cumprod(1).sum(1)

@@ -32,3 +32,35 @@ def score_rows(h, W, w_rank, Vr, prior, alpha_rows, beta_rows) -> torch.Tensor:
             logits = logits - key[1] * prior
         out[idx] = torch.argmax(logits, dim=-1)
     return out
+
+
+@torch.inference_mode()
+def runner_rollout(prefix_ids, base_logits, table, w_hh, w_rank, Vr, prior, alpha, beta) -> torch.Tensor:
+    """DeLSGraphRunner._forward_impl's torch path (code/kernel/dels.py:425-467 with the
+    fallback cell :368-373 and mix :447-456), on the host: GRU over the chosen tokens,
+    rank projection, base + alpha * low-rank - beta * prior, argmax, per step."""
+    B, steps, _ = base_logits.shape
+    G = w_hh.shape[1]
+    h = torch.zeros(B, G, dtype=base_logits.dtype)
+
+    def cell(gi, h):
+        gh = F.linear(h, w_hh)
+        i_r, i_z, i_n = gi.chunk(3, dim=-1)
+        h_r, h_z, h_n = gh.chunk(3, dim=-1)
+        r = torch.sigmoid(i_r + h_r)
+        z = torch.sigmoid(i_z + h_z)
+        n = torch.tanh(i_n + r * h_n)
+        return (1.0 - z) * n + z * h
+
+    h = cell(table[prefix_ids[:, 0]], h)
+    out = torch.empty(B, steps, dtype=torch.long)
+    for step in range(steps):
+        rank_state = F.linear(h, w_rank)
+        logits = base_logits[:, step, :] + alpha[step] * F.linear(rank_state, Vr)
+        if prior is not None and beta[step] != 0.0:
+            logits = logits - beta[step] * prior.view(1, -1)
+        tok = torch.argmax(logits, dim=-1)
+        out[:, step] = tok
+        if step + 1 < steps:
+            h = cell(table[tok], h)
+    return out

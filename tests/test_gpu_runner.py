@@ -146,3 +146,35 @@ def test_runner_full_vocab_b1(cuda_device):
     toks, gaps = O.dels_runner_rollout(prefix, base, embed=None, w_ih=None, w_hh=w["w_hh"], w_rank=w["w_rank"],
                                        Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta, bf16=True, table=table)
     assert _compare(out.cpu().numpy(), gaps, toks, 1e-2) >= 3
+
+
+def test_fused_long_logit_runner_matches_oracle(cuda_device):
+    """DeLSFusedGraphRunner: long logits computed inside the scorer from the hidden states."""
+    from kernel.dels import DeLSFusedGraphRunner
+
+    rng = np.random.default_rng(31)
+    V, E, G, r, H, B, steps = 3001, 32, 64, 32, 256, 3, 6
+    w = {
+        "embed": O.bf16_round((rng.standard_normal((V, E)) * 0.5).astype(np.float32)),
+        "w_ih": O.bf16_round((rng.standard_normal((3 * G, E)) * 0.2).astype(np.float32)),
+        "w_hh": O.bf16_round((rng.standard_normal((3 * G, G)) * 0.2).astype(np.float32)),
+        "w_rank": O.bf16_round((rng.standard_normal((r, G)) * 0.3).astype(np.float32)),
+        "Vr": O.bf16_round((rng.standard_normal((V, r)) * 0.3).astype(np.float32)),
+    }
+    W = O.bf16_round((rng.standard_normal((V, H)) * 0.06).astype(np.float32))
+    hid = O.bf16_round(rng.standard_normal((B, steps, H)).astype(np.float32))
+    head = _head(cuda_device, V, E, G, r, "silu", w)
+    prior = O.bf16_round(O.zipf_log_prior(V).astype(np.float32))
+    alpha = list(np.linspace(0.9, 0.4, steps))
+    beta = list(np.linspace(0.1, 0.3, steps))
+    runner = DeLSFusedGraphRunner(local_head=head, target_lm_head_weight=torch.from_numpy(W).to(cuda_device),
+                                  batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha, beta_values=beta,
+                                  baseline_logits=torch.from_numpy(prior).to(cuda_device), device=cuda_device)
+    prefix = np.array([[5], [77], [2999]])
+    out = runner(torch.from_numpy(prefix).to(cuda_device),
+                 torch.from_numpy(hid).to(cuda_device).to(torch.bfloat16)).cpu().numpy()
+    base = np.einsum("bsh,vh->bsv", hid.astype(np.float64), W.astype(np.float64))  # exact, never rounded
+    toks, gaps = O.dels_runner_rollout(prefix, base, embed=w["embed"], w_ih=w["w_ih"], w_hh=w["w_hh"],
+                                       w_rank=w["w_rank"], Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta,
+                                       activation="silu", bf16=True)
+    assert _compare(out, gaps, toks, 1e-2) >= 3
