@@ -15,6 +15,7 @@
 #include "small_kernels.cuh"
 #include "tc_gemm.cuh"
 #include "tc_scorer_pair.cuh"
+#include "tc_skinny.cuh"
 
 using namespace dels;
 
@@ -31,6 +32,10 @@ constexpr int kScorerTailSplit = 4;
 // Paired scorer enabled (DELS_SCORER_PAIRS=0 in the environment selects the
 // single-CTA scorer for every shape, e.g. to compare the two).
 bool g_use_pairs = true;
+// Skinny (rows as the MMA's N side) scorer for calls of at most kSkinnyMaxRows rows
+// (DELS_SCORER_SKINNY=0 in the environment selects the 128-row tile kernel instead).
+bool g_use_skinny = true;
+constexpr int kSkinnyMaxRows = 32;
 
 thread_local std::string g_last_error;
 
@@ -134,6 +139,7 @@ int init_device(int dev) {
   std::lock_guard<std::mutex> lock(g_dev_mu);
   if (g_dev[dev].ready) return DELS_OK;
   if (const char* env = getenv("DELS_SCORER_PAIRS")) g_use_pairs = env[0] != '0';
+  if (const char* env = getenv("DELS_SCORER_SKINNY")) g_use_skinny = env[0] != '0';
   int prev = -1;
   cudaError_t e = cudaGetDevice(&prev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -149,7 +155,7 @@ int init_device(int dev) {
 #define SET(k, b)                                            \
   if (rc == DELS_OK && (e = set_smem(k, b)) != cudaSuccess) rc = cuda_fail(e, "kernel setup: " #k);
     SET((tc_gemm_kernel<256, kArgmax, false>), TcConfig<256>::kSmemBytes);
-    SET((tc_gemm_kernel<256, kArgmax, true>), TcConfig<256>::kSmemBytes);
+    SET((tc_gemm_kernel<256, kArgmax, true>), (TcConfig<256, true>::kSmemBytes));
     SET((tc_gemm_kernel<256, kStore, false>), TcConfig<256>::kSmemBytes);
     SET((tc_gemm_kernel<128, kStore, false>), TcConfig<128>::kSmemBytes);
     SET((tc_gemm_kernel<64, kStore, false>), TcConfig<64>::kSmemBytes);
@@ -157,6 +163,8 @@ int init_device(int dev) {
     if (rc == DELS_OK && (e = f32_score_setup(kMaxSmem)) != cudaSuccess) rc = cuda_fail(e, "kernel setup: f32_score");
     SET((tc_scorer_pair_kernel<false>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<true>), PairConfig::kSmemBytes);
+    SET((tc_skinny_kernel<16>), SkinnyConfig<16>::kSmemBytes);
+    SET((tc_skinny_kernel<32>), SkinnyConfig<32>::kSmemBytes);
     SET(rnn_recurrence_kernel, kMaxSmem);
     SET(rank_finalize_kernel, 0);
     SET(keys_init_kernel, 0);
@@ -277,9 +285,41 @@ int launch_tc(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) 
   const long long want = tiles < sm_count ? tiles * (args.tail_split > 1 ? args.tail_split : 1) : tiles;
   const int grid = (int)(want < sm_count ? want : sm_count);
   if (grid <= 0) return DELS_OK;
-  tc_gemm_kernel<BN, MODE, VB><<<grid, kTcThreads, TcConfig<BN>::kSmemBytes, st>>>(ma0, mb0, ma1, mb1, mb0t, mb1t,
-                                                                                   args);
+  constexpr int smem = TcConfig<BN, VB && MODE == kArgmax>::kSmemBytes;
+  tc_gemm_kernel<BN, MODE, VB><<<grid, kTcThreads, smem, st>>>(ma0, mb0, ma1, mb1, mb0t, mb1t, args);
   DELS_CHECK_LAUNCH("tc_gemm_kernel launch");
+  return DELS_OK;
+}
+
+// The skinny scorer: weight maps (W, Vr) in 64 x 128 boxes as the MMA's A operand, row
+// maps (h, s) in 64 x NB boxes as its B operand; one persistent CTA per SM.
+template <int NB>
+int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) {
+  int rc = ensure_encode();
+  if (rc != DELS_OK) return rc;
+  CUtensorMap wa0, rb0, wa1, rb1;
+  if (op.K1 > 0) {
+    if ((rc = make_map_bf16(&wa1, op.b1, op.K1, op.n_extent, op.ldb1, kSkinnyBM)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&rb1, op.a1, op.K1, op.m_extent, op.lda1, NB)) != DELS_OK) return rc;
+  }
+  if (op.K0 > 0) {
+    if ((rc = make_map_bf16(&wa0, op.b0, op.K0, op.n_extent, op.ldb0, kSkinnyBM)) != DELS_OK) return rc;
+    if ((rc = make_map_bf16(&rb0, op.a0, op.K0, op.m_extent, op.lda0, NB)) != DELS_OK) return rc;
+  } else {
+    wa0 = wa1;
+    rb0 = rb1;
+  }
+  if (op.K1 == 0) {
+    wa1 = wa0;
+    rb1 = rb0;
+  }
+  args.kb0 = cdiv(op.K0, kBK);
+  args.kb1 = cdiv(op.K1, kBK);
+  const int tiles = cdiv(op.n_extent, kSkinnyBM);
+  const int grid = tiles < sm_count ? tiles : sm_count;
+  if (grid <= 0) return DELS_OK;
+  tc_skinny_kernel<NB><<<grid, kTcThreads, SkinnyConfig<NB>::kSmemBytes, st>>>(wa0, rb0, wa1, rb1, args);
+  DELS_CHECK_LAUNCH("tc_skinny_kernel launch");
   return DELS_OK;
 }
 
@@ -469,6 +509,11 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
   a.idx_out = reinterpret_cast<long long*>(idx_out);
   a.score_out = score_out;
   a.counter = hdr.counter;
+  if (rows <= kSkinnyMaxRows && g_use_skinny) {
+    // Decode-shaped call: the vocab tile is the MMA's M side, the rows its N side.
+    if (rows <= 16) return launch_skinny<16>(op, a, ds->sm_count, st);
+    return launch_skinny<32>(op, a, ds->sm_count, st);
+  }
   const bool vec_base = base != nullptr && aligned16(base) && (ld_base % 8) == 0;
   if (rows > kBM && ds->max_pairs > 0 && g_use_pairs) {
     // More than one 128-row tile: CTA pairs share each LM-head tile across two SMs.
@@ -826,7 +871,7 @@ int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi
   int rc;
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;
-  gru_step_kernel<<<cdiv(G, kGruCols), 256, gru_smem_bytes(G), reinterpret_cast<cudaStream_t>(stream)>>>(
+  gru_step_kernel<<<cdiv(G, kGruCols), kGruThreads, gru_smem_bytes(G), reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const long long*>(tokens), tok_stride, reinterpret_cast<const __nv_bfloat16*>(gi_table),
       ld_table, reinterpret_cast<const __nv_bfloat16*>(w_hh), reinterpret_cast<const __nv_bfloat16*>(b_hh),
       reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V, status);
@@ -850,8 +895,8 @@ int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w
   DeviceState* ds = nullptr;
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;
-  const int grid = cdiv(r, 4) < ds->sm_count ? cdiv(r, 4) : ds->sm_count;
-  rank_gemv_kernel<<<grid, 128, rank_gemv_smem_bytes(K), reinterpret_cast<cudaStream_t>(stream)>>>(
+  const int grid = cdiv(r, kGemvThreads / 32) < 2 * ds->sm_count ? cdiv(r, kGemvThreads / 32) : 2 * ds->sm_count;
+  rank_gemv_kernel<<<grid, kGemvThreads, rank_gemv_smem_bytes(K), reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), ld_x, reinterpret_cast<const __nv_bfloat16*>(w), ld_w,
       reinterpret_cast<const __nv_bfloat16*>(bias), B, K, r, activation, alpha, n_pos, row_pos,
       reinterpret_cast<__nv_bfloat16*>(s_out), reinterpret_cast<__nv_bfloat16*>(s_scaled),

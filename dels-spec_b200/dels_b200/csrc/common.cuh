@@ -78,6 +78,34 @@ __device__ __forceinline__ bool scan_takes(float s, float best) {
   return (s > best) || ((s != s) && (best == best));
 }
 
+// ordered_i32 without branches, for the scoring epilogues: x + 0 turns -0 into +0 and
+// leaves every other value (NaN included) as it is.
+__device__ __forceinline__ int32_t ordered_i32_dev(float f) {
+  const int32_t i = __float_as_int(__fadd_rn(f, 0.0f));
+  const int32_t o = i ^ ((i >> 31) & 0x7FFFFFFF);
+  return f != f ? 0x7FFFFFFF : o;
+}
+
+// Packed key (pack_key order) of the best of sc[0..valid) with global indices idx0 + j:
+// a 5-level tree of 64-bit maxima, branch-free, so its latency is a few dependent
+// steps rather than one compare-and-select per column.  Entries past `valid` do not
+// take part.
+__device__ __forceinline__ long long chunk_best_key(const float (&sc)[32], int valid, uint32_t idx0) {
+  long long k[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const long long key = (long long)(((unsigned long long)(uint32_t)ordered_i32_dev(sc[j]) << 32) |
+                                      (unsigned long long)(0xFFFFFFFFu - (idx0 + (uint32_t)j)));
+    k[j] = j < valid ? key : kKeyEmpty;
+  }
+#pragma unroll
+  for (int w = 1; w < 32; w *= 2) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2 * w) k[j] = k[j + w] > k[j] ? k[j + w] : k[j];
+  }
+  return k[0];
+}
+
 // Row position (the draft-block slot that selects alpha_p / beta_p).
 __device__ __forceinline__ int row_position(const int* row_pos, int row, int n_pos) {
   return row_pos != nullptr ? row_pos[row] : (row % n_pos);
@@ -166,6 +194,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 // --------------------------------------------------------------------------------
+// Per-thread asynchronous 16-byte copies global -> shared (the epilogue's operand
+// prefetch).  src_bytes < 16 zero-fills the rest of the 16 bytes without reading past
+// src + src_bytes.
+// --------------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// --------------------------------------------------------------------------------
 // tcgen05: tensor memory, MMA, commit, loads
 // --------------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
@@ -249,10 +289,23 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&v)[32]
 
 // Wait for this thread's outstanding tcgen05.ld, then pin the loaded registers after
 // the wait so that no consumer is scheduled ahead of it.
-__device__ __forceinline__ void tmem_ld_wait(uint32_t (&v)[32]) {
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&v)[N]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(v[i]));
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(v[i]));
+}
+
+// 16 consecutive fp32 columns of this warp's 32 lanes (lane i of the warp <-> TMEM lane
+// base + i).
+__device__ __forceinline__ void tmem_ld_16cols(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
 }
 
 // --------------------------------------------------------------------------------

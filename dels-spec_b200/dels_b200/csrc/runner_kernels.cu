@@ -21,32 +21,70 @@ namespace dels {
 
 namespace {
 
-// dot products of one weight row (bf16, length K) with `nb` bf16 rows staged in shared
-// memory (row stride ldx elements); the full sums end up in every lane.
+// One weight row, lane l holding elements 8l..8l+7 of each 256-element chunk.  The
+// first kRowPre chunks are loaded into registers ahead of time (before the input rows
+// are staged), so a warp has its whole row in flight at once instead of one 16-byte
+// load per lane per round trip.
+constexpr int kRowPre = 4;
+
+struct RowPrefetch {
+  uint4 w[kRowPre];
+};
+
+__device__ __forceinline__ void row_prefetch(const __nv_bfloat16* __restrict__ wrow, int K, int lane,
+                                             RowPrefetch& p) {
+#pragma unroll
+  for (int i = 0; i < kRowPre; ++i) {
+    const int k = lane * 8 + i * 256;
+    p.w[i] = k < K ? __ldg(reinterpret_cast<const uint4*>(wrow + k)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// acc[b] += w[k..k+7] . xs[b][k..k+7] for the nb staged rows
 template <int MAXB>
-__device__ __forceinline__ void warp_row_dots(const __nv_bfloat16* __restrict__ wrow, const __nv_bfloat16* xs,
-                                              int ldx, int nb, int K, int lane, float (&acc)[MAXB]) {
+__device__ __forceinline__ void dot_chunk(const uint4 w, const __nv_bfloat16* xs, int ldx, int nb, int k,
+                                          float (&acc)[MAXB]) {
+  const float w0 = bf16_lo(w.x), w1 = bf16_hi(w.x), w2 = bf16_lo(w.y), w3 = bf16_hi(w.y);
+  const float w4 = bf16_lo(w.z), w5 = bf16_hi(w.z), w6 = bf16_lo(w.w), w7 = bf16_hi(w.w);
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) {
+    if (b < nb) {
+      const uint4 x = *reinterpret_cast<const uint4*>(xs + b * ldx + k);
+      float a = acc[b];
+      a = fmaf(w0, bf16_lo(x.x), a);
+      a = fmaf(w1, bf16_hi(x.x), a);
+      a = fmaf(w2, bf16_lo(x.y), a);
+      a = fmaf(w3, bf16_hi(x.y), a);
+      a = fmaf(w4, bf16_lo(x.z), a);
+      a = fmaf(w5, bf16_hi(x.z), a);
+      a = fmaf(w6, bf16_lo(x.w), a);
+      a = fmaf(w7, bf16_hi(x.w), a);
+      acc[b] = a;
+    }
+  }
+}
+
+// dot products of one weight row (bf16, length K, first chunks already in `pre`) with
+// `nb` bf16 rows staged in shared memory (row stride ldx elements); the full sums end
+// up in every lane.  Chunks past the prefetched ones stream in batches of kRowPre.
+template <int MAXB>
+__device__ __forceinline__ void warp_row_dots(const RowPrefetch& pre, const __nv_bfloat16* __restrict__ wrow,
+                                              const __nv_bfloat16* xs, int ldx, int nb, int K, int lane,
+                                              float (&acc)[MAXB]) {
 #pragma unroll
   for (int b = 0; b < MAXB; ++b) acc[b] = 0.0f;
-  for (int k = lane * 8; k < K; k += 256) {
-    const uint4 w = __ldg(reinterpret_cast<const uint4*>(wrow + k));
-    const float w0 = bf16_lo(w.x), w1 = bf16_hi(w.x), w2 = bf16_lo(w.y), w3 = bf16_hi(w.y);
-    const float w4 = bf16_lo(w.z), w5 = bf16_hi(w.z), w6 = bf16_lo(w.w), w7 = bf16_hi(w.w);
 #pragma unroll
-    for (int b = 0; b < MAXB; ++b) {
-      if (b < nb) {
-        const uint4 x = *reinterpret_cast<const uint4*>(xs + b * ldx + k);
-        float a = acc[b];
-        a = fmaf(w0, bf16_lo(x.x), a);
-        a = fmaf(w1, bf16_hi(x.x), a);
-        a = fmaf(w2, bf16_lo(x.y), a);
-        a = fmaf(w3, bf16_hi(x.y), a);
-        a = fmaf(w4, bf16_lo(x.z), a);
-        a = fmaf(w5, bf16_hi(x.z), a);
-        a = fmaf(w6, bf16_lo(x.w), a);
-        a = fmaf(w7, bf16_hi(x.w), a);
-        acc[b] = a;
-      }
+  for (int i = 0; i < kRowPre; ++i) {
+    const int k = lane * 8 + i * 256;
+    if (k < K) dot_chunk<MAXB>(pre.w[i], xs, ldx, nb, k, acc);
+  }
+  for (int k0 = kRowPre * 256; k0 < K; k0 += kRowPre * 256) {
+    RowPrefetch more;
+    row_prefetch(wrow + k0, K - k0, lane, more);
+#pragma unroll
+    for (int i = 0; i < kRowPre; ++i) {
+      const int k = k0 + lane * 8 + i * 256;
+      if (k < K) dot_chunk<MAXB>(more.w[i], xs, ldx, nb, k, acc);
     }
   }
 #pragma unroll
@@ -64,19 +102,28 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf
 
 }  // namespace
 
-// One CTA per kGruCols hidden units; B rows in chunks of kRunnerMaxB.
-__global__ void __launch_bounds__(256) gru_step_kernel(const long long* __restrict__ tokens, long long tok_stride,
-                                                       const __nv_bfloat16* __restrict__ table, long long ld_table,
-                                                       const __nv_bfloat16* __restrict__ w_hh,
-                                                       const __nv_bfloat16* __restrict__ b_hh,
-                                                       const __nv_bfloat16* h_in, __nv_bfloat16* h_out, int B, int G,
-                                                       int V, int* status) {
+// One CTA per kGruCols hidden units, one warp per gate row of those units (the CTA has
+// 3 * kGruCols warps); B rows in chunks of kRunnerMaxB.  Each warp loads its W_hh row
+// before h is staged, so the weight stream and the h gather overlap.
+__global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long long* __restrict__ tokens,
+                                                               long long tok_stride,
+                                                               const __nv_bfloat16* __restrict__ table,
+                                                               long long ld_table,
+                                                               const __nv_bfloat16* __restrict__ w_hh,
+                                                               const __nv_bfloat16* __restrict__ b_hh,
+                                                               const __nv_bfloat16* h_in, __nv_bfloat16* h_out, int B,
+                                                               int G, int V, int* status) {
   extern __shared__ uint4 smem4[];
   __nv_bfloat16* hs = reinterpret_cast<__nv_bfloat16*>(smem4);     // [kRunnerMaxB][G]
   float* gh_s = reinterpret_cast<float*>(hs + (size_t)kRunnerMaxB * G);  // [3][kGruCols][kRunnerMaxB]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
   const int g0 = blockIdx.x * kGruCols;
+  // this warp's gate row: gate = warp / kGruCols, unit g0 + warp % kGruCols
+  const int gate = warp / kGruCols, c_w = warp % kGruCols;
+  const bool has_row = gate < 3 && g0 + c_w < G;
+  const __nv_bfloat16* wrow = w_hh + (long long)(gate * G + g0 + c_w) * G;
+  RowPrefetch pre;
+  if (has_row) row_prefetch(wrow, G, lane, pre);
   for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
     const int nb = min(kRunnerMaxB, B - b0);
     __syncthreads();
@@ -88,17 +135,14 @@ __global__ void __launch_bounds__(256) gru_step_kernel(const long long* __restri
       reinterpret_cast<uint4*>(hs + (size_t)b * G)[k8] = v;
     }
     __syncthreads();
-    // gh for the gate rows {g, G + g, 2G + g} of this CTA's columns
-    for (int rr = warp; rr < 3 * kGruCols; rr += nwarps) {
-      const int gate = rr / kGruCols, c = rr % kGruCols;
-      const int g = g0 + c;
+    // gh for the gate row {g, G + g, 2G + g} this warp owns
+    if (has_row) {
       float acc[kRunnerMaxB];
-      if (g < G) {
-        warp_row_dots<kRunnerMaxB>(w_hh + (long long)(gate * G + g) * G, hs, G, nb, G, lane, acc);
-        if (lane == 0) {
-          const float bias = b_hh != nullptr ? __bfloat162float(b_hh[gate * G + g]) : 0.0f;
-          for (int b = 0; b < nb; ++b) gh_s[(gate * kGruCols + c) * kRunnerMaxB + b] = bf16r(acc[b] + bias);
-        }
+      warp_row_dots<kRunnerMaxB>(pre, wrow, hs, G, nb, G, lane, acc);
+      if (lane == 0) {
+        const int g = g0 + c_w;
+        const float bias = b_hh != nullptr ? __bfloat162float(b_hh[gate * G + g]) : 0.0f;
+        for (int b = 0; b < nb; ++b) gh_s[(gate * kGruCols + c_w) * kRunnerMaxB + b] = bf16r(acc[b] + bias);
       }
     }
     __syncthreads();
@@ -127,18 +171,20 @@ __global__ void __launch_bounds__(256) gru_step_kernel(const long long* __restri
   }
 }
 
-// One warp per output feature j (grid-stride), all B rows at once.
-__global__ void __launch_bounds__(256) rank_gemv_kernel(const __nv_bfloat16* __restrict__ x, long long ld_x,
-                                                        const __nv_bfloat16* __restrict__ w, long long ld_w,
-                                                        const __nv_bfloat16* __restrict__ bias, int B, int K, int r,
-                                                        int activation, const float* __restrict__ alpha, int n_pos,
-                                                        const int* __restrict__ row_pos, __nv_bfloat16* s_out,
-                                                        __nv_bfloat16* s_scaled, long long* keys, unsigned* counter) {
+// One warp per output feature j (grid-stride), all B rows at once.  The warp's first
+// weight row is loaded before x is staged.
+__global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ld_x, const __nv_bfloat16* __restrict__ w, long long ld_w,
+    const __nv_bfloat16* __restrict__ bias, int B, int K, int r, int activation, const float* __restrict__ alpha,
+    int n_pos, const int* __restrict__ row_pos, __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys,
+    unsigned* counter) {
   extern __shared__ uint4 smem4[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);  // [kRunnerMaxB][K]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
   const int nwarps = gridDim.x * (blockDim.x >> 5);
+  RowPrefetch first;
+  if (gwarp < r) row_prefetch(w + (long long)gwarp * ld_w, K, lane, first);
   for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
     const int nb = min(kRunnerMaxB, B - b0);
     __syncthreads();
@@ -149,8 +195,15 @@ __global__ void __launch_bounds__(256) rank_gemv_kernel(const __nv_bfloat16* __r
     }
     __syncthreads();
     for (int j = gwarp; j < r; j += nwarps) {
+      const __nv_bfloat16* wrow = w + (long long)j * ld_w;
+      RowPrefetch pre;
+      if (j == gwarp) {
+        pre = first;
+      } else {
+        row_prefetch(wrow, K, lane, pre);
+      }
       float acc[kRunnerMaxB];
-      warp_row_dots<kRunnerMaxB>(w + (long long)j * ld_w, xs, K, nb, K, lane, acc);
+      warp_row_dots<kRunnerMaxB>(pre, wrow, xs, K, nb, K, lane, acc);
       if (lane < nb) {
         float a = 0.0f;
 #pragma unroll

@@ -6,7 +6,9 @@
 namespace dels {
 
 constexpr int kRunnerMaxB = 16;  // rows staged in shared memory per pass
-constexpr int kGruCols = 16;     // hidden units per CTA in the GRU step
+constexpr int kGruCols = 4;      // hidden units per CTA in the GRU step
+constexpr int kGruThreads = 3 * kGruCols * 32;  // one warp per gate row of the CTA's units
+constexpr int kGemvThreads = 128;
 
 inline size_t gru_smem_bytes(int G) {
   return (size_t)kRunnerMaxB * G * 2 + (size_t)3 * kGruCols * kRunnerMaxB * 4;

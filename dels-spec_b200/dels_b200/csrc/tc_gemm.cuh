@@ -67,16 +67,27 @@ struct TcArgs {
   long long split_stride;
 };
 
-template <int BN>
+// STAGED: the argmax epilogue with base logits prefetches each tile's base rows and
+// prior slice into shared memory (one region per epilogue warp) before it waits for
+// the accumulator, so their load latency overlaps the tile's MMAs instead of being
+// paid once per 32-column chunk.  It gives up one operand stage for the room.
+template <int BN, bool STAGED = false>
 struct TcConfig {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int kStages = STAGED ? 3 : ((BN >= 256) ? 4 : (BN >= 128 ? 6 : 8));
   static constexpr int kAccCols = 2 * BN;
   static constexpr int kTmemCols =
       kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
-  static constexpr int kBarOffset = kStages * kStageBytes;
+  // per epilogue warp: 32 rows of BN bf16, each padded by 16 bytes so that the
+  // lane-per-row 16-byte reads of a quarter warp hit distinct banks, and BN fp32 prior
+  static constexpr int kBaseLd = BN + 8;
+  static constexpr int kBaseWarpBytes = 32 * kBaseLd * 2;
+  static constexpr int kPriorWarpBytes = BN * 4;
+  static constexpr int kEpiOffset = kStages * kStageBytes;
+  static constexpr int kEpiBytes = STAGED ? 4 * (kBaseWarpBytes + kPriorWarpBytes) : 0;
+  static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
@@ -159,7 +170,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
                    const __grid_constant__ CUtensorMap map_b0t, const __grid_constant__ CUtensorMap map_b1t,
                    const TcArgs args) {
-  using Cfg = TcConfig<BN>;
+  constexpr bool STAGED = VEC_BASE && MODE == kArgmax;
+  using Cfg = TcConfig<BN, STAGED>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
 
@@ -340,6 +352,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
+    // STAGED: this warp's base rows and prior slice in shared memory
+    const int epi_slot = warp - 2;
+    uint8_t* base_s = smem + Cfg::kEpiOffset + epi_slot * (Cfg::kBaseWarpBytes + Cfg::kPriorWarpBytes);
+    const float* prior_s = reinterpret_cast<const float*>(base_s + Cfg::kBaseWarpBytes);
     for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
       const WorkUnit wu = work_unit<BN>(u, sched);
       const TileCoord tc = wu.c;
@@ -348,7 +364,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int n0 = wu.n0;
       const int ncols = min(wu.bn, args.n_cols - n0);
       const int nchunks = wu.bn / 32;
-      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status)) break;
+      // A warp whose 32 rows are all past the end skips the tile (warp-uniform, so the
+      // collective tensor-memory loads stay aligned); lanes past the end skip the arithmetic.
+      const int warp_row0 = tc.m_tile * kBM + quad * 32;
+      const bool warp_rows = warp_row0 < m_rows;
+      if constexpr (STAGED) {
+        if (warp_rows) {
+          // Row by row, each row's slice one coalesced warp-wide copy (lane l takes
+          // elements 8l..8l+7 of every 256); the partial last 16 bytes are zero-filled.
+          __syncwarp();  // every lane has finished reading the previous tile's copy
+          const uint32_t dst0 = smem_u32(base_s);
+          const int nr = min(32, m_rows - warp_row0);
+          for (int rr = 0; rr < nr; ++rr) {
+            const __nv_bfloat16* src = args.base + (long long)(warp_row0 + rr) * args.ld_base + n0;
+            for (int e = lane * 8; e < ncols; e += 256)
+              cp_async_16(dst0 + (uint32_t)((rr * Cfg::kBaseLd + e) * 2), src + e, (uint32_t)min(16, (ncols - e) * 2));
+          }
+          if (args.prior != nullptr) {
+            const uint32_t pdst = smem_u32(prior_s);
+            for (int e = lane * 4; e < ncols; e += 128)
+              cp_async_16(pdst + (uint32_t)(e * 4), args.prior + n0 + e, (uint32_t)min(16, (ncols - e) * 4));
+          }
+          cp_async_commit();
+        }
+      }
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status)) {
+        if constexpr (STAGED) cp_async_wait_all();
+        break;
+      }
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 
@@ -359,68 +402,93 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const __nv_bfloat16* brow =
             (args.base != nullptr && row_ok) ? args.base + (long long)row * args.ld_base + n0 : nullptr;
         const float* prow = args.prior != nullptr ? args.prior + n0 : nullptr;
-        float best = -INFINITY;
-        int best_c = 0;
+        const __nv_bfloat16* brow_s = reinterpret_cast<const __nv_bfloat16*>(base_s) + lane * Cfg::kBaseLd;
+        if constexpr (STAGED) {
+          cp_async_wait_all();
+          __syncwarp();
+        }
+        long long best_key = kKeyEmpty;
 #pragma unroll 1
-        for (int c = 0; c < nchunks; ++c) {
+        for (int c = 0; c < (warp_rows ? nchunks : 0); ++c) {
           uint32_t v[32];
           tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
           tmem_ld_wait(v);
           const int c0 = c * 32;
-          if (c0 < ncols) {
+          if (row_ok && c0 < ncols) {
             float sc[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(v[j]);
             const bool full_chunk = (c0 + 32 <= ncols);
-            if (brow != nullptr) {
-              if (VEC_BASE && full_chunk) {
+            if constexpr (STAGED) {
+              // staged operands; columns past ncols hold stale data and are masked in the scan
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const uint4 w = __ldg(reinterpret_cast<const uint4*>(brow + c0) + q);
-                  sc[8 * q + 0] += bf16_lo(w.x);
-                  sc[8 * q + 1] += bf16_hi(w.x);
-                  sc[8 * q + 2] += bf16_lo(w.y);
-                  sc[8 * q + 3] += bf16_hi(w.y);
-                  sc[8 * q + 4] += bf16_lo(w.z);
-                  sc[8 * q + 5] += bf16_hi(w.z);
-                  sc[8 * q + 6] += bf16_lo(w.w);
-                  sc[8 * q + 7] += bf16_hi(w.w);
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (c0 + j < ncols) sc[j] += __bfloat162float(brow[c0 + j]);
+              for (int q = 0; q < 4; ++q) {
+                const uint4 w = reinterpret_cast<const uint4*>(brow_s + c0)[q];
+                sc[8 * q + 0] += bf16_lo(w.x);
+                sc[8 * q + 1] += bf16_hi(w.x);
+                sc[8 * q + 2] += bf16_lo(w.y);
+                sc[8 * q + 3] += bf16_hi(w.y);
+                sc[8 * q + 4] += bf16_lo(w.z);
+                sc[8 * q + 5] += bf16_hi(w.z);
+                sc[8 * q + 6] += bf16_lo(w.w);
+                sc[8 * q + 7] += bf16_hi(w.w);
               }
-            }
-            if (prow != nullptr) {
-              if (full_chunk) {
+              if (prow != nullptr) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                  const float4 p = __ldg(reinterpret_cast<const float4*>(prow + c0) + q);
+                  const float4 p = reinterpret_cast<const float4*>(prior_s + c0)[q];
                   sc[4 * q + 0] = fmaf(negb, p.x, sc[4 * q + 0]);
                   sc[4 * q + 1] = fmaf(negb, p.y, sc[4 * q + 1]);
                   sc[4 * q + 2] = fmaf(negb, p.z, sc[4 * q + 2]);
                   sc[4 * q + 3] = fmaf(negb, p.w, sc[4 * q + 3]);
                 }
-              } else {
+              }
+            } else {
+              if (brow != nullptr) {
+                if (VEC_BASE && full_chunk) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (c0 + j < ncols) sc[j] = fmaf(negb, __ldg(prow + c0 + j), sc[j]);
+                  for (int q = 0; q < 4; ++q) {
+                    const uint4 w = __ldg(reinterpret_cast<const uint4*>(brow + c0) + q);
+                    sc[8 * q + 0] += bf16_lo(w.x);
+                    sc[8 * q + 1] += bf16_hi(w.x);
+                    sc[8 * q + 2] += bf16_lo(w.y);
+                    sc[8 * q + 3] += bf16_hi(w.y);
+                    sc[8 * q + 4] += bf16_lo(w.z);
+                    sc[8 * q + 5] += bf16_hi(w.z);
+                    sc[8 * q + 6] += bf16_lo(w.w);
+                    sc[8 * q + 7] += bf16_hi(w.w);
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (c0 + j < ncols) sc[j] += __bfloat162float(brow[c0 + j]);
+                }
+              }
+              if (prow != nullptr) {
+                if (full_chunk) {
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) {
+                    const float4 p = __ldg(reinterpret_cast<const float4*>(prow + c0) + q);
+                    sc[4 * q + 0] = fmaf(negb, p.x, sc[4 * q + 0]);
+                    sc[4 * q + 1] = fmaf(negb, p.y, sc[4 * q + 1]);
+                    sc[4 * q + 2] = fmaf(negb, p.z, sc[4 * q + 2]);
+                    sc[4 * q + 3] = fmaf(negb, p.w, sc[4 * q + 3]);
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (c0 + j < ncols) sc[j] = fmaf(negb, __ldg(prow + c0 + j), sc[j]);
+                }
               }
             }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (c0 + j < ncols && scan_takes(sc[j], best)) {
-                best = sc[j];
-                best_c = c0 + j;
-              }
-            }
+            const long long ck = chunk_best_key(sc, ncols - c0, (uint32_t)(args.v_begin + n0 + c0));
+            best_key = ck > best_key ? ck : best_key;
           }
         }
         tc_fence_before();
         mbar_arrive(tempty_bar(acc));
         if (row_ok) {
-          atomicMax(&args.keys[row], pack_key(best, (uint32_t)(args.v_begin + n0 + best_c)));
+          atomicMax(&args.keys[row], best_key);
           __threadfence();
         }
       } else {

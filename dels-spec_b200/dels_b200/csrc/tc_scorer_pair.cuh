@@ -249,15 +249,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       const __nv_bfloat16* brow =
           (args.base != nullptr && row_ok) ? args.base + (long long)row * args.ld_base + n0 : nullptr;
       const float* prow = args.prior != nullptr ? args.prior + n0 : nullptr;
-      float best = -INFINITY;
-      int best_c = 0;
+      long long best_key = kKeyEmpty;
+      // A warp whose 32 rows are all past the end skips the tile (warp-uniform, so the
+      // collective tensor-memory loads stay aligned); lanes past the end skip the
+      // arithmetic.
+      const bool warp_rows = (wu.c.m_tile * 2 * kBM + (int)rank * kBM + quad * 32) < m_rows;
 #pragma unroll 1
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = 0; c < (warp_rows ? nchunks : 0); ++c) {
         uint32_t v[32];
         tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
         tmem_ld_wait(v);
         const int c0 = c * 32;
-        if (c0 < ncols) {
+        if (row_ok && c0 < ncols) {
           float sc[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(v[j]);
@@ -298,13 +301,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                 if (c0 + j < ncols) sc[j] = fmaf(negb, __ldg(prow + c0 + j), sc[j]);
             }
           }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (c0 + j < ncols && scan_takes(sc[j], best)) {
-              best = sc[j];
-              best_c = c0 + j;
-            }
-          }
+          const long long ck = chunk_best_key(sc, ncols - c0, (uint32_t)(args.v_begin + n0 + c0));
+          best_key = ck > best_key ? ck : best_key;
         }
       }
       tc_fence_before();
@@ -316,7 +314,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           mbar_arrive_remote(acc == 0 ? tempty_leader0 : tempty_leader1);
       }
       if (row_ok) {
-        atomicMax(&args.keys[row], pack_key(best, (uint32_t)(args.v_begin + n0 + best_c)));
+        atomicMax(&args.keys[row], best_key);
         __threadfence();
       }
       if (++acc == 2) {

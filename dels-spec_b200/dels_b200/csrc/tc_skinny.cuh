@@ -1,0 +1,317 @@
+// Skinny draft scorer for decode-shaped calls (a few rows: the graph runners score one
+// position of B sequences per step), sm_100a.
+//
+//   score[row, v] = (sum_k h[row, k] W[v, k]) + (sum_j s'[row, j] Vr[v, j])
+//                   (+ base[row, v]) - beta_p * prior[v]          s' = alpha_p * s
+//   token[row]    = argmax_v score[row, v]   (lowest index on ties)
+//
+// Same contraction and epilogue arithmetic as tc_gemm_kernel<kArgmax>, with the operand
+// roles swapped: the vocab tile is the MMA's M side (128 TMEM lanes, one vocab row per
+// epilogue thread) and the rows are its N side (NB = 16 or 32 columns).  Per K block
+// a stage then holds 16 KB of the streamed weight and only NB x 128 B of rows, so eight
+// stages keep ~150 KB of the weight in flight per SM, and every epilogue thread has
+// work: it adds its vocab row's base logits and prior, packs (score, index) keys and
+// keeps a running maximum per row in registers across all the tiles its CTA scores.
+// The maxima meet once per CTA (warp shuffles, then shared memory) before one 64-bit
+// atomicMax per row.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
+// warps 2..5 = epilogue (TMEM lane quadrant = warp % 4).
+// Reference: code/kernel/dels.py:49-79 + :443-456 (the per-step low-rank scorer and
+// argmax of the greedy rollout) and code/dflash.py:468 (the long-logit GEMM).
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace dels {
+
+constexpr int kSkinnyBM = 128;  // vocab rows per tile (MMA M)
+
+template <int NB>
+struct SkinnyConfig {
+  static_assert(NB == 16 || NB == 32, "NB is 16 or 32");
+  static constexpr int kABytes = kSkinnyBM * kBK * 2;  // vocab tile: 128 x 64 bf16
+  static constexpr int kBBytes = NB * kBK * 2;         // row tile: NB x 64 bf16
+  static constexpr int kStages = 8;
+  static constexpr int kAcc = 4;  // accumulators (tiles) in flight in TMEM
+  static constexpr int kTmemCols = kAcc * NB <= 32 ? 32 : (kAcc * NB <= 64 ? 64 : 128);
+  static constexpr int kBarOffset = kStages * (kABytes + kBBytes);
+  static constexpr int kNumBars = 2 * kStages + 2 * kAcc;
+  static constexpr int kRedOffset = kBarOffset + kNumBars * 8 + 16;
+  static constexpr int kSmemBytes = kRedOffset + 4 * NB * 8 + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+// `map_a0`/`map_a1`: the weights (W [V, H], Vr [V, r]) in 64 x 128 boxes; `map_b0`/`map_b1`:
+// the rows (h [rows, H], alpha-scaled s [rows, r]) in 64 x NB boxes.  args.kb0 / kb1 are
+// the K blocks of the two segments (kb0 = 0 for the base-logit variant).
+template <int NB>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_skinny_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                     const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                     const TcArgs args) {
+  using Cfg = SkinnyConfig<NB>;
+  constexpr int S = Cfg::kStages;
+  constexpr int NA = Cfg::kAcc;
+  extern __shared__ uint8_t smem_raw[];
+
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_addr - raw_addr);
+  const uint32_t a_base = base_addr;
+  const uint32_t b_base = base_addr + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  long long* red = reinterpret_cast<long long*>(smem + Cfg::kRedOffset);  // [4][NB]
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[S + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * S + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * S + NA + a]); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  int m_rows = args.m_rows;
+  if (args.m_rows_dev != nullptr) {
+    const int d = *args.m_rows_dev;
+    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
+  }
+  const int num_tiles = (args.n_cols + kSkinnyBM - 1) / kSkinnyBM;
+  const int total_kb = args.kb0 + args.kb1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < NA; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4 * 32);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&map_a0);
+    tma_prefetch_map(&map_b0);
+    tma_prefetch_map(&map_a1);
+    tma_prefetch_map(&map_b1);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      constexpr uint32_t tx = (uint32_t)(Cfg::kABytes + Cfg::kBBytes);
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int n0 = t * kSkinnyBM;
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(stage), tx);
+          const uint32_t a_dst = a_base + stage * Cfg::kABytes;
+          const uint32_t b_dst = b_base + stage * Cfg::kBBytes;
+          if (kb < args.kb0) {
+            tma_load_2d(a_dst, &map_a0, full_bar(stage), kb * kBK, n0);
+            tma_load_2d(b_dst, &map_b0, full_bar(stage), kb * kBK, 0);
+          } else {
+            const int k1 = kb - args.kb0;
+            tma_load_2d(a_dst, &map_a1, full_bar(stage), k1 * kBK, n0);
+            tma_load_2d(b_dst, &map_b1, full_bar(stage), k1 * kBK, 0);
+          }
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Aborting: let the copies already in flight land before the CTA exits.
+        const int outstanding = issued < S ? issued : S;
+        int s = stage;
+        uint32_t p = phase;
+        for (int i = 0; i < outstanding; ++i) {
+          if (--s < 0) {
+            s = S - 1;
+            p ^= 1u;
+          }
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(full_bar(s), p) && globaltimer_ns() - t0 < kWaitLimitNs / 20) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(kSkinnyBM, NB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag, args.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * NB);
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_desc(a_base + stage * Cfg::kABytes);
+          const uint64_t bdesc = make_sw128_desc(b_base + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes per 16-element K step inside the 128-byte swizzled row.
+            tc_mma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                        (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(empty_bar(stage));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(tfull_bar(acc));
+        if (++acc == NA) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok || *abort_flag) {
+        // Drain: every MMA this thread issued completes before TMEM is released.
+        const uint32_t drain = tfull_bar(acc);
+        tc_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, acc_phase) && globaltimer_ns() - t0 < kWaitLimitNs / 20) {
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp can access
+    const int nrows = m_rows < NB ? m_rows : NB;
+    float negb[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      negb[b] = (b < nrows && args.prior != nullptr) ? -__ldg(&args.beta[row_position(args.row_pos, b, args.n_pos)])
+                                                     : 0.0f;
+    long long run[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) run[b] = kKeyEmpty;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const int v = t * kSkinnyBM + quad * 32 + lane;  // this thread's vocab row in the slice
+      const bool v_ok = v < args.n_cols;
+      // Operands of the epilogue, loaded before the accumulator wait so their latency
+      // overlaps the tile's MMAs.
+      const float pv = (v_ok && args.prior != nullptr) ? __ldg(args.prior + v) : 0.0f;
+      float bv[NB];
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        bv[b] = (v_ok && args.base != nullptr && b < nrows) ? __bfloat162float(args.base[(long long)b * args.ld_base + v])
+                                                            : 0.0f;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * NB);
+      uint32_t d[NB];
+      if constexpr (NB == 16) {
+        tmem_ld_16cols(taddr, d);
+      } else {
+        tmem_ld_32cols(taddr, d);
+      }
+      tmem_ld_wait(d);
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+      if (v_ok) {
+        const uint32_t vidx = (uint32_t)(args.v_begin + v);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          if (b < nrows) {
+            float sc = __uint_as_float(d[b]) + bv[b];
+            sc = fmaf(negb[b], pv, sc);
+            const long long key = (long long)(((unsigned long long)(uint32_t)ordered_i32_dev(sc) << 32) |
+                                              (unsigned long long)(0xFFFFFFFFu - vidx));
+            run[b] = key > run[b] ? key : run[b];
+          }
+        }
+      }
+      if (++acc == NA) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    // Per row: maximum over the warp's lanes, then over the four epilogue warps.
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      if (b < nrows) {
+        long long k = run[b];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const long long other = __shfl_xor_sync(0xFFFFFFFFu, k, o);
+          k = other > k ? other : k;
+        }
+        if (lane == 0) red[quad * NB + b] = k;
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const int et = threadIdx.x - 64;  // 0..127 over the epilogue warps
+    if (et < nrows && *abort_flag == 0) {
+      long long k = red[et];
+      for (int q = 1; q < 4; ++q) k = red[q * NB + et] > k ? red[q * NB + et] : k;
+      if (k != kKeyEmpty) {
+        atomicMax(&args.keys[et], k);
+        __threadfence();
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+  if (args.idx_out != nullptr) {
+    // The last CTA to finish turns the packed keys into token ids.
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned prev = atomicAdd(args.counter, 1u);
+      *last_flag = (prev == gridDim.x - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (*last_flag) {
+      __threadfence();
+      for (int row = threadIdx.x; row < m_rows; row += blockDim.x) {
+        const long long key = (long long)atomicAdd(reinterpret_cast<unsigned long long*>(&args.keys[row]), 0ull);
+        args.idx_out[row] = (long long)key_index(key);
+        if (args.score_out != nullptr) args.score_out[row] = key_score(key);
+      }
+      if (threadIdx.x == 0) atomicExch(args.counter, 0u);
+    }
+  }
+}
+
+}  // namespace dels

@@ -60,8 +60,12 @@ def _rand_case(rng, rows, H, r, V, n_pos):
 
 SHAPES = [
     # rows, H, r, V, n_pos, activation, prior
+    # at most 32 rows: the skinny scorer (16- or 32-column row tiles)
     (16, 256, 64, 4099, 16, "identity", True),
     (1, 128, 64, 1000, 1, "identity", True),
+    (24, 256, 64, 5003, 8, "silu", True),
+    # 33..128 rows: one 128-row tile; more: CTA pairs
+    (48, 320, 96, 2347, 16, "identity", True),
     (130, 320, 96, 2347, 8, "silu", True),
     (300, 200, 40, 517, 16, "identity", False),
     (512, 4096, 256, 3000, 16, "identity", True),
@@ -114,23 +118,29 @@ def test_base_variant_matches_oracle(cuda_device):
     """The DeLSGraphRunner step: base logits + alpha * low-rank - beta * prior."""
     from dels_b200 import ops
 
-    rng = np.random.default_rng(9)
-    rows, r, V, n_pos = 5, 48, 3001, 5
+    for rows in (5, 24, 40, 150):  # skinny (16 / 32 columns), one 128-row tile, CTA pairs
+        _base_variant_case(cuda_device, rows)
+
+
+def _base_variant_case(dev, rows):
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(9 + rows)
+    r, V, n_pos = 48, 3001, 5
     base = O.bf16_round(rng.standard_normal((rows, V)).astype(np.float32))
     s = O.bf16_round(rng.standard_normal((rows, r)).astype(np.float32))
     Vr = O.bf16_round((rng.standard_normal((V, r)) * 0.1).astype(np.float32))
     prior = O.bf16_round(O.zipf_log_prior(V).astype(np.float32))
     alpha = np.linspace(0.8, 0.3, n_pos)
     beta = np.linspace(0.1, 0.3, n_pos)
-    s_scaled = O.bf16_round((alpha[:, None] * s).astype(np.float32))
-    dev = cuda_device
+    s_scaled = O.bf16_round((alpha[np.arange(rows) % n_pos][:, None] * s).astype(np.float32))
     for ld_extra in (7, 3):  # row stride 3008 takes the 16-byte vector path, 3004 the scalar one
         base_t = torch.zeros(rows, V + ld_extra, dtype=torch.bfloat16, device=dev)
         base_t[:, :V] = _bf16(base, dev)
         out = ops.fused_argmax_base_bf16(base_t[:, :V], _bf16(s_scaled, dev), _bf16(Vr, dev), _f32(prior, dev),
                                          _f32(beta, dev), n_pos=n_pos, with_scores=True)
         torch.cuda.synchronize()
-        ref = O.base_scores(base, s_scaled, Vr, prior, np.ones(rows), beta)
+        ref = O.base_scores(base, s_scaled, Vr, prior, np.ones(rows), beta[np.arange(rows) % n_pos])
         _check_tokens(out.tokens.cpu().numpy(), out.scores.cpu().numpy(), ref, BF16_TOL)
 
 
