@@ -8,6 +8,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <string>
 
 #include "f32_score.cuh"
@@ -36,6 +37,9 @@ bool g_use_pairs = true;
 // (DELS_SCORER_SKINNY=0 in the environment selects the 128-row tile kernel instead).
 bool g_use_skinny = true;
 constexpr int kSkinnyMaxRows = 32;
+// Programmatic dependent launch for the kernels of a rollout step (DELS_PDL=0 in the
+// environment turns it off).
+bool g_use_pdl = true;
 
 thread_local std::string g_last_error;
 
@@ -56,6 +60,31 @@ int cuda_fail(cudaError_t e, const char* what) {
 #define DELS_CHECK_LAUNCH(what)                    \
   do {                                             \
     cudaError_t e_ = cudaGetLastError();           \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+// Launch with programmatic stream serialisation: the kernel may start while the previous
+// kernel in the stream finishes.  Only kernels that call pdl_wait() before touching the
+// data of earlier kernels are launched this way.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_use_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+#define DELS_CHECK_PDL(what, ...)                    \
+  do {                                               \
+    cudaError_t e_ = (__VA_ARGS__);                  \
     if (e_ != cudaSuccess) return cuda_fail(e_, what); \
   } while (0)
 
@@ -140,6 +169,7 @@ int init_device(int dev) {
   if (g_dev[dev].ready) return DELS_OK;
   if (const char* env = getenv("DELS_SCORER_PAIRS")) g_use_pairs = env[0] != '0';
   if (const char* env = getenv("DELS_SCORER_SKINNY")) g_use_skinny = env[0] != '0';
+  if (const char* env = getenv("DELS_PDL")) g_use_pdl = env[0] != '0';
   int prev = -1;
   cudaError_t e = cudaGetDevice(&prev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -286,8 +316,8 @@ int launch_tc(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) 
   const int grid = (int)(want < sm_count ? want : sm_count);
   if (grid <= 0) return DELS_OK;
   constexpr int smem = TcConfig<BN, VB && MODE == kArgmax>::kSmemBytes;
-  tc_gemm_kernel<BN, MODE, VB><<<grid, kTcThreads, smem, st>>>(ma0, mb0, ma1, mb1, mb0t, mb1t, args);
-  DELS_CHECK_LAUNCH("tc_gemm_kernel launch");
+  DELS_CHECK_PDL("tc_gemm_kernel launch", launch_pdl(tc_gemm_kernel<BN, MODE, VB>, dim3(grid),
+      dim3(kTcThreads), smem, st, ma0, mb0, ma1, mb1, mb0t, mb1t, args));
   return DELS_OK;
 }
 
@@ -318,8 +348,8 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
   const int tiles = cdiv(op.n_extent, kSkinnyBM);
   const int grid = tiles < sm_count ? tiles : sm_count;
   if (grid <= 0) return DELS_OK;
-  tc_skinny_kernel<NB><<<grid, kTcThreads, SkinnyConfig<NB>::kSmemBytes, st>>>(wa0, rb0, wa1, rb1, args);
-  DELS_CHECK_LAUNCH("tc_skinny_kernel launch");
+  DELS_CHECK_PDL("tc_skinny_kernel launch", launch_pdl(tc_skinny_kernel<NB>, dim3(grid), dim3(kTcThreads),
+      SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
   return DELS_OK;
 }
 
@@ -471,9 +501,9 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
   if (rows == 0) return DELS_OK;
 
   if ((flags & DELS_FLAG_KEYS_READY) == 0u) {
-    keys_init_kernel<<<cdiv(rows, 256) < 1024 ? cdiv(rows, 256) : 1024, 256, 0, st>>>(
-        reinterpret_cast<long long*>(keys), rows, hdr.counter);
-    DELS_CHECK_LAUNCH("keys_init_kernel launch");
+    DELS_CHECK_PDL("keys_init_kernel launch", launch_pdl(keys_init_kernel,
+        dim3(cdiv(rows, 256) < 1024 ? cdiv(rows, 256) : 1024), dim3(256), 0, st,
+        reinterpret_cast<long long*>(keys), rows, hdr.counter));
   }
 
   TcOperands op;
@@ -585,12 +615,10 @@ int dels_rank_project_bf16(const void* x, int64_t ld_x, const void* w_rank, int6
     return rc;
   const long long total = (long long)rows * r;
   const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
-  rank_finalize_kernel<<<grid, 256, 0, st>>>(partials, plan.splits, (long long)rows * plan.ld_out, plan.ld_out, rows,
-                                             r, activation, alpha, n_pos, row_pos,
-                                             reinterpret_cast<__nv_bfloat16*>(s_out),
-                                             reinterpret_cast<__nv_bfloat16*>(s_scaled),
-                                             reinterpret_cast<long long*>(keys), hdr.counter);
-  DELS_CHECK_LAUNCH("rank_finalize_kernel launch");
+  DELS_CHECK_PDL("rank_finalize_kernel launch", launch_pdl(rank_finalize_kernel, dim3(grid), dim3(256), 0, st,
+      partials, plan.splits, (long long)rows * plan.ld_out, plan.ld_out, rows, r, activation, alpha, n_pos,
+      row_pos, reinterpret_cast<__nv_bfloat16*>(s_out), reinterpret_cast<__nv_bfloat16*>(s_scaled),
+      reinterpret_cast<long long*>(keys), hdr.counter));
   return DELS_OK;
 }
 
@@ -658,11 +686,10 @@ int dels_draft_score_bf16(const void* h, int64_t ld_h, const void* W, int64_t ld
     return rc;
   const long long total = (long long)rows * r;
   const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
-  rank_finalize_kernel<<<grid, 256, 0, st>>>(partials, plan.splits, (long long)rows * plan.ld_out, plan.ld_out, rows,
-                                             r, activation, alpha, n_pos, row_pos, nullptr,
-                                             reinterpret_cast<__nv_bfloat16*>(s_scaled),
-                                             reinterpret_cast<long long*>(keys), hdr.counter);
-  DELS_CHECK_LAUNCH("rank_finalize_kernel launch");
+  DELS_CHECK_PDL("rank_finalize_kernel launch", launch_pdl(rank_finalize_kernel, dim3(grid), dim3(256), 0, st,
+      partials, plan.splits, (long long)rows * plan.ld_out, plan.ld_out, rows, r, activation, alpha, n_pos,
+      row_pos, nullptr, reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys),
+      hdr.counter));
   return fused_argmax_common(h, ld_h, W, ld_w, nullptr, 0, s_scaled, r, Vr, ld_vr, prior, beta, n_pos, row_pos,
                              rows, rows_dev, H, r, V, v_begin, DELS_FLAG_KEYS_READY, keys, idx_out, score_out, ws,
                              ws_bytes, st);
@@ -724,9 +751,9 @@ int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t l
     if (e != cudaSuccess) return cuda_fail(e, "f32_score_kernel launch");
   }
   if (idx_out != nullptr) {
-    keys_decode_kernel<<<cdiv(rows, 256), 256, 0, st>>>(reinterpret_cast<const long long*>(keys), rows, nullptr,
-                                                        reinterpret_cast<long long*>(idx_out), score_out);
-    DELS_CHECK_LAUNCH("keys_decode_kernel launch");
+    DELS_CHECK_PDL("keys_decode_kernel launch", launch_pdl(keys_decode_kernel, dim3(cdiv(rows, 256)),
+        dim3(256), 0, st, reinterpret_cast<const long long*>(keys), rows, nullptr,
+        reinterpret_cast<long long*>(idx_out), score_out));
   }
   return DELS_OK;
 }
@@ -743,9 +770,8 @@ int dels_keys_init(int64_t* keys, int rows, void* ws, void* stream) {
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (rows == 0 && counter == nullptr) return DELS_OK;
   const int grid = rows > 0 ? (cdiv(rows, 256) < 1024 ? cdiv(rows, 256) : 1024) : 1;
-  keys_init_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(reinterpret_cast<long long*>(keys),
-                                                                            rows, counter);
-  DELS_CHECK_LAUNCH("keys_init_kernel launch");
+  DELS_CHECK_PDL("keys_init_kernel launch", launch_pdl(keys_init_kernel, dim3(grid), dim3(256), 0,
+      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<long long*>(keys), rows, counter));
   return DELS_OK;
 }
 
@@ -757,9 +783,9 @@ int dels_keys_decode(const int64_t* keys, int rows, const int32_t* rows_dev, int
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (rows == 0) return DELS_OK;
   const int grid = cdiv(rows, 256) < 1024 ? cdiv(rows, 256) : 1024;
-  keys_decode_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const long long*>(keys), rows, rows_dev, reinterpret_cast<long long*>(idx_out), score_out);
-  DELS_CHECK_LAUNCH("keys_decode_kernel launch");
+  DELS_CHECK_PDL("keys_decode_kernel launch", launch_pdl(keys_decode_kernel, dim3(grid), dim3(256), 0,
+      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<const long long*>(keys), rows, rows_dev,
+      reinterpret_cast<long long*>(idx_out), score_out));
   return DELS_OK;
 }
 
@@ -871,11 +897,13 @@ int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi
   int rc;
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;
-  gru_step_kernel<<<cdiv(G, kGruCols), kGruThreads, gru_smem_bytes(G), reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const long long*>(tokens), tok_stride, reinterpret_cast<const __nv_bfloat16*>(gi_table),
-      ld_table, reinterpret_cast<const __nv_bfloat16*>(w_hh), reinterpret_cast<const __nv_bfloat16*>(b_hh),
-      reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V, status);
-  DELS_CHECK_LAUNCH("gru_step_kernel launch");
+  DELS_CHECK_PDL("gru_step_kernel launch", launch_pdl(gru_step_kernel, dim3(cdiv(G, kGruCols)),
+      dim3(kGruThreads), gru_smem_bytes(G), reinterpret_cast<cudaStream_t>(stream),
+      reinterpret_cast<const long long*>(tokens), tok_stride,
+      reinterpret_cast<const __nv_bfloat16*>(gi_table), ld_table,
+      reinterpret_cast<const __nv_bfloat16*>(w_hh), reinterpret_cast<const __nv_bfloat16*>(b_hh),
+      reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V,
+      status));
   return DELS_OK;
 }
 
@@ -896,12 +924,12 @@ int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;
   const int grid = cdiv(r, kGemvThreads / 32) < 2 * ds->sm_count ? cdiv(r, kGemvThreads / 32) : 2 * ds->sm_count;
-  rank_gemv_kernel<<<grid, kGemvThreads, rank_gemv_smem_bytes(K), reinterpret_cast<cudaStream_t>(stream)>>>(
+  DELS_CHECK_PDL("rank_gemv_kernel launch", launch_pdl(rank_gemv_kernel, dim3(grid), dim3(kGemvThreads),
+      rank_gemv_smem_bytes(K), reinterpret_cast<cudaStream_t>(stream),
       reinterpret_cast<const __nv_bfloat16*>(x), ld_x, reinterpret_cast<const __nv_bfloat16*>(w), ld_w,
       reinterpret_cast<const __nv_bfloat16*>(bias), B, K, r, activation, alpha, n_pos, row_pos,
       reinterpret_cast<__nv_bfloat16*>(s_out), reinterpret_cast<__nv_bfloat16*>(s_scaled),
-      reinterpret_cast<long long*>(keys), counter);
-  DELS_CHECK_LAUNCH("rank_gemv_kernel launch");
+      reinterpret_cast<long long*>(keys), counter));
   return DELS_OK;
 }
 
@@ -918,11 +946,10 @@ int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, cons
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;
   const int grid = cdiv((long long)B * r, 256) < 1024 ? cdiv((long long)B * r, 256) : 1024;
-  gather_scaled_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const long long*>(tokens), tok_stride, reinterpret_cast<const __nv_bfloat16*>(emb), ld_emb,
-      alpha, n_pos, B, r, V, reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys), counter,
-      status);
-  DELS_CHECK_LAUNCH("gather_scaled_kernel launch");
+  DELS_CHECK_PDL("gather_scaled_kernel launch", launch_pdl(gather_scaled_kernel, dim3(grid), dim3(256), 0,
+      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<const long long*>(tokens), tok_stride,
+      reinterpret_cast<const __nv_bfloat16*>(emb), ld_emb, alpha, n_pos, B, r, V,
+      reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys), counter, status));
   return DELS_OK;
 }
 

@@ -125,6 +125,17 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 }
 
 // --------------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while the previous kernel in the stream is still running; it
+// calls pdl_wait() before it reads anything an earlier kernel wrote or writes anything
+// an earlier kernel reads (the wait returns once the previous grid has completed and
+// its memory is visible).  pdl_trigger() lets the next kernel launch now.  Both are
+// no-ops in a normal launch.
+// --------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// --------------------------------------------------------------------------------
 // mbarrier
 // --------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

@@ -123,7 +123,8 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
   const bool has_row = gate < 3 && g0 + c_w < G;
   const __nv_bfloat16* wrow = w_hh + (long long)(gate * G + g0 + c_w) * G;
   RowPrefetch pre;
-  if (has_row) row_prefetch(wrow, G, lane, pre);
+  if (has_row) row_prefetch(wrow, G, lane, pre);  // weights only: safe before the wait
+  pdl_wait();
   for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
     const int nb = min(kRunnerMaxB, B - b0);
     __syncthreads();
@@ -169,6 +170,7 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
       h_out[(long long)(b0 + b) * G + g] = __float2bfloat16_rn((1.0f - zg) * ng + zg * h);
     }
   }
+  pdl_trigger();
 }
 
 // One warp per output feature j (grid-stride), all B rows at once.  The warp's first
@@ -184,7 +186,8 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
   const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
   const int nwarps = gridDim.x * (blockDim.x >> 5);
   RowPrefetch first;
-  if (gwarp < r) row_prefetch(w + (long long)gwarp * ld_w, K, lane, first);
+  if (gwarp < r) row_prefetch(w + (long long)gwarp * ld_w, K, lane, first);  // weights only
+  pdl_wait();
   for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
     const int nb = min(kRunnerMaxB, B - b0);
     __syncthreads();
@@ -223,12 +226,14 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
     for (int i = threadIdx.x; i < B; i += blockDim.x) keys[i] = kKeyEmpty;
   }
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
+  pdl_trigger();
 }
 
 __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride,
                                      const __nv_bfloat16* __restrict__ emb, long long ld_emb,
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter, int* status) {
+  pdl_wait();
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < B * r; e += gridDim.x * blockDim.x) {
     const int b = e / r, j = e % r;
     long long tok = tokens[(long long)b * tok_stride];
@@ -241,6 +246,7 @@ __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long 
     if (keys != nullptr && j == 0) keys[b] = kKeyEmpty;
   }
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
+  pdl_trigger();
 }
 
 }  // namespace dels

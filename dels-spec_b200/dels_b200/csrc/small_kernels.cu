@@ -22,6 +22,7 @@ __global__ void rank_finalize_kernel(const float* __restrict__ partials, int spl
                                      long long ld_part, int rows, int r, int activation, const float* __restrict__ alpha,
                                      int n_pos, const int* __restrict__ row_pos, __nv_bfloat16* s_out,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter) {
+  pdl_wait();
   const long long total = (long long)rows * r;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -42,6 +43,7 @@ __global__ void rank_finalize_kernel(const float* __restrict__ partials, int spl
 }
 
 __global__ void keys_init_kernel(long long* keys, int rows, unsigned* counter) {
+  pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x)
     keys[i] = kKeyEmpty;
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
@@ -49,6 +51,7 @@ __global__ void keys_init_kernel(long long* keys, int rows, unsigned* counter) {
 
 __global__ void keys_decode_kernel(const long long* __restrict__ keys, int rows, const int* rows_dev,
                                    long long* idx_out, float* score_out) {
+  pdl_wait();
   int n = rows;
   if (rows_dev != nullptr) {
     const int d = *rows_dev;

@@ -192,6 +192,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_wait();
 
   int m_rows = args.m_rows;
   if (args.m_rows_dev != nullptr) {
@@ -528,6 +529,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   // ------------------------------------------------------------------ teardown
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -74,11 +74,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  int m_rows = args.m_rows;
-  if (args.m_rows_dev != nullptr) {
-    const int d = *args.m_rows_dev;
-    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
-  }
   const int num_tiles = (args.n_cols + kSkinnyBM - 1) / kSkinnyBM;
   const int total_kb = args.kb0 + args.kb1;
 
@@ -109,6 +104,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Set-up above touches no global memory; from here on the inputs of earlier kernels
+  // (rows, keys, device row count) are read.
+  pdl_wait();
+  int m_rows = args.m_rows;
+  if (args.m_rows_dev != nullptr) {
+    const int d = *args.m_rows_dev;
+    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -288,6 +291,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   // ------------------------------------------------------------------ teardown
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
