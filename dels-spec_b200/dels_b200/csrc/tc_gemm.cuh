@@ -21,9 +21,9 @@
 // issuer (one thread), warps 2..5 = epilogue (one thread per accumulator row).
 //
 // Epilogues:
-//   kArgmax : score = acc (+ base[row, v]) - beta_p * prior[v]; running (max, first
-//             index) over the tile's columns in registers, then one 64-bit atomicMax
-//             of the packed key per (row, tile).  The last CTA to finish decodes the
+//   kArgmax : score = acc (+ base[row, v]) - beta_p * prior[v]; the packed (score,
+//             index) key of each 32-column chunk (chunk_best_key) folded into a running
+//             maximum in registers, then one 64-bit atomicMax per (row, tile).  The last CTA to finish decodes the
 //             keys into int64 token ids (optional).
 //   kStore  : write the fp32 accumulator tile to out[split][row][n] (split-K partial
 //             sums; used by the rank projection and the RNN input projection).
