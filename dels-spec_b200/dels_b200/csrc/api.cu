@@ -204,6 +204,7 @@ int init_device(int dev) {
     SET(f32_rank_kernel, 0);
     SET(gru_step_kernel, kMaxSmem);
     SET(rank_gemv_kernel, kMaxSmem);
+    SET(linear_finalize_kernel, 0);
     SET(gather_scaled_kernel, 0);
     SET(wait_selftest_kernel, 0);
 #undef SET
@@ -907,9 +908,10 @@ int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi
   return DELS_OK;
 }
 
-int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias, int B, int K,
-                        int r, int activation, const float* alpha, int n_pos, const int32_t* row_pos, void* s_out,
-                        void* s_scaled, int64_t* keys, void* ws, void* stream) {
+static int rank_gemv_common(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias,
+                            const void* addend, int64_t ld_add, int B, int K, int r, int activation,
+                            const float* alpha, int n_pos, const int32_t* row_pos, void* s_out, void* s_scaled,
+                            int64_t* keys, void* ws, void* stream) {
   int rc;
   if (B < 0 || K <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d K=%d r=%d", B, K, r);
   if ((K % 8) != 0) return fail(DELS_ERR_UNSUPPORTED, "K = %d must be a multiple of 8", K);
@@ -918,6 +920,8 @@ int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w
   if (n_pos <= 0 || s_scaled == nullptr) return fail(DELS_ERR_INVALID_ARG, "n_pos <= 0 or s_scaled NULL");
   if ((rc = check_bf16_matrix("x", x, ld_x, K)) != DELS_OK) return rc;
   if ((rc = check_bf16_matrix("w_rank", w, ld_w, K)) != DELS_OK) return rc;
+  if (addend != nullptr && ld_add < r) return fail(DELS_ERR_INVALID_ARG, "z leading dimension %lld < %d",
+                                                   (long long)ld_add, r);
   if (rank_gemv_smem_bytes(K) > (size_t)kMaxSmem) return fail(DELS_ERR_UNSUPPORTED, "K = %d too large", K);
   unsigned* counter = ws != nullptr ? reinterpret_cast<unsigned*>(ws) : nullptr;
   DeviceState* ds = nullptr;
@@ -927,9 +931,55 @@ int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w
   DELS_CHECK_PDL("rank_gemv_kernel launch", launch_pdl(rank_gemv_kernel, dim3(grid), dim3(kGemvThreads),
       rank_gemv_smem_bytes(K), reinterpret_cast<cudaStream_t>(stream),
       reinterpret_cast<const __nv_bfloat16*>(x), ld_x, reinterpret_cast<const __nv_bfloat16*>(w), ld_w,
-      reinterpret_cast<const __nv_bfloat16*>(bias), B, K, r, activation, alpha, n_pos, row_pos,
-      reinterpret_cast<__nv_bfloat16*>(s_out), reinterpret_cast<__nv_bfloat16*>(s_scaled),
-      reinterpret_cast<long long*>(keys), counter));
+      reinterpret_cast<const __nv_bfloat16*>(bias), reinterpret_cast<const __nv_bfloat16*>(addend),
+      (long long)ld_add, B, K, r, activation, alpha, n_pos, row_pos, reinterpret_cast<__nv_bfloat16*>(s_out),
+      reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys), counter));
+  return DELS_OK;
+}
+
+int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias, int B, int K,
+                        int r, int activation, const float* alpha, int n_pos, const int32_t* row_pos, void* s_out,
+                        void* s_scaled, int64_t* keys, void* ws, void* stream) {
+  return rank_gemv_common(x, ld_x, w, ld_w, bias, nullptr, 0, B, K, r, activation, alpha, n_pos, row_pos, s_out,
+                          s_scaled, keys, ws, stream);
+}
+
+int dels_correction_mid_bf16(const void* h, int64_t ld_h, const void* w_s, int64_t ld_ws, const void* z,
+                             int64_t ld_z, int B, int G, int M, const float* alpha, void* s_scaled, int64_t* keys,
+                             void* ws, void* stream) {
+  if (z == nullptr) return fail(DELS_ERR_INVALID_ARG, "z is NULL");
+  return rank_gemv_common(h, ld_h, w_s, ld_ws, nullptr, z, ld_z, B, G, M, DELS_ACT_IDENTITY, alpha, 1, nullptr,
+                          nullptr, s_scaled, keys, ws, stream);
+}
+
+size_t dels_linear_workspace_bytes(int rows, int K, int N) {
+  if (rows <= 0 || K <= 0 || N <= 0) return DELS_WS_HEADER_BYTES;
+  return DELS_WS_HEADER_BYTES + projection_partials_bytes(rows, K, N);
+}
+
+int dels_linear_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias, int rows, int K,
+                     int N, void* out, int64_t ld_out, void* ws, size_t ws_bytes, void* stream) {
+  int rc;
+  if (rows < 0 || K <= 0 || N <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape rows=%d K=%d N=%d", rows, K, N);
+  if (out == nullptr || ld_out < N) return fail(DELS_ERR_INVALID_ARG, "out is NULL or ld_out < N");
+  if ((rc = check_bf16_matrix("x", x, ld_x, K)) != DELS_OK) return rc;
+  if ((rc = check_bf16_matrix("w", w, ld_w, K)) != DELS_OK) return rc;
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, dels_linear_workspace_bytes(rows, K, N), &hdr)) != DELS_OK) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (rows == 0) return DELS_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + DELS_WS_HEADER_BYTES);
+  SplitPlan plan;
+  if ((rc = launch_projection(x, ld_x, w, ld_w, rows, K, N, partials, hdr.status, ds->sm_count, st, &plan)) !=
+      DELS_OK)
+    return rc;
+  const long long total = (long long)rows * N;
+  const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
+  DELS_CHECK_PDL("linear_finalize_kernel launch", launch_pdl(linear_finalize_kernel, dim3(grid), dim3(256), 0, st,
+      partials, plan.splits, (long long)rows * plan.ld_out, (long long)plan.ld_out, rows, N,
+      reinterpret_cast<const __nv_bfloat16*>(bias), reinterpret_cast<__nv_bfloat16*>(out), (long long)ld_out));
   return DELS_OK;
 }
 

@@ -6,7 +6,9 @@
 //                            (code/kernel/dels.py:359-373 + the Triton cell :140-211 +
 //                            the table gather :432, :461);
 //   * rank_gemv_kernel     — s = bf16(act(bf16(W_rank h + b))), s_scaled = bf16(alpha s),
-//                            and the packed keys reset (code/kernel/dels.py:437-443);
+//                            and the packed keys reset (code/kernel/dels.py:437-443); for the
+//                            Domino correction MLP, s = SiLU(z + bf16(W_s h)) in fp32
+//                            (code/kernel/domino.py:422, :92-97);
 //   * gather_scaled_kernel — Markov rank state s = embedding[token], s_scaled = bf16(alpha s)
 //                            (code/kernel/markov_dels.py:288).
 //
@@ -174,12 +176,13 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
 }
 
 // One warp per output feature j (grid-stride), all B rows at once.  The warp's first
-// weight row is loaded before x is staged.
+// weight row is loaded before x is staged.  With `addend` (the Domino correction MLP)
+// the output is SiLU(addend + bf16(W x)) in fp32 instead of the rank activation.
 __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
     const __nv_bfloat16* __restrict__ x, long long ld_x, const __nv_bfloat16* __restrict__ w, long long ld_w,
-    const __nv_bfloat16* __restrict__ bias, int B, int K, int r, int activation, const float* __restrict__ alpha,
-    int n_pos, const int* __restrict__ row_pos, __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys,
-    unsigned* counter) {
+    const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ addend, long long ld_add, int B,
+    int K, int r, int activation, const float* __restrict__ alpha, int n_pos, const int* __restrict__ row_pos,
+    __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter) {
   extern __shared__ uint4 smem4[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);  // [kRunnerMaxB][K]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -215,7 +218,13 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
         const int row = b0 + lane;
         const float bj = bias != nullptr ? __bfloat162float(bias[j]) : 0.0f;
         float s = bf16r(a + bj);
-        if (activation == DELS_ACT_SILU) s = bf16r(s / (1.0f + expf(-s)));
+        if (addend != nullptr) {
+          // correction MLP: SiLU(z + s) in fp32, not re-rounded (code/kernel/domino.py:92-97)
+          const float pre = __bfloat162float(addend[(long long)row * ld_add + j]) + s;
+          s = pre / (1.0f + expf(-pre));
+        } else if (activation == DELS_ACT_SILU) {
+          s = bf16r(s / (1.0f + expf(-s)));
+        }
         if (s_out != nullptr) s_out[(long long)row * r + j] = __float2bfloat16_rn(s);
         const float al = alpha != nullptr ? alpha[row_position(row_pos, row, n_pos)] : 1.0f;
         s_scaled[(long long)row * r + j] = __float2bfloat16_rn(al * s);

@@ -22,7 +22,8 @@ __global__ void gru_step_kernel(const long long* __restrict__ tokens, long long 
 
 __global__ void rank_gemv_kernel(const __nv_bfloat16* __restrict__ x, long long ld_x,
                                  const __nv_bfloat16* __restrict__ w, long long ld_w,
-                                 const __nv_bfloat16* __restrict__ bias, int B, int K, int r, int activation,
+                                 const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ addend,
+                                 long long ld_add, int B, int K, int r, int activation,
                                  const float* __restrict__ alpha, int n_pos, const int* __restrict__ row_pos,
                                  __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter);
 

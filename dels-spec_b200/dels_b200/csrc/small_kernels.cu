@@ -42,6 +42,29 @@ __global__ void rank_finalize_kernel(const float* __restrict__ partials, int spl
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
 }
 
+// -----------------------------------------------------------------------------------
+// F.linear epilogue: out[row, n] = bf16(sum of the split-K partials + bias[n]).  The bias
+// joins the fp32 accumulator before the single rounding, like the bias epilogue of the
+// bf16 GEMM behind F.linear (code/kernel/domino.py:404-408, :325-327).
+// -----------------------------------------------------------------------------------
+__global__ void linear_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
+                                       long long ld_part, int rows, int n, const __nv_bfloat16* __restrict__ bias,
+                                       __nv_bfloat16* out, long long ld_out) {
+  pdl_wait();
+  const long long total = (long long)rows * n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / n);
+    const int col = (int)(i - (long long)row * n);
+    const long long pi = (long long)row * ld_part + col;
+    float acc = 0.0f;
+    for (int s = 0; s < splits; ++s) acc += partials[s * split_stride + pi];
+    if (bias != nullptr) acc += __bfloat162float(bias[col]);
+    out[(long long)row * ld_out + col] = __float2bfloat16_rn(acc);
+  }
+  pdl_trigger();
+}
+
 __global__ void keys_init_kernel(long long* keys, int rows, unsigned* counter) {
   pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x)

@@ -12,6 +12,10 @@ __global__ void rank_finalize_kernel(const float* __restrict__ partials, int spl
                                      int n_pos, const int* __restrict__ row_pos, __nv_bfloat16* s_out,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter);
 
+__global__ void linear_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
+                                       long long ld_part, int rows, int n, const __nv_bfloat16* __restrict__ bias,
+                                       __nv_bfloat16* out, long long ld_out);
+
 __global__ void keys_init_kernel(long long* keys, int rows, unsigned* counter);
 
 __global__ void keys_decode_kernel(const long long* __restrict__ keys, int rows, const int* rows_dev,

@@ -574,3 +574,80 @@ def gather_scaled_rows(
               _ptr(alpha), int(n_pos), B, r, emb.shape[0], _ptr(s_scaled), _ptr(keys),
               None if ws is None else ws.ptr, _stream(s_scaled.device))
     return s_scaled
+
+
+def linear_bf16(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    out: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """F.linear(x, w, bias) for bf16 operands: out = bf16(x . w^T + bias), one rounding."""
+    _require_cuda("x", x, torch.bfloat16, 2)
+    _require_cuda("w", w, torch.bfloat16, 2)
+    rows, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"w {tuple(w.shape)} does not match x {tuple(x.shape)}")
+    if bias is not None:
+        _require_cuda("bias", bias, torch.bfloat16, 1)
+        if bias.shape[0] != N or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous [N] tensor")
+    if out is None:
+        out = torch.empty(rows, N, dtype=torch.bfloat16, device=x.device)
+    elif out.shape != (rows, N) or out.dtype != torch.bfloat16 or out.stride(1) != 1:
+        raise ValueError("out must be a row-major bf16 [rows, N] tensor")
+    need = _lib.query("dels_linear_workspace_bytes", rows, K, N)
+    ws = workspace(need, x.device) if ws is None else ws.ensure(need)
+    _lib.call("dels_linear_bf16", _ptr(x), _row_major("x", x), _ptr(w), _row_major("w", w), _ptr(bias), rows, K, N,
+              _ptr(out), _row_major("out", out), ws.ptr, ws.nbytes, _stream(x.device))
+    return out
+
+
+def correction_mid(
+    h: torch.Tensor,
+    w_s: torch.Tensor,
+    z: torch.Tensor,
+    alpha: torch.Tensor,
+    s_scaled: torch.Tensor,
+    *,
+    keys: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """Domino correction MLP hidden layer: s_scaled = bf16(alpha * SiLU(z + bf16(W_s h))), SiLU in fp32."""
+    _require_cuda("h", h, torch.bfloat16, 2)
+    _require_cuda("w_s", w_s, torch.bfloat16, 2)
+    _require_cuda("z", z, torch.bfloat16, 2)
+    B, G = h.shape
+    M = w_s.shape[0]
+    if w_s.shape[1] != G or z.shape != (B, M) or z.stride(1) != 1 or s_scaled.shape != (B, M) \
+            or not s_scaled.is_contiguous():
+        raise ValueError("correction MLP shapes do not match")
+    _lib.call("dels_correction_mid_bf16", _ptr(h), _row_major("h", h), _ptr(w_s), _row_major("w_s", w_s), _ptr(z),
+              _row_major("z", z), B, G, M, _ptr(alpha), _ptr(s_scaled), _ptr(keys),
+              None if ws is None else ws.ptr, _stream(h.device))
+    return s_scaled
+
+
+def zero_pad(t: torch.Tensor | None, rows: int | None = None, cols: int | None = None) -> torch.Tensor | None:
+    """``t`` zero-padded to ``rows`` (dim 0) x ``cols`` (dim 1).  The runners carry weight
+    widths as multiples of 8 because TMA tiles need 16-byte row pitches; the zero entries
+    contribute nothing to any contraction."""
+    if t is None:
+        return None
+    shape = list(t.shape)
+    if rows is not None:
+        shape[0] = rows
+    if cols is not None:
+        shape[1] = cols
+    if list(t.shape) == shape:
+        return t
+    out = torch.zeros(shape, dtype=t.dtype, device=t.device)
+    out[tuple(slice(0, n) for n in t.shape)] = t
+    return out
+
+
+def round8(n: int) -> int:
+    return -(-int(n) // 8) * 8

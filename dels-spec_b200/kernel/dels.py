@@ -71,6 +71,7 @@ class DeLSGraphRunner:
         if dtype != torch.bfloat16:
             raise ValueError(f"DeLSGraphRunner kernels are bf16; the local head is {dtype}.")
         self.rank_dim = int(local_head.low_rank_lm_head.weight.shape[1])
+        self._r = ops.round8(self.rank_dim)  # carried rank width, zero-padded to a multiple of 8
         # Kept for the reference's log line (code/benchmark.py:481-484): the fused path
         # is always used here.
         self._can_triton_fuse = True
@@ -89,22 +90,23 @@ class DeLSGraphRunner:
             self.gru_b_ih = gru.bias_ih_l0.detach().to(device).contiguous() if gru.bias else None
             self.gru_b_hh = gru.bias_hh_l0.detach().to(device).contiguous() if gru.bias else None
 
-            embed_weight = local_head.embed_tokens.weight.detach().to(device).contiguous()
-            if self.gru_b_ih is None:
-                # gi table = F.linear(embed, W_ih) (code/kernel/dels.py:265-268) on the
-                # tensor-core projection kernel: bf16 output of an fp32 accumulation.
-                table, _ = ops.rank_project_bf16(embed_weight, self.gru_w_ih, None, n_pos=1)
-            else:
-                table = torch.nn.functional.linear(embed_weight, self.gru_w_ih, self.gru_b_ih)
-            self._gru_input_proj_table = table.contiguous()
+            # gi table = F.linear(embed, W_ih, b_ih) (code/kernel/dels.py:265-268) on the
+            # tensor-core projection kernel: one bf16 rounding of an fp32 accumulation.  The
+            # embedding width is zero-padded to a multiple of 8 for the TMA tiles.
+            E8 = ops.round8(self.gru_w_ih.shape[1])
+            embed_weight = ops.zero_pad(local_head.embed_tokens.weight.detach().to(device).contiguous(), cols=E8)
+            self._gru_input_proj_table = ops.linear_bf16(embed_weight, ops.zero_pad(self.gru_w_ih, cols=E8),
+                                                         self.gru_b_ih)
 
-            self.rank_weight = local_head.rank_proj.weight.detach().to(device).contiguous()
+            self.rank_weight = ops.zero_pad(local_head.rank_proj.weight.detach().to(device).contiguous(),
+                                            rows=self._r)
             self.rank_bias = (
-                local_head.rank_proj.bias.detach().to(device).contiguous()
+                ops.zero_pad(local_head.rank_proj.bias.detach().to(device).contiguous(), rows=self._r)
                 if local_head.rank_proj.bias is not None
                 else None
             )
-            self.lm_head_weight = local_head.low_rank_lm_head.weight.detach().to(device).contiguous()
+            self.lm_head_weight = ops.zero_pad(local_head.low_rank_lm_head.weight.detach().to(device).contiguous(),
+                                               cols=self._r)
 
             baseline_flat = torch.zeros(self.vocab_size, dtype=dtype, device=device)
             if baseline_logits is not None:
@@ -120,7 +122,7 @@ class DeLSGraphRunner:
         # the scorer reads the prior in fp32 (exactly the bf16 values above)
         self._prior_f32 = self.baseline_logits.to(torch.float32) if self.has_baseline else None
 
-        B, G, r, S = self.batch_size, self.gru_hidden_dim, self.rank_dim, self.steps
+        B, G, r, S = self.batch_size, self.gru_hidden_dim, self._r, self.steps
         self.static_prefix_ids = torch.zeros(B, 1, dtype=torch.long, device=device)
         self._alloc_step_inputs(dtype, device)
         self.static_out = torch.zeros(B, S, dtype=torch.long, device=device)

@@ -1,0 +1,213 @@
+"""CUDA-graph runner for the Domino draft correction, on the B200 kernels.
+
+Drop-in for ``kernel.domino.DraftCorrectionGraphRunner`` of the reference
+(code/kernel/domino.py:232-520): same constructor keywords and checks, same
+``__call__(prefix_ids, parallel_hiddens, base_logits, guidance_alpha=None) ->
+LongTensor[B, steps]`` returning a fresh tensor, same static buffers
+(``static_prefix_ids``, ``static_parallel_hiddens``, ``static_base_logits``,
+``static_out``), warm-up on a side stream and capture into ``self.graph``.
+
+Per call (all on ``libdels_b200.so``):
+
+  z = F.linear(parallel_hiddens, W_z, b1)          ``dels_linear_bf16`` (tcgen05, once)
+  h = GRU over the prefix tokens from zero           ``dels_gru_step_bf16`` per token
+  per step t:
+    s' = bf16(alpha * SiLU(z_t + W_s h))             ``dels_correction_mid_bf16``
+    tok = argmax(s' . fc2^T + alpha * b2 + base_t)   ``dels_fused_argmax_base_bf16``
+                                                     (prior = b2, beta = -alpha)
+    h = GRUCell(table[tok], h)                       ``dels_gru_step_bf16``
+
+The correction MLP must be Linear -> SiLU -> Linear (the released Domino head,
+code/dflash.py:271-276, and the only form the reference fuses, :283-291); its weights
+must be bf16.  Other forms raise ``ValueError``.
+"""
+
+from __future__ import annotations
+
+from typing import Tuple
+
+import torch
+import torch.nn as nn
+
+from dels_b200 import ops
+
+
+def unwrap_correction_mlp(embed_proj: nn.Module) -> Tuple[nn.Linear, nn.Module, nn.Linear]:
+    """(fc1, middle, fc2) of ``nn.Sequential(Linear(H + G, M), ..., Linear(M, V))``; the
+    input of fc1 is concat([z, s]) (code/kernel/domino.py:15-50, same errors)."""
+    if not isinstance(embed_proj, nn.Sequential):
+        raise TypeError("Graph runner requires draft_model.embed_proj to be nn.Sequential.")
+    layers = list(embed_proj.children())
+    if len(layers) < 2:
+        raise ValueError("embed_proj must contain at least two layers.")
+    if not isinstance(layers[0], nn.Linear):
+        raise ValueError("embed_proj first layer must be nn.Linear.")
+    if not isinstance(layers[-1], nn.Linear):
+        raise ValueError("embed_proj last layer must be nn.Linear.")
+    middle = nn.Sequential(*layers[1:-1]) if len(layers) > 2 else nn.Identity()
+    return layers[0], middle, layers[-1]
+
+
+def _is_silu(middle: nn.Module) -> bool:
+    if isinstance(middle, nn.SiLU):
+        return True
+    inner = list(middle.children()) if isinstance(middle, nn.Sequential) else []
+    return len(inner) == 1 and isinstance(inner[0], nn.SiLU)
+
+
+def _bf16(t: torch.Tensor | None, device: torch.device) -> torch.Tensor | None:
+    return None if t is None else t.detach().to(device=device, dtype=torch.bfloat16).contiguous()
+
+
+class DraftCorrectionGraphRunner:
+    """
+    CUDA Graph runner for block draft correction (greedy), every step on hand-written
+    sm_100a kernels: correction-MLP hidden layer, fused fc2 GEMV + bias + base logits +
+    argmax on tcgen05 tensor cores, and the GRU cell over the realised token.
+    """
+
+    def __init__(
+        self,
+        draft_model: nn.Module,
+        target_model: nn.Module,
+        batch_size: int,
+        steps: int,
+        hidden_dim: int,
+        gru_hidden_dim: int,
+        vocab_size: int,
+        prefix_token_count: int,
+        device: torch.device,
+        guidance_alpha: float = 1.0,
+    ):
+        self.steps = int(steps)
+        self.draft_model = draft_model
+        self.target_model = target_model
+        self.prefix_token_count = int(prefix_token_count)
+        self.gru_hidden_dim = int(gru_hidden_dim)
+        self.guidance_alpha = float(guidance_alpha)
+        self.batch_size = int(batch_size)
+        self.vocab_size = int(vocab_size)
+
+        fc1, self.middle, fc2 = unwrap_correction_mlp(draft_model.embed_proj)
+        expected_in = hidden_dim + gru_hidden_dim
+        if fc1.in_features != expected_in:
+            raise ValueError(
+                f"Correction MLP input dim mismatch: got {fc1.in_features}, "
+                f"expected {expected_in} = hidden_dim + gru_hidden_dim."
+            )
+        self._middle_is_silu = _is_silu(self.middle)
+        if not self._middle_is_silu:
+            raise ValueError("DraftCorrectionGraphRunner (sm_100a kernels) needs a SiLU correction MLP "
+                             f"(Linear -> SiLU -> Linear); got middle={self.middle!r}.")
+        # Kept for the reference's log line: the fused path is always taken here.
+        self._can_triton_fuse = True
+
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("DraftCorrectionGraphRunner runs on a CUDA device (sm_100a kernels only).")
+        dtype = next(draft_model.parameters()).dtype
+        if dtype != torch.bfloat16:
+            raise ValueError(f"DraftCorrectionGraphRunner kernels are bf16; the draft model is {dtype}.")
+        if self.prefix_token_count < 1:
+            raise ValueError(f"prefix_token_count must be >= 1, got {prefix_token_count}.")
+
+        gru = draft_model.prefix_gru
+        assert gru.num_layers == 1 and not gru.bidirectional
+        B, S, H, G = self.batch_size, self.steps, int(hidden_dim), self.gru_hidden_dim
+        self.hidden_dim = H
+        self.mlp_hidden_dim = int(fc1.out_features)
+        M = ops.round8(self.mlp_hidden_dim)  # carried width, zero-padded to a multiple of 8
+        self._m = M
+        with torch.no_grad():
+            w1 = fc1.weight.detach()
+            self.w_z = ops.zero_pad(_bf16(w1[:, :H], device), rows=M)
+            self.w_s = ops.zero_pad(_bf16(w1[:, H:], device), rows=M)
+            self.fc1_bias = ops.zero_pad(_bf16(fc1.bias, device), rows=M)
+            self.fc2_weight = ops.zero_pad(_bf16(fc2.weight, device), cols=M)
+            self.fc2_bias = _bf16(fc2.bias, device)
+            self.gru_w_ih = _bf16(gru.weight_ih_l0, device)
+            self.gru_w_hh = _bf16(gru.weight_hh_l0, device)
+            self.gru_b_ih = _bf16(gru.bias_ih_l0, device) if gru.bias else None
+            self.gru_b_hh = _bf16(gru.bias_hh_l0, device) if gru.bias else None
+            # gi table = F.linear(embed, W_ih, b_ih) (code/kernel/domino.py:323-327); the
+            # embedding width is zero-padded to a multiple of 8 for the TMA tiles.
+            E8 = ops.round8(self.gru_w_ih.shape[1])
+            embed_weight = ops.zero_pad(_bf16(target_model.model.embed_tokens.weight, device), cols=E8)
+            self._gru_input_proj_table = ops.linear_bf16(embed_weight, ops.zero_pad(self.gru_w_ih, cols=E8),
+                                                         self.gru_b_ih)
+        if int(self.fc2_weight.shape[0]) != self.vocab_size:
+            raise ValueError(f"fc2 has {self.fc2_weight.shape[0]} outputs, vocab_size is {self.vocab_size}.")
+
+        self.static_prefix_ids = torch.zeros(B, self.prefix_token_count, dtype=torch.long, device=device)
+        self.static_parallel_hiddens = torch.zeros(B, S, H, dtype=dtype, device=device)
+        self.static_base_logits = torch.zeros(B, S, self.vocab_size, dtype=dtype, device=device)
+        self.static_out = torch.zeros(B, S, dtype=torch.long, device=device)
+
+        # alpha * b2 enters the scorer as -beta * prior with prior = b2, beta = -alpha
+        self._alpha = torch.tensor([self.guidance_alpha], dtype=torch.float32, device=device)
+        self._beta = torch.tensor([-self.guidance_alpha], dtype=torch.float32, device=device)
+        self._prior_f32 = self.fc2_bias.to(torch.float32).contiguous() if self.fc2_bias is not None else None
+        self._z = torch.zeros(B * S, M, dtype=dtype, device=device)
+        self._h = [torch.zeros(B, G, dtype=dtype, device=device) for _ in range(2)]
+        self._s_scaled = torch.zeros(B, M, dtype=dtype, device=device)
+        self._tokens = torch.zeros(max(S, 1), B, dtype=torch.long, device=device)  # step-major
+        self._keys = torch.empty(B, dtype=torch.int64, device=device)
+        self._ws = ops.Workspace(1 << 12, device)
+        self._ws_lin = ops.Workspace(1 << 12, device)
+        self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
+
+        ops.init(device)
+        stream = torch.cuda.Stream(device=device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.inference_mode(), torch.cuda.stream(stream):
+            for _ in range(3):
+                self._forward_impl()
+        torch.cuda.current_stream(device).wait_stream(stream)
+
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.inference_mode(), torch.cuda.graph(self.graph):
+            self._forward_impl()
+
+    def _forward_impl(self):
+        B, S, H, M = self.batch_size, self.steps, self.hidden_dim, self._m
+        if S > 0:
+            ops.linear_bf16(self.static_parallel_hiddens.view(B * S, H), self.w_z, self.fc1_bias, out=self._z,
+                            ws=self._ws_lin)
+        z = self._z.view(B, S, M)
+        h = None
+        cur = 0
+        for p in range(self.prefix_token_count):
+            h = ops.gru_step(self.static_prefix_ids[:, p], self._gru_input_proj_table, self.gru_w_hh, h,
+                             self._h[cur], b_hh=self.gru_b_hh, ws=self._ws)
+            cur ^= 1
+        for t in range(S):
+            ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys, ws=self._ws)
+            ops.fused_argmax_base_bf16(
+                self.static_base_logits[:, t, :], self._s_scaled, self.fc2_weight, self._prior_f32, self._beta,
+                n_pos=1, keys_ready=True, out=self._outs[t], ws=self._ws,
+            )
+            if t + 1 < S:
+                h = ops.gru_step(self._tokens[t], self._gru_input_proj_table, self.gru_w_hh, h, self._h[cur],
+                                 b_hh=self.gru_b_hh, ws=self._ws)
+                cur ^= 1
+        if S > 0:
+            self.static_out.copy_(self._tokens[:S].t())
+
+    @torch.inference_mode()
+    def __call__(
+        self,
+        prefix_ids: torch.Tensor,
+        parallel_hiddens: torch.Tensor,
+        base_logits: torch.Tensor,
+        guidance_alpha: float | None = None,
+    ) -> torch.Tensor:
+        if guidance_alpha is not None and float(guidance_alpha) != self.guidance_alpha:
+            raise ValueError(
+                "DraftCorrectionGraphRunner captures a fixed domino guidance alpha; "
+                f"got {float(guidance_alpha)} but runner was built with {self.guidance_alpha}."
+            )
+        self.static_prefix_ids.copy_(prefix_ids)
+        self.static_parallel_hiddens.copy_(parallel_hiddens)
+        self.static_base_logits.copy_(base_logits)
+        self.graph.replay()
+        return self.static_out.clone()

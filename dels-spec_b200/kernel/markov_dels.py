@@ -53,9 +53,12 @@ class MarkovDeLSGraphRunner:
         self.vocab_size = int(vocab_size)
         self.alpha_values = [float(x) for x in alpha_values]
         self.beta_values = [float(x) for x in beta_values]
-        self.embedding_weight = local_head.embedding_weight.detach().to(device=device).contiguous()
-        self.lm_head_weight = local_head.lm_head_weight.detach().to(device=device).contiguous()
-        self.rank = int(self.lm_head_weight.shape[1])
+        self.rank = int(local_head.lm_head_weight.shape[1])
+        self._r = ops.round8(self.rank)  # carried rank width, zero-padded to a multiple of 8
+        self.embedding_weight = ops.zero_pad(local_head.embedding_weight.detach().to(device=device).contiguous(),
+                                             cols=self._r)
+        self.lm_head_weight = ops.zero_pad(local_head.lm_head_weight.detach().to(device=device).contiguous(),
+                                           cols=self._r)
         self._can_triton_fuse = True
         dtype = self.lm_head_weight.dtype
         if dtype != torch.bfloat16:
@@ -81,7 +84,7 @@ class MarkovDeLSGraphRunner:
         self._alpha = torch.tensor(self.alpha_values, dtype=torch.float32, device=device)
         self._beta = torch.tensor(self.beta_values, dtype=torch.float32, device=device)
         self._tokens = torch.zeros(S, B, dtype=torch.long, device=device)
-        self._s_scaled = torch.zeros(B, self.rank, dtype=dtype, device=device)
+        self._s_scaled = torch.zeros(B, self._r, dtype=dtype, device=device)
         self._keys = torch.empty(B, dtype=torch.int64, device=device)
         self._ws = ops.Workspace(1 << 12, device)
         self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]

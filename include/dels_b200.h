@@ -231,6 +231,33 @@ DELS_API int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_str
                                           int64_t* keys, void* ws, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * Domino draft-correction rollout (code/kernel/domino.py:232-520).  Per step the
+ * correction MLP's logits are alpha * (SiLU(z_t + W_s h) . fc2^T + b2) + base_t; the
+ * step runs dels_correction_mid_bf16 (below), then dels_fused_argmax_base_bf16 with
+ * Vr = fc2 [V, M], prior = b2 as fp32 and beta = -alpha (so -beta * prior = alpha * b2),
+ * then dels_gru_step_bf16 on the chosen token.
+ * --------------------------------------------------------------------------------- */
+
+/* F.linear with an optional bias (code/kernel/domino.py:404-408 z = F.linear(hiddens,
+ * W_z, b1); :325-327 and code/kernel/dels.py:265-268, the GRU input table):
+ *   out[row] = bf16(x[row] . w^T + bias)     x [rows, K], w [N, K], bias [N] bf16 or NULL,
+ * one rounding of the fp32 accumulator (bias included), like the bf16 GEMM's bias
+ * epilogue.  tcgen05 split-K GEMM with deterministic fp32 partials in ws, then the
+ * finalisation.  ws >= dels_linear_workspace_bytes(rows, K, N). */
+DELS_API size_t dels_linear_workspace_bytes(int rows, int K, int N);
+DELS_API int dels_linear_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias, int rows,
+                              int K, int N, void* out, int64_t ld_out, void* ws, size_t ws_bytes, void* stream);
+
+/* The correction MLP's hidden layer for one step (code/kernel/domino.py:422 s_proj =
+ * F.linear(h, W_s); :92-97 SiLU(z + s) in fp32; :113 the guidance alpha):
+ *   s = bf16(W_s . h[b]),  mid = SiLU(z[b] + s) (fp32),  s_scaled[b] = bf16(alpha[0] * mid),
+ * h [B, G], W_s [M, G], z [B, M] (row stride ld_z), keys[0..B) reset.  G % 8 == 0.
+ * ws (optional) supplies the counter that the following scorer call expects at zero. */
+DELS_API int dels_correction_mid_bf16(const void* h, int64_t ld_h, const void* w_s, int64_t ld_ws, const void* z,
+                                      int64_t ld_z, int B, int G, int M, const float* alpha, void* s_scaled,
+                                      int64_t* keys, void* ws, void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Allocation-free variant of dels_draft_score_bf16 (no counterpart in the reference).
  * For callers that cannot hand the library device memory — an FFI host without a
  * device allocator, or a serving engine whose memory pool already owns the device —

@@ -413,6 +413,74 @@ def markov_runner_rollout(
     return out, gaps
 
 
+def domino_runner_rollout(
+    prefix_ids: np.ndarray,
+    hiddens: np.ndarray,
+    base_logits: np.ndarray,
+    *,
+    embed: np.ndarray,
+    w_ih: np.ndarray,
+    w_hh: np.ndarray,
+    b_ih: np.ndarray | None,
+    b_hh: np.ndarray | None,
+    w1: np.ndarray,
+    b1: np.ndarray | None,
+    fc2: np.ndarray,
+    b2: np.ndarray | None,
+    alpha: float,
+    bf16: bool = False,
+) -> tuple[np.ndarray, np.ndarray]:
+    """Greedy Domino correction rollout of DraftCorrectionGraphRunner._forward_impl
+    (code/kernel/domino.py:399-451) with the fused step of :57-139:
+
+      z      = F.linear(hiddens, W_z, b1)                 W_z = w1[:, :H]   (:404-408)
+      h      = GRU over the prefix tokens from h = 0       (:410-414)
+      per step t:
+        s    = F.linear(h, W_s)                            W_s = w1[:, H:]   (:422)
+        mid  = SiLU(z_t + s)                               fp32 in the kernel (:92-97)
+        logit= alpha * (mid . fc2^T + b2) + base_t         (:104-121)
+        tok  = argmax (first index)                        (:123-173)
+        h    = GRUCell(table[tok], h), table = F.linear(embed, W_ih, b_ih)  (:436-447)
+
+    With ``bf16=True`` the tensors the reference keeps in bf16 are rounded (z, the
+    table, gh = F.linear(h, W_hh, b_hh), the GRU state, s) and the fused step is exact.
+    Returns tokens [B, steps] and per-step top-2 gaps [B, steps]."""
+    rnd = bf16_round if bf16 else (lambda a: np.asarray(a, np.float64))
+    f64 = lambda a: np.asarray(a, np.float64)  # noqa: E731
+    B, steps, H = hiddens.shape
+    G = w_hh.shape[1]
+    z = f64(rnd((f64(hiddens) @ f64(w1)[:, :H].T + (0.0 if b1 is None else f64(b1))).astype(np.float32)))
+    w_s = f64(w1)[:, H:]
+
+    def table_rows(tok):  # rows of F.linear(embed, W_ih, b_ih), only those gathered
+        gi = f64(embed)[np.asarray(tok)] @ f64(w_ih).T + (0.0 if b_ih is None else f64(b_ih))
+        return f64(rnd(gi.astype(np.float32)))
+
+    def advance(tok, h):
+        gh = f64(rnd((h @ f64(w_hh).T + (0.0 if b_hh is None else f64(b_hh))).astype(np.float32)))
+        return f64(rnd(gru_cell(table_rows(tok), gh, h).astype(np.float32)))
+
+    h = np.zeros((B, G))
+    for p in range(np.asarray(prefix_ids).shape[1]):
+        h = advance(np.asarray(prefix_ids)[:, p], h)
+    out = np.zeros((B, steps), dtype=np.int64)
+    gaps = np.zeros((B, steps))
+    for t in range(steps):
+        s = f64(rnd((h @ w_s.T).astype(np.float32)))
+        pre = z[:, t] + s
+        mid = pre / (1.0 + np.exp(-pre))
+        logit = mid @ f64(fc2).T
+        if b2 is not None:
+            logit = logit + f64(b2)[None, :]
+        sc = float(alpha) * logit + f64(base_logits[:, t])
+        tok = argmax_first(sc)
+        out[:, t] = tok
+        gaps[:, t] = top2_gap(sc)
+        if t + 1 < steps:
+            h = advance(tok, h)
+    return out, gaps
+
+
 def iter_seeded(seed: int) -> np.random.Generator:
     return np.random.default_rng(seed)
 

@@ -18,6 +18,9 @@ What runs, and from where in the reference:
     end to end on the CPU: their CUDA stream / graph calls are replaced by stand-ins
     that run the captured function eagerly, and the Triton kernels are disabled, so the
     runners execute their own torch fallback path (code/kernel/dels.py:447-456);
+  * ``kernel.domino.DraftCorrectionGraphRunner`` (code/kernel/domino.py:232-520) on the CPU
+    the same way: its torch path in fp32 and bf16 (Triton disabled), and its fused
+    Triton step (code/kernel/domino.py:57-229) run by Triton's CPU interpreter in bf16;
   * the acceptance expression of code/dflash.py:645-651, evaluated with torch exactly as
     written there;
   * the checkpoint loaders of code/dels.py (``detect_local_head_checkpoint_kind``,
@@ -272,6 +275,98 @@ def gen_runners(ref) -> None:
     np.savez_compressed(HERE / "runners.npz", **arrays)
 
 
+# ------------------------------------------------------------------------------ Domino
+class _DominoDraft(nn.Module):
+    """The Domino correction parts of the reference draft model (code/dflash.py:262-276)."""
+
+    def __init__(self, H: int, G: int, M: int, V: int, bias: bool):
+        super().__init__()
+        self.prefix_gru = nn.GRU(input_size=H, hidden_size=G, num_layers=1, batch_first=True, bias=bias)
+        self.embed_proj = nn.Sequential(nn.Linear(H + G, M, bias=bias), nn.SiLU(), nn.Linear(M, V, bias=bias))
+
+
+DOMINO_CASES = [
+    # name, seed, B, steps, prefix tokens, V, H, G, M, biases, alpha
+    ("d1", 21, 2, 5, 2, 700, 48, 32, 24, True, 0.8),
+    ("d2", 22, 1, 6, 1, 500, 32, 16, 40, False, 1.0),
+    ("d3", 23, 3, 4, 3, 333, 40, 24, 16, True, 1.5),
+]
+
+
+def _domino_inputs(seed, B, steps, P, V, H, G, M, bias):
+    g = torch.Generator().manual_seed(seed)
+    draft = _DominoDraft(H, G, M, V, bias)
+    with torch.no_grad():
+        for prm in draft.parameters():
+            prm.copy_(bf16_values(torch.randn(prm.shape, generator=g) * 0.3))
+    embed = bf16_values(torch.randn(V, H, generator=g) * 0.5)
+    hiddens = bf16_values(torch.randn(B, steps, H, generator=g))
+    base = bf16_values(torch.randn(B, steps, V, generator=g))
+    prefix = torch.randint(0, V, (B, P), generator=g)
+    return draft, embed, hiddens, base, prefix
+
+
+def _domino_run(module, case, dtype):
+    name, seed, B, steps, P, V, H, G, M, bias, alpha = case
+    draft, embed, hiddens, base, prefix = _domino_inputs(seed, B, steps, P, V, H, G, M, bias)
+    draft = draft.to(dtype)
+    target = types.SimpleNamespace(model=types.SimpleNamespace(embed_tokens=nn.Embedding(V, H)))
+    with torch.no_grad():
+        target.model.embed_tokens.weight.copy_(embed)
+    target.model.embed_tokens = target.model.embed_tokens.to(dtype)
+    with cpu_graph_standins():
+        runner = module.DraftCorrectionGraphRunner(
+            draft_model=draft, target_model=target, batch_size=B, steps=steps, hidden_dim=H, gru_hidden_dim=G,
+            vocab_size=V, prefix_token_count=P, device=torch.device("cpu"), guidance_alpha=alpha,
+        )
+    runner.graph.replay = runner._forward_impl
+    return runner(prefix, hiddens.to(dtype), base.to(dtype), alpha).numpy(), runner._can_triton_fuse
+
+
+def domino_fused_worker(out_path: str) -> None:
+    """Run in a process started with TRITON_INTERPRET=1 (the interpreter must be chosen
+    before triton is first imported): the fused Triton step on the CPU, bf16."""
+    import kernel.domino as interp  # noqa: E402
+
+    arrays = {}
+    for case in DOMINO_CASES:
+        tokens, fused = _domino_run(interp, case, torch.bfloat16)
+        assert fused, "the Triton path was not taken"
+        arrays[f"{case[0]}_tokens_bf16_fused"] = tokens
+    np.savez(out_path, **arrays)
+
+
+def gen_domino(ref, reference_dir: Path) -> None:
+    import os
+    import subprocess
+
+    arrays: dict[str, np.ndarray] = {}
+    meta = []
+    ref.kernel_domino.HAS_TRITON = False
+    for case in DOMINO_CASES:
+        name, seed, B, steps, P, V, H, G, M, bias, alpha = case
+        draft, embed, hiddens, base, prefix = _domino_inputs(seed, B, steps, P, V, H, G, M, bias)
+        for k, t in (("embed", embed), ("hiddens", hiddens), ("base", base)):
+            arrays[f"{name}_{k}"] = f32(t)
+        arrays[f"{name}_prefix"] = prefix.numpy()
+        for k, t in draft.named_parameters():
+            arrays[f"{name}_{k.replace('.', '_')}"] = f32(t)
+        for dtype, dname in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+            arrays[f"{name}_tokens_{dname}"], fused = _domino_run(ref.kernel_domino, case, dtype)
+            assert not fused
+        meta.append({"name": name, "B": B, "steps": steps, "P": P, "V": V, "H": H, "G": G, "M": M, "bias": bias,
+                     "alpha": alpha})
+    with tempfile.TemporaryDirectory() as td:
+        out = Path(td) / "fused.npz"
+        subprocess.run([sys.executable, str(Path(__file__).resolve()), "--reference", str(reference_dir),
+                        "--domino-fused-worker", str(out)], check=True, env={**os.environ, "TRITON_INTERPRET": "1"})
+        with np.load(out) as f:
+            for k in f.files:
+                arrays[k] = f[k]
+    arrays["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "domino.npz", **arrays)
+
+
 # ------------------------------------------------------------------------------ acceptance
 def gen_accept() -> None:
     g = torch.Generator().manual_seed(2)
@@ -421,22 +516,36 @@ def gen_checkpoints(ref) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="the reference checkout's code/ directory")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="generate only these groups (schedules priors scorer runners domino accept checkpoints)")
+    ap.add_argument("--domino-fused-worker", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
+    if args.domino_fused_worker:
+        torch.set_num_threads(4)
+        domino_fused_worker(args.domino_fused_worker)
+        return
     import dels as ref_dels  # noqa: E402
     import dflash as ref_dflash  # noqa: E402
     import kernel.dels as ref_kernel_dels  # noqa: E402
+    import kernel.domino as ref_kernel_domino  # noqa: E402
     import kernel.markov_dels as ref_kernel_markov  # noqa: E402
 
     ref = types.SimpleNamespace(dels=ref_dels, dflash=ref_dflash, kernel_dels=ref_kernel_dels,
-                                kernel_markov=ref_kernel_markov)
+                                kernel_markov=ref_kernel_markov, kernel_domino=ref_kernel_domino)
     torch.set_num_threads(4)
-    gen_schedules(ref)
-    gen_priors(ref)
-    gen_scorer(ref)
-    gen_runners(ref)
-    gen_accept()
-    gen_checkpoints(ref)
+    groups = {
+        "schedules": lambda: gen_schedules(ref),
+        "priors": lambda: gen_priors(ref),
+        "scorer": lambda: gen_scorer(ref),
+        "runners": lambda: gen_runners(ref),
+        "domino": lambda: gen_domino(ref, Path(args.reference)),
+        "accept": gen_accept,
+        "checkpoints": lambda: gen_checkpoints(ref),
+    }
+    for name, fn in groups.items():
+        if args.only is None or name in args.only:
+            fn()
     for p in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")) + sorted((HERE / "ckpt").glob("*")):
         print(f"{p.name}: {p.stat().st_size} bytes")
 

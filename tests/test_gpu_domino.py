@@ -1,0 +1,184 @@
+"""The drop-in Domino correction runner (kernel/domino.py) and its two new entry points
+(dels_linear_bf16, dels_correction_mid_bf16) against the oracle and the reference's own
+runner outputs (tests/golden/domino.npz: its torch path in fp32 / bf16 and its fused
+Triton step).  Needs a B200.  Token comparisons stop at the first step whose exact top-2
+gap is below the tolerance (after a legitimate near-tie greedy rollouts may part ways)."""
+
+from __future__ import annotations
+
+import json
+import types
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from oracle import dels_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+class _Draft(nn.Module):
+    def __init__(self, H, G, M, V, bias, middle=None):
+        super().__init__()
+        self.prefix_gru = nn.GRU(input_size=H, hidden_size=G, num_layers=1, batch_first=True, bias=bias)
+        self.embed_proj = nn.Sequential(nn.Linear(H + G, M, bias=bias), middle or nn.SiLU(),
+                                        nn.Linear(M, V, bias=bias))
+
+
+def _target(embed, dev):
+    V, H = embed.shape
+    t = types.SimpleNamespace(model=types.SimpleNamespace(embed_tokens=nn.Embedding(V, H)))
+    with torch.no_grad():
+        t.model.embed_tokens.weight.copy_(torch.from_numpy(np.asarray(embed)))
+    t.model.embed_tokens = t.model.embed_tokens.to(device=dev, dtype=torch.bfloat16)
+    return t
+
+
+def _compare(ours, gaps, ref, thresh):
+    n = 0
+    for b in range(ours.shape[0]):
+        for t in range(ours.shape[1]):
+            if gaps[b, t] <= thresh:
+                break
+            assert ours[b, t] == ref[b, t], (b, t, ours[b], ref[b])
+            n += 1
+    return n
+
+
+def _bf16(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev).to(torch.bfloat16)
+
+
+def test_linear_bf16_matches_oracle(cuda_device):
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(31)
+    for rows, K, N, bias in ((7, 96, 40, True), (300, 520, 200, False), (1, 64, 24, True)):
+        x = O.bf16_round(rng.standard_normal((rows, K)).astype(np.float32))
+        w = O.bf16_round((rng.standard_normal((N, K)) * 0.1).astype(np.float32))
+        b = O.bf16_round(rng.standard_normal(N).astype(np.float32)) if bias else None
+        out = ops.linear_bf16(_bf16(x, cuda_device), _bf16(w, cuda_device),
+                              _bf16(b, cuda_device) if bias else None).float().cpu().numpy()
+        acc = x.astype(np.float64) @ w.astype(np.float64).T + (0.0 if b is None else b.astype(np.float64))
+        ref = O.bf16_round(acc.astype(np.float32))
+        assert np.mean(out == ref) > 0.99  # one rounding of an fp32 accumulation
+        np.testing.assert_allclose(out, ref, rtol=2 ** -7, atol=1e-3)
+
+
+def test_correction_mid_matches_oracle(cuda_device):
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(32)
+    B, G, M, S = 5, 64, 48, 3
+    h = O.bf16_round(rng.standard_normal((B, G)).astype(np.float32))
+    w_s = O.bf16_round((rng.standard_normal((M, G)) * 0.2).astype(np.float32))
+    z = O.bf16_round(rng.standard_normal((B, S, M)).astype(np.float32))
+    alpha = 0.7
+    dev = cuda_device
+    z_t = _bf16(z, dev)
+    out = torch.empty(B, M, dtype=torch.bfloat16, device=dev)
+    keys = torch.zeros(B, dtype=torch.int64, device=dev)
+    ops.correction_mid(_bf16(h, dev), _bf16(w_s, dev), z_t[:, 1, :], torch.tensor([alpha], device=dev), out,
+                       keys=keys)
+    s = O.bf16_round((h.astype(np.float64) @ w_s.astype(np.float64).T).astype(np.float32)).astype(np.float64)
+    pre = z[:, 1, :].astype(np.float64) + s
+    ref = O.bf16_round((alpha * pre / (1.0 + np.exp(-pre))).astype(np.float32))
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, rtol=2 ** -7, atol=1e-6)
+    assert (keys.cpu().numpy() == np.iinfo(np.int64).min).all()
+
+
+def test_domino_runner_matches_reference_fixture(cuda_device, golden_dir):
+    from kernel.domino import DraftCorrectionGraphRunner
+
+    g = np.load(golden_dir / "domino.npz")
+    total = 0
+    for c in json.loads(str(g["meta"])):
+        n = c["name"]
+        draft = _Draft(c["H"], c["G"], c["M"], c["V"], c["bias"])
+        with torch.no_grad():
+            for k, prm in draft.named_parameters():
+                prm.copy_(torch.from_numpy(g[f"{n}_{k.replace('.', '_')}"]))
+        draft = draft.to(device=cuda_device, dtype=torch.bfloat16)
+        runner = DraftCorrectionGraphRunner(
+            draft_model=draft, target_model=_target(g[f"{n}_embed"], cuda_device), batch_size=c["B"],
+            steps=c["steps"], hidden_dim=c["H"], gru_hidden_dim=c["G"], vocab_size=c["V"],
+            prefix_token_count=c["P"], device=cuda_device, guidance_alpha=c["alpha"],
+        )
+        assert runner._can_triton_fuse
+        out = runner(torch.from_numpy(g[f"{n}_prefix"]).to(cuda_device), _bf16(g[f"{n}_hiddens"], cuda_device),
+                     _bf16(g[f"{n}_base"], cuda_device), c["alpha"]).cpu().numpy()
+        assert out.shape == (c["B"], c["steps"]) and out.dtype == np.int64
+        opt = (lambda k: g[f"{n}_{k}"]) if c["bias"] else (lambda k: None)
+        toks, gaps = O.domino_runner_rollout(
+            g[f"{n}_prefix"], g[f"{n}_hiddens"], g[f"{n}_base"], alpha=c["alpha"], bf16=True,
+            embed=g[f"{n}_embed"], w_ih=g[f"{n}_prefix_gru_weight_ih_l0"], w_hh=g[f"{n}_prefix_gru_weight_hh_l0"],
+            b_ih=opt("prefix_gru_bias_ih_l0"), b_hh=opt("prefix_gru_bias_hh_l0"),
+            w1=g[f"{n}_embed_proj_0_weight"], b1=opt("embed_proj_0_bias"), fc2=g[f"{n}_embed_proj_2_weight"],
+            b2=opt("embed_proj_2_bias"),
+        )
+        total += _compare(out, gaps, toks, 1e-2)
+        _compare(out, gaps, g[f"{n}_tokens_bf16_fused"], 0.05)
+        _compare(out, gaps, g[f"{n}_tokens_bf16"], 0.05)
+    assert total >= 12
+
+
+def test_domino_runner_validation_errors(cuda_device):
+    from kernel.domino import DraftCorrectionGraphRunner, unwrap_correction_mlp
+
+    with pytest.raises(TypeError, match="nn.Sequential"):
+        unwrap_correction_mlp(nn.Linear(4, 4))
+    with pytest.raises(ValueError, match="at least two layers"):
+        unwrap_correction_mlp(nn.Sequential(nn.Linear(4, 4)))
+    with pytest.raises(ValueError, match="first layer"):
+        unwrap_correction_mlp(nn.Sequential(nn.SiLU(), nn.Linear(4, 4)))
+    with pytest.raises(ValueError, match="last layer"):
+        unwrap_correction_mlp(nn.Sequential(nn.Linear(4, 4), nn.SiLU()))
+    embed = O.bf16_round(np.random.default_rng(0).standard_normal((64, 16)).astype(np.float32))
+    kw = dict(target_model=_target(embed, cuda_device), batch_size=1, steps=2, hidden_dim=16, gru_hidden_dim=8,
+              vocab_size=64, prefix_token_count=1, device=cuda_device)
+    with pytest.raises(ValueError, match="input dim mismatch"):
+        DraftCorrectionGraphRunner(draft_model=_Draft(16, 8, 12, 64, False).to(cuda_device, torch.bfloat16),
+                                   **{**kw, "gru_hidden_dim": 4})
+    with pytest.raises(ValueError, match="SiLU"):
+        DraftCorrectionGraphRunner(draft_model=_Draft(16, 8, 12, 64, False, nn.ReLU()).to(cuda_device, torch.bfloat16),
+                                   **kw)
+    with pytest.raises(ValueError, match="bf16"):
+        DraftCorrectionGraphRunner(draft_model=_Draft(16, 8, 12, 64, False).to(cuda_device), **kw)
+    runner = DraftCorrectionGraphRunner(draft_model=_Draft(16, 8, 12, 64, False).to(cuda_device, torch.bfloat16),
+                                        guidance_alpha=0.5, **kw)
+    with pytest.raises(ValueError, match="fixed domino guidance alpha"):
+        runner(torch.zeros(1, 1, dtype=torch.long, device=cuda_device),
+               torch.zeros(1, 2, 16, dtype=torch.bfloat16, device=cuda_device),
+               torch.zeros(1, 2, 64, dtype=torch.bfloat16, device=cuda_device), 0.25)
+
+
+def test_domino_runner_full_vocab(cuda_device):
+    """Full vocabulary (151936), batch 2, 8 steps, 2 prefix tokens, against the oracle."""
+    from kernel.domino import DraftCorrectionGraphRunner
+
+    V, H, G, M, B, S, P, alpha = 151936, 1024, 512, 512, 2, 8, 2, 1.0
+    gen = torch.Generator(device="cpu").manual_seed(41)
+    draft = _Draft(H, G, M, V, False)
+    with torch.no_grad():
+        for prm in draft.parameters():
+            prm.copy_((torch.randn(prm.shape, generator=gen) * 0.05).to(torch.bfloat16).float())
+    embed = (torch.randn(V, H, generator=gen) * 0.5).to(torch.bfloat16).float().numpy()
+    hiddens = (torch.randn(B, S, H, generator=gen)).to(torch.bfloat16).float().numpy()
+    base = (torch.randn(B, S, V, generator=gen)).to(torch.bfloat16).float().numpy()
+    prefix = torch.randint(0, V, (B, P), generator=gen).numpy()
+    params = {k.replace(".", "_"): p.detach().numpy().copy() for k, p in draft.named_parameters()}
+    runner = DraftCorrectionGraphRunner(
+        draft_model=draft.to(cuda_device, torch.bfloat16), target_model=_target(embed, cuda_device), batch_size=B,
+        steps=S, hidden_dim=H, gru_hidden_dim=G, vocab_size=V, prefix_token_count=P, device=cuda_device,
+        guidance_alpha=alpha,
+    )
+    out = runner(torch.from_numpy(prefix).to(cuda_device), _bf16(hiddens, cuda_device),
+                 _bf16(base, cuda_device)).cpu().numpy()
+    toks, gaps = O.domino_runner_rollout(
+        prefix, hiddens, base, alpha=alpha, bf16=True, embed=embed, w_ih=params["prefix_gru_weight_ih_l0"],
+        w_hh=params["prefix_gru_weight_hh_l0"], b_ih=None, b_hh=None, w1=params["embed_proj_0_weight"], b1=None,
+        fc2=params["embed_proj_2_weight"], b2=None,
+    )
+    assert _compare(out, gaps, toks, 1e-2) >= 4

@@ -178,3 +178,46 @@ def test_fused_long_logit_runner_matches_oracle(cuda_device):
                                        w_rank=w["w_rank"], Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta,
                                        activation="silu", bf16=True)
     assert _compare(out, gaps, toks, 1e-2) >= 3
+
+
+def test_runners_odd_widths(cuda_device):
+    """Rank width 12 and embedding width 20 (not multiples of 8): the runners carry them
+    zero-padded; results must still match the oracle."""
+    from kernel.dels import DeLSGraphRunner
+    from kernel.markov_dels import MarkovDeLSGraphRunner
+
+    import dels as D
+
+    rng = np.random.default_rng(77)
+    V, E, G, r, B, steps = 900, 20, 24, 12, 2, 5
+    w = {
+        "embed": O.bf16_round((rng.standard_normal((V, E)) * 0.5).astype(np.float32)),
+        "w_ih": O.bf16_round((rng.standard_normal((3 * G, E)) * 0.2).astype(np.float32)),
+        "w_hh": O.bf16_round((rng.standard_normal((3 * G, G)) * 0.2).astype(np.float32)),
+        "w_rank": O.bf16_round((rng.standard_normal((r, G)) * 0.3).astype(np.float32)),
+        "Vr": O.bf16_round((rng.standard_normal((V, r)) * 0.3).astype(np.float32)),
+    }
+    base = O.bf16_round(rng.standard_normal((B, steps, V)).astype(np.float32))
+    prefix = rng.integers(0, V, (B, 1))
+    alpha = [0.9, 0.8, 0.7, 0.6, 0.5]
+    beta = [0.0] * steps
+    head = _head(cuda_device, V, E, G, r, "silu", w)
+    runner = DeLSGraphRunner(local_head=head, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha,
+                             beta_values=beta, baseline_logits=None, device=cuda_device)
+    out = runner(torch.from_numpy(prefix).to(cuda_device),
+                 torch.from_numpy(base).to(cuda_device).to(torch.bfloat16)).cpu().numpy()
+    toks, gaps = O.dels_runner_rollout(prefix, base, embed=w["embed"], w_ih=w["w_ih"], w_hh=w["w_hh"],
+                                       w_rank=w["w_rank"], Vr=w["Vr"], prior=None, alpha=alpha, beta=beta,
+                                       activation="silu", bf16=True)
+    assert _compare(out, gaps, toks, 1e-2) >= 5
+    emb_r = O.bf16_round((rng.standard_normal((V, r)) * 0.5).astype(np.float32))
+    mhead = D.MarkovDeLSLocalHead(embedding_weight=torch.from_numpy(emb_r).to(torch.bfloat16),
+                                  lm_head_weight=torch.from_numpy(w["Vr"]).to(torch.bfloat16), dtype=torch.bfloat16,
+                                  device=cuda_device)
+    mrunner = MarkovDeLSGraphRunner(local_head=mhead, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha,
+                                    beta_values=beta, baseline_logits=None, device=cuda_device)
+    mout = mrunner(torch.from_numpy(prefix).to(cuda_device),
+                   torch.from_numpy(base).to(cuda_device).to(torch.bfloat16)).cpu().numpy()
+    mtoks, mgaps = O.markov_runner_rollout(prefix, base, embedding=emb_r, lm_head=w["Vr"], prior=None, alpha=alpha,
+                                           beta=beta)
+    assert _compare(mout, mgaps, mtoks, 1e-2) >= 5

@@ -150,6 +150,32 @@ def test_markov_runner_matches_reference(golden_dir, mode):
     assert total >= 20
 
 
+def domino_params(g, n, bias):
+    """Oracle keyword arguments for Domino case n of tests/golden/domino.npz."""
+    opt = (lambda k: g[f"{n}_{k}"]) if bias else (lambda k: None)
+    return dict(
+        embed=g[f"{n}_embed"], w_ih=g[f"{n}_prefix_gru_weight_ih_l0"], w_hh=g[f"{n}_prefix_gru_weight_hh_l0"],
+        b_ih=opt("prefix_gru_bias_ih_l0"), b_hh=opt("prefix_gru_bias_hh_l0"), w1=g[f"{n}_embed_proj_0_weight"],
+        b1=opt("embed_proj_0_bias"), fc2=g[f"{n}_embed_proj_2_weight"], b2=opt("embed_proj_2_bias"),
+    )
+
+
+@pytest.mark.parametrize("mode", ["f32", "bf16", "bf16_fused"])
+def test_domino_runner_matches_reference(golden_dir, mode):
+    """DraftCorrectionGraphRunner (code/kernel/domino.py:232-520): the torch path in fp32 /
+    bf16 and the fused Triton step (run by Triton's CPU interpreter) against the oracle."""
+    g = _load(golden_dir, "domino.npz")
+    total = 0
+    for c in _runner_cases(g):
+        n = c["name"]
+        toks, gaps = O.domino_runner_rollout(
+            g[f"{n}_prefix"], g[f"{n}_hiddens"], g[f"{n}_base"], alpha=c["alpha"], bf16=(mode != "f32"),
+            **domino_params(g, n, c["bias"]),
+        )
+        total += _compare_rollout(toks, gaps, g[f"{n}_tokens_{mode}"], 1e-5 if mode == "f32" else 0.05)
+    assert total >= 12
+
+
 def test_accept_matches_reference(golden_dir):
     g = _load(golden_dir, "accept.npz")
     draft = g["verify"][:, 1:]
