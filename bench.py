@@ -11,7 +11,9 @@ Workloads (seeded synthetic inputs, see dels_b200.workloads):
     V = 151936 (the configuration the headline metric is quoted on);
   * N > 1 default: the vocab-sharded large batch, 16384 rows, each rank owning a
     contiguous vocabulary slice of W / Vr / prior (strong scaling: total work fixed);
-  * ``--workload cfg1|cfg2|cfg3|cfg4|cfg5`` selects any of the five explicitly.
+  * ``--workload cfg1|cfg2|cfg3|cfg4|cfg5`` selects any of the five explicitly;
+  * ``--workload runner|domino`` times the drop-in rollout runners (DeLSGraphRunner,
+    DraftCorrectionGraphRunner) call by call, batch ``--runner-batch``.
 
 ``value`` is device-timed (CUDA events, max over ranks) with inputs resident in HBM;
 ``e2e`` is the same metric through the public API with the step's input rows copied
@@ -337,6 +339,8 @@ def run_ours(args, rank, world, dev):
         return run_rnn(args, rank, world, dev)
     elif wname == "runner":
         return run_runner(args, rank, world, dev)
+    elif wname == "domino":
+        return run_domino(args, rank, world, dev)
     else:
         raise SystemExit(f"unknown workload {wname}")
 
@@ -621,6 +625,99 @@ def run_runner(args, rank, world, dev):
     return res
 
 
+def run_domino(args, rank, world, dev):
+    """The drop-in Domino DraftCorrectionGraphRunner (kernel/domino.py) at Qwen3-8B target
+    shapes (V = 151936, H = 4096) with GRU and correction-MLP widths G = M = 1024 (the
+    reference fixes no released width), batch B, 14 suffix steps, 2 prefix tokens: one call
+    = copy-in of prefix ids, draft hiddens and base logits, graph replay, clone of the tokens
+    (code/kernel/domino.py:499-520)."""
+    import torch.nn as nn
+
+    from kernel.domino import DraftCorrectionGraphRunner
+    from dels_b200 import workloads
+
+    if world > 1:
+        raise SystemExit("the domino workload is single-GPU")
+    V, H, G, M, steps, P, B, alpha = workloads.VOCAB, 4096, 1024, 1024, 14, 2, args.runner_batch, 1.0
+    g = torch.Generator(device=dev)
+    g.manual_seed(6)
+
+    class Draft(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.prefix_gru = nn.GRU(input_size=H, hidden_size=G, num_layers=1, batch_first=True, bias=False)
+            self.embed_proj = nn.Sequential(nn.Linear(H + G, M, bias=False), nn.SiLU(), nn.Linear(M, V, bias=False))
+
+    draft = Draft().to(device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for p in draft.parameters():
+            p.copy_(torch.randn(p.shape, generator=g, device=dev) * 0.02)
+    stub = type("T", (), {})()
+    stub.model = type("M", (), {})()
+    stub.model.embed_tokens = nn.Embedding(V, H).to(device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        stub.model.embed_tokens.weight.copy_(torch.randn(V, H, generator=g, device=dev) * 0.02)
+    runner = DraftCorrectionGraphRunner(draft_model=draft, target_model=stub, batch_size=B, steps=steps,
+                                        hidden_dim=H, gru_hidden_dim=G, vocab_size=V, prefix_token_count=P,
+                                        device=dev, guidance_alpha=alpha)
+    hiddens = torch.randn(B, steps, H, generator=g, device=dev).to(torch.bfloat16)
+    base = torch.randn(B, steps, V, generator=g, device=dev).to(torch.bfloat16)
+    prefix = torch.randint(0, V, (B, P), generator=g, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    call = lambda: runner(prefix, hiddens, base)  # noqa: E731
+    clocks = ClockSampler(dev)
+    ms = timed(call, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
+    clk = clocks.stop()
+    host = [t.cpu().pin_memory() for t in (prefix, hiddens, base)]
+    tok_host = torch.empty(B, steps, dtype=torch.int64).pin_memory()
+
+    def e2e_call():
+        out = runner(*(t.to(dev, non_blocking=True) for t in host))
+        tok_host.copy_(out, non_blocking=True)
+
+    ms_e2e = timed(e2e_call, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0)
+    _, pk_gbs, pk_src = peaks()
+    # per step: fc2 [V, M], W_s [M, G], W_hh [3G, G], base row, table rows; per call: W_z, hiddens,
+    # the prefix GRU steps and the copy-in of the base logits (read + write)
+    per_step = (V * M + M * G + 3 * G * G + B * V + B * 3 * G) * 2
+    bytes_call = steps * per_step + (M * H + B * steps * H + P * (3 * G * G + B * 3 * G)) * 2 + B * steps * V * 4
+    achieved = bytes_call / (ms / args.steps * 1e-3) / 1e9
+    rows = B * steps
+    res = {
+        "metric": METRIC, "value": rows * args.steps / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, random-init Domino head; G = M = 1024 assumed)",
+        "config": {"workload": f"domino_b{B}_steps{steps}", "V": V, "H": H, "G": G, "M": M, "prefix_tokens": P,
+                   "note": "one step = one DraftCorrectionGraphRunner call (14 scored positions per sequence)"},
+        "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
+                "d2h_bytes_per_step": B * steps * 8},
+        "gpu_launches": (2 + P + 3 * steps - 1) * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
+                     "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call},
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        from oracle.reference_torch import domino_rollout
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu = lambda t: t.detach().cpu()  # noqa: E731
+        w1 = cpu(draft.embed_proj[0].weight)
+        table = torch.nn.functional.linear(stub.model.embed_tokens.weight, draft.prefix_gru.weight_ih_l0).cpu()
+        cpu_args = (prefix[:1].cpu(), hiddens[:1].cpu(), base[:1].cpu(), table, cpu(draft.prefix_gru.weight_hh_l0),
+                    w1[:, :H].contiguous(), w1[:, H:].contiguous(), cpu(draft.embed_proj[2].weight), alpha)
+        domino_rollout(*cpu_args)
+        t0 = time.perf_counter()
+        reps = 2
+        for _ in range(reps):
+            domino_rollout(*cpu_args)
+        dt = (time.perf_counter() - t0) / reps
+        res["cpu_baseline"] = {"value": steps / dt, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+                               "sample": "one batch-1 rollout of 14 steps x 2 repetitions, bf16 torch on the host"}
+    return res
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, dev):
     """The reference's CPU formula on the host cores, same workload / metric / unit."""
@@ -659,7 +756,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="auto", choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "runner"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "runner", "domino"])
     ap.add_argument("--runner-batch", type=int, default=1, help="batch of the runner workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

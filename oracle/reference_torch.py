@@ -64,3 +64,33 @@ def runner_rollout(prefix_ids, base_logits, table, w_hh, w_rank, Vr, prior, alph
         if step + 1 < steps:
             h = cell(table[tok], h)
     return out
+
+
+def domino_rollout(prefix_ids, hiddens, base_logits, table, w_hh, w_z, w_s, fc2, alpha) -> torch.Tensor:
+    """DraftCorrectionGraphRunner._forward_impl's torch path (code/kernel/domino.py:399-451,
+    bias-free released head: SiLU middle, GRU without biases), on the host."""
+    B, steps, _ = base_logits.shape
+    G = w_hh.shape[1]
+    z_all = F.linear(hiddens, w_z)
+    h = torch.zeros(B, G, dtype=base_logits.dtype)
+
+    def cell(gi, h):
+        gh = F.linear(h, w_hh)
+        i_r, i_z, i_n = gi.chunk(3, dim=-1)
+        h_r, h_z, h_n = gh.chunk(3, dim=-1)
+        r = torch.sigmoid(i_r + h_r)
+        z = torch.sigmoid(i_z + h_z)
+        n = torch.tanh(i_n + r * h_n)
+        return (1.0 - z) * n + z * h
+
+    for p in range(prefix_ids.shape[1]):
+        h = cell(table[prefix_ids[:, p]], h)
+    out = torch.empty(B, steps, dtype=torch.long)
+    for t in range(steps):
+        mid = F.silu(z_all[:, t, :] + F.linear(h, w_s))
+        logits = base_logits[:, t, :] + alpha * F.linear(mid, fc2)
+        tok = torch.argmax(logits, dim=-1)
+        out[:, t] = tok
+        if t + 1 < steps:
+            h = cell(table[tok], h)
+    return out
