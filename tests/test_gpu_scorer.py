@@ -200,33 +200,44 @@ def test_draft_score_f32_matches_oracle(cuda_device, golden_dir):
         _check_tokens(out.tokens.cpu().numpy(), out.scores.cpu().numpy(), g[f"{n}_final_f32"], F32_TOL)
 
 
-def test_edge_cases(cuda_device):
+@pytest.mark.parametrize("rows", [3, 40, 150], ids=["skinny", "tile", "pair"])
+def test_edge_cases(cuda_device, rows):
     from dels_b200 import ops, _lib
 
     dev = cuda_device
     # all-equal scores: lowest index wins
-    rows, H, r, V = 3, 64, 64, 777
+    H, r, V = 64, 64, 5000
     h = torch.zeros(rows, H, dtype=torch.bfloat16, device=dev)
     W = torch.zeros(V, H, dtype=torch.bfloat16, device=dev)
     Ut = torch.zeros(r, H, dtype=torch.bfloat16, device=dev)
     Vr = torch.zeros(V, r, dtype=torch.bfloat16, device=dev)
     a = torch.ones(1, device=dev)
     out = ops.draft_score_bf16(h, W, Ut, Vr, None, a, a, with_scores=True)
-    assert out.tokens.tolist() == [0, 0, 0]
-    # planted ties in different vocabulary tiles: the lower index wins
+    assert out.tokens.tolist() == [0] * rows
+    # planted ties in vocabulary tiles owned by different CTAs: the lower index wins
     W2 = torch.zeros(V, H, dtype=torch.bfloat16, device=dev)
-    W2[700, 0] = 1.0
-    W2[300, 0] = 1.0
+    W2[4700, 0] = 1.0
+    W2[3001, 0] = 1.0
     W2[5, 0] = 0.5
     h2 = torch.zeros(rows, H, dtype=torch.bfloat16, device=dev)
     h2[:, 0] = 1.0
     out = ops.draft_score_bf16(h2, W2, Ut, Vr, None, a, a, with_scores=True)
-    assert out.tokens.tolist() == [300, 300, 300]
+    assert out.tokens.tolist() == [3001] * rows
+    assert out.scores.tolist() == [1.0] * rows
+    # NaN scores win, and the first NaN index among them (torch.argmax)
+    W3 = W2.clone()
+    W3[4100, 1] = float("nan")
+    W3[3900, 1] = float("nan")
+    h3 = h2.clone()
+    h3[:, 1] = 1.0
+    out = ops.draft_score_bf16(h3, W3, Ut, Vr, None, a, a, with_scores=True)
+    assert out.tokens.tolist() == [3900] * rows
+    assert torch.isnan(out.scores).all()
     # a prior of -inf everywhere but one token (beta < 0 makes it +inf there)
     prior = torch.full((V,), 0.0, device=dev)
     prior[613] = -1.0
     out = ops.draft_score_bf16(h2, W2, Ut, Vr, prior, a, torch.full((1,), 5.0, device=dev), with_scores=True)
-    assert out.tokens.tolist() == [613] * 3
+    assert out.tokens.tolist() == [613] * rows
     # zero rows is a no-op
     e = ops.draft_score_bf16(h2[:0], W2, Ut, Vr, None, a, a)
     assert e.tokens.numel() == 0
