@@ -275,7 +275,7 @@ def run_ours(args, rank, world, dev):
         out = ops.ScoreOut(tokens=torch.empty(rows, dtype=torch.int64, device=dev), scores=None,
                            keys=torch.empty(rows, dtype=torch.int64, device=dev))
         need = ops._lib.query("dels_score_f32_workspace_bytes" if fp32 else "dels_score_workspace_bytes",
-                              *((rows, r) if fp32 else (rows, H, r)))
+                              rows, H, r)
         ws = ops.Workspace(need, dev)
         score = ops.draft_score_f32 if fp32 else ops.draft_score_bf16
 

@@ -60,7 +60,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _I64, _I, _P, _P, _P, _P,
          _SZ, _P],
     ),
-    "dels_score_f32_workspace_bytes": (_SZ, [_I, _I]),
+    "dels_score_f32_workspace_bytes": (_SZ, [_I, _I, _I]),
     "dels_draft_score_f32": (
         _I,
         [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I64, _P, _P, _P, _P, _SZ,

@@ -127,13 +127,13 @@ int make_map_bf16(CUtensorMap* m, const void* ptr, long long inner, long long ou
   return DELS_OK;
 }
 
-// 2-D fp32 tensor map, box = [box_outer rows, 32 elements] (128 bytes), optional
+// 2-D fp32 tensor map, box = [box_outer rows, box_inner elements] (32 = 128 bytes), optional
 // 128-byte swizzle, zero fill outside the extents.
 int make_map_f32(CUtensorMap* m, const void* ptr, long long inner, long long outer, long long ld, int box_outer,
-                 bool swizzle) {
+                 bool swizzle, int box_inner = 32) {
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {32u, (cuuint32_t)box_outer};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -202,6 +202,7 @@ int init_device(int dev) {
     SET(accept_offsets_kernel, 0);
     SET(pack_rows_kernel, 0);
     SET(f32_rank_kernel, 0);
+    SET(f32_transpose_pass_kernel, 0);
     SET(gru_step_kernel, kMaxSmem);
     SET(rank_gemv_kernel, kMaxSmem);
     SET(linear_finalize_kernel, 0);
@@ -696,9 +697,11 @@ int dels_draft_score_bf16(const void* h, int64_t ld_h, const void* W, int64_t ld
                              ws_bytes, st);
 }
 
-size_t dels_score_f32_workspace_bytes(int rows, int r) {
-  if (rows <= 0 || r <= 0) return DELS_WS_HEADER_BYTES;
-  return DELS_WS_HEADER_BYTES + align256((size_t)rows * 8) + align256((size_t)rows * r * 4);
+size_t dels_score_f32_workspace_bytes(int rows, int H, int r) {
+  if (rows <= 0 || H <= 0 || r <= 0) return DELS_WS_HEADER_BYTES;
+  // keys, s' = alpha * s, and one pass's rows transposed ([H][16] and [r][16])
+  return DELS_WS_HEADER_BYTES + align256((size_t)rows * 8) + align256((size_t)rows * r * 4) +
+         align256((size_t)H * 16 * 4) + align256((size_t)r * 16 * 4);
 }
 
 int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t ld_w, const float* w_rank,
@@ -718,7 +721,7 @@ int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t l
   const int have_keys = 1;
   if ((rc = check_common_score_args(rows, V, v_begin, beta, prior, n_pos, &have_keys)) != DELS_OK) return rc;
   WsHeader hdr;
-  if ((rc = ws_header(ws, ws_bytes, dels_score_f32_workspace_bytes(rows, r), &hdr)) != DELS_OK) return rc;
+  if ((rc = ws_header(ws, ws_bytes, dels_score_f32_workspace_bytes(rows, H, r), &hdr)) != DELS_OK) return rc;
   DeviceState* ds = nullptr;
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (rows == 0) return DELS_OK;
@@ -728,6 +731,8 @@ int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t l
   char* base = reinterpret_cast<char*>(ws);
   if (keys == nullptr) keys = reinterpret_cast<int64_t*>(base + DELS_WS_HEADER_BYTES);
   float* s_scaled = reinterpret_cast<float*>(base + DELS_WS_HEADER_BYTES + align256((size_t)rows * 8));
+  float* hT = reinterpret_cast<float*>(reinterpret_cast<char*>(s_scaled) + align256((size_t)rows * r * 4));
+  float* sT = reinterpret_cast<float*>(reinterpret_cast<char*>(hT) + align256((size_t)H * 16 * 4));
 
   {
     const int warps = rows * r;
@@ -742,11 +747,19 @@ int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t l
   if ((rc = make_map_f32(&mw, W, H, V, ld_w, 64, true)) != DELS_OK) return rc;
   if ((rc = make_map_f32(&mvr, Vr, r, V, ld_vr, 64, true)) != DELS_OK) return rc;
   const int kb0 = cdiv(H, 64), kb1 = cdiv(r, 64);
+  // the transposed pass buffers: [k][16] rows, 32 k per box
+  CUtensorMap mh, ms;
+  if ((rc = make_map_f32(&mh, hT, 16, H, 16, 32, false, 16)) != DELS_OK) return rc;
+  if ((rc = make_map_f32(&ms, sT, 16, r, 16, 32, false, 16)) != DELS_OK) return rc;
   for (int row0 = 0; row0 < rows; row0 += 16) {
     const int nrows = rows - row0 < 16 ? rows - row0 : 16;
-    CUtensorMap mh, ms;
-    if ((rc = make_map_f32(&mh, h + (long long)row0 * ld_h, H, nrows, ld_h, 16, false)) != DELS_OK) return rc;
-    if ((rc = make_map_f32(&ms, s_scaled + (long long)row0 * r, r, nrows, r, 16, false)) != DELS_OK) return rc;
+    {
+      const long long total = (long long)(H + r) * 16;
+      const int grid = (int)(cdiv(total, 256) < 2 * ds->sm_count ? cdiv(total, 256) : 2 * ds->sm_count);
+      f32_transpose_pass_kernel<<<grid, 256, 0, st>>>(h + (long long)row0 * ld_h, ld_h, H,
+                                                      s_scaled + (long long)row0 * r, r, r, nrows, hT, sT);
+      DELS_CHECK_LAUNCH("f32_transpose_pass_kernel launch");
+    }
     cudaError_t e = f32_score_launch(ds->sm_count, st, mw, mh, mvr, ms, kb0, kb1, prior, beta, n_pos, row_pos, row0,
                                      nrows, V, v_begin, reinterpret_cast<long long*>(keys), hdr.status);
     if (e != cudaSuccess) return cuda_fail(e, "f32_score_kernel launch");

@@ -1,5 +1,6 @@
 // fp32 draft scorer on the CUDA cores (fp32 workloads with a 1e-5 score tolerance, so the
-// contraction stays in IEEE fp32 FMAs; TF32 tensor cores would not meet it).
+// contraction stays in IEEE fp32 FMAs: a split-TF32 tensor-core variant measured 1.2e-5
+// worst-case error and ran slower at 16 rows).
 //
 //   s'[row, j]     = alpha_p * sum_k h[row, k] * U^T[j, k]                 (prologue)
 //   score[row, v]  = sum_k W[v, k] h[row, k] + sum_j Vr[v, j] s'[row, j] - beta_p * prior[v]
@@ -9,25 +10,27 @@
 // logits of code/dflash.py:468 fused in and the rank state of code/dels.py:334-339.
 //
 // The scorer is an HBM-bound multi-row GEMV: every W element is read once and used
-// for all rows of the pass.  Each warp streams NV=8 vocabulary rows of [W | Vr] with
-// coalesced 16-byte loads (lane l owns k = 4l..4l+3 of every 128-wide chunk), keeps
-// ROWS x NV partial dot products in registers, and reads the rows' [h | s'] from
-// shared memory.  A 5-stage recursive-halving shuffle then reduce-scatters the
-// partials so each lane ends with complete scores for one row, applies the prior, and
-// keeps a running packed (score, index) key; one 64-bit atomicMax per (row, warp)
-// merges the warps.
+// for all 16 rows of a pass.  The design is described above f32_score_kernel.
 #include "f32_score.cuh"
 
 namespace dels {
 
-// Register select that the compiler cannot turn into an indexed (local-memory) access
-// of the partial-sum array.
-__device__ __forceinline__ float select_f32(bool c, float a, float b) {
-  float r;
-  asm("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\tselp.f32 %0, %1, %2, p;\n\t}"
-      : "=f"(r)
-      : "f"(a), "f"(b), "r"((int)c));
-  return r;
+// The data rows of one pass, transposed: dst[k][16] = src[r][k] for r < nrows, zero for
+// the padding rows, for both segments (h over H, s' over r) in one launch.  The scorer
+// then reads one k of all 16 rows as four 16-byte shared-memory broadcasts.
+__global__ void f32_transpose_pass_kernel(const float* __restrict__ h, long long ld_h, int H,
+                                          const float* __restrict__ s, long long ld_s, int r, int nrows,
+                                          float* __restrict__ hT, float* __restrict__ sT) {
+  const long long nh = (long long)H * 16, total = nh + (long long)r * 16;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const bool seg0 = e < nh;
+    const long long f = seg0 ? e : e - nh;
+    const int k = (int)(f >> 4), row = (int)(f & 15);
+    float v = 0.0f;
+    if (row < nrows) v = seg0 ? h[row * ld_h + k] : s[row * ld_s + k];
+    (seg0 ? hT : sT)[f] = v;
+  }
 }
 
 __global__ void f32_rank_kernel(const float* __restrict__ h, long long ld_h, const float* __restrict__ ut,
@@ -58,12 +61,15 @@ __global__ void f32_rank_kernel(const float* __restrict__ h, long long ld_h, con
 // fp32 scorer.  Persistent: CTA c owns a contiguous run of 64-token vocabulary tiles.
 // Each K block of 64 is staged by TMA: the tile's 64 W rows (two 32-float boxes, 128-B
 // swizzle, so a warp reading 32 different rows at one k hits 8 distinct 16-B banks
-// groups per wavefront) and the pass's 16 [h | s'] rows (two boxes, read as shared-
-// memory broadcasts).  Compute warp w owns the 4-wide K slice [4w, 4w+4) of every block
-// (one 16-byte chunk of a 128-byte row) and keeps, per lane, 2 vocabulary rows x 16 data
-// rows of partial sums in registers; after the last K block the 16 slices are summed
-// through shared memory, the prior term applied, and each thread keeps a running packed
-// (score, index) key for one data row.  Sixteen compute warps give the SM enough warps
+// groups per wavefront) and the pass's 16 data rows transposed ([k][16], two boxes of 32
+// k, read as shared-memory broadcasts).  Compute warp w owns the 4-wide K slice
+// [4w, 4w+4) of every block (one 16-byte chunk of a 128-byte row) and keeps, per lane,
+// 2 vocabulary rows x 16 data rows of partial sums in registers as pairs of data rows:
+// one packed two-lane FMA (__ffma2_rn, the same rounding as two fmaf) updates two data
+// rows, so a K block costs 64 FMA instructions per warp instead of 128, with every
+// partial sum accumulated in exactly the same order.  After the last K block the 16
+// slices are summed through shared memory, the prior term applied, and each thread
+// keeps a running packed (score, index) key for one data row.  Sixteen compute warps give the SM enough warps
 // to hide shared-memory latency; a seventeenth issues the TMA loads (6-stage mbarrier
 // ring, bounded waits).
 // ------------------------------------------------------------------------------------
@@ -134,8 +140,8 @@ __global__ void __launch_bounds__(kF32Threads, 1)
           const CUtensorMap* mh = seg0 ? &map_h : &map_s;
           tma_load_2d(dst, mw, full_bar(st), k, v0);
           tma_load_2d(dst + kF32WBox, mw, full_bar(st), k + 32, v0);
-          tma_load_2d(dst + 2 * kF32WBox, mh, full_bar(st), k, 0);
-          tma_load_2d(dst + 2 * kF32WBox + kF32HBox, mh, full_bar(st), k + 32, 0);
+          tma_load_2d(dst + 2 * kF32WBox, mh, full_bar(st), 0, k);
+          tma_load_2d(dst + 2 * kF32WBox + kF32HBox, mh, full_bar(st), 0, k + 32);
           if (++st == kF32Stages) {
             st = 0;
             phase ^= 1u;
@@ -161,11 +167,11 @@ __global__ void __launch_bounds__(kF32Threads, 1)
 
   for (int t = t_lo; t < t_hi && ok; ++t) {
     const int v0 = t * kF32TileV;
-    float acc[2][kF32Rows];
+    float2 acc[2][kF32Rows / 2];  // acc[j][p] = partial sums of data rows (2p, 2p + 1)
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int r = 0; r < kF32Rows; ++r) acc[j][r] = 0.0f;
+      for (int p = 0; p < kF32Rows / 2; ++p) acc[j][p] = make_float2(0.0f, 0.0f);
 
     for (int kb = 0; kb < nkb; ++kb) {
       if (!mbar_wait(full_bar(st), phase, abort_flag, status)) {
@@ -174,7 +180,7 @@ __global__ void __launch_bounds__(kF32Threads, 1)
       }
       const uint8_t* stage = smem + st * kF32StageBytes;
       const uint8_t* wbox = stage + box * kF32WBox;
-      const float* hbox = reinterpret_cast<const float*>(stage + 2 * kF32WBox + box * kF32HBox);
+      const float* hbox = reinterpret_cast<const float*>(stage + 2 * kF32WBox + box * kF32HBox);  // [32 k][16]
       {
         float4 w[2];
 #pragma unroll
@@ -183,16 +189,19 @@ __global__ void __launch_bounds__(kF32Threads, 1)
           w[j] = *reinterpret_cast<const float4*>(wbox + v * 128 + ((c ^ (v & 7)) << 4));
         }
 #pragma unroll
-        for (int r = 0; r < kF32Rows; ++r) {
-          const float4 hv = *reinterpret_cast<const float4*>(hbox + r * 32 + c * 4);
+        for (int kk = 0; kk < 4; ++kk) {
+          const float wk0 = kk == 0 ? w[0].x : (kk == 1 ? w[0].y : (kk == 2 ? w[0].z : w[0].w));
+          const float wk1 = kk == 0 ? w[1].x : (kk == 1 ? w[1].y : (kk == 2 ? w[1].z : w[1].w));
+          const float2 w0 = make_float2(wk0, wk0), w1 = make_float2(wk1, wk1);
+          const float4* hk = reinterpret_cast<const float4*>(hbox + (c * 4 + kk) * kF32Rows);
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            float a = acc[j][r];
-            a = fmaf(w[j].x, hv.x, a);
-            a = fmaf(w[j].y, hv.y, a);
-            a = fmaf(w[j].z, hv.z, a);
-            a = fmaf(w[j].w, hv.w, a);
-            acc[j][r] = a;
+          for (int q = 0; q < kF32Rows / 4; ++q) {
+            const float4 hv = hk[q];  // data rows 4q .. 4q+3 at this k
+            const float2 ha = make_float2(hv.x, hv.y), hb = make_float2(hv.z, hv.w);
+            acc[0][2 * q] = __ffma2_rn(w0, ha, acc[0][2 * q]);
+            acc[0][2 * q + 1] = __ffma2_rn(w0, hb, acc[0][2 * q + 1]);
+            acc[1][2 * q] = __ffma2_rn(w1, ha, acc[1][2 * q]);
+            acc[1][2 * q + 1] = __ffma2_rn(w1, hb, acc[1][2 * q + 1]);
           }
         }
       }
@@ -211,7 +220,7 @@ __global__ void __launch_bounds__(kF32Threads, 1)
       float4* dst = reinterpret_cast<float4*>(red + (warp * kF32TileV + lane + 32 * j) * kF32Rows);
 #pragma unroll
       for (int q = 0; q < kF32Rows / 4; ++q)
-        dst[q] = make_float4(acc[j][4 * q], acc[j][4 * q + 1], acc[j][4 * q + 2], acc[j][4 * q + 3]);
+        dst[q] = make_float4(acc[j][2 * q].x, acc[j][2 * q].y, acc[j][2 * q + 1].x, acc[j][2 * q + 1].y);
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kF32ComputeWarps * 32) : "memory");
     if (r_own < nrows) {

@@ -368,7 +368,7 @@ def draft_score_f32(
             scores=torch.empty(rows, dtype=torch.float32, device=dev) if with_scores else None,
             keys=torch.empty(rows, dtype=torch.int64, device=dev),
         )
-    need = _lib.query("dels_score_f32_workspace_bytes", rows, r)
+    need = _lib.query("dels_score_f32_workspace_bytes", rows, H, r)
     ws = workspace(need, dev) if ws is None else ws.ensure(need)
     _lib.call(
         "dels_draft_score_f32",

@@ -135,9 +135,9 @@ DELS_API int dels_draft_score_bf16(const void* h, int64_t ld_h, const void* W, i
  * fp32 draft scorer on CUDA cores (fp32 workloads; scores within 1e-5).  Same
  * formula as dels_draft_score_bf16 with every tensor fp32 and s kept in fp32:
  *   s[i] = alpha_p * (h[i] . w_rank^T),  score = h.W[v] + s.Vr[v] - beta_p prior[v].
- * H % 4 == 0, r % 4 == 0.  ws >= dels_score_f32_workspace_bytes(rows, r).
+ * H % 4 == 0, r % 4 == 0.  ws >= dels_score_f32_workspace_bytes(rows, H, r).
  * --------------------------------------------------------------------------------- */
-DELS_API size_t dels_score_f32_workspace_bytes(int rows, int r);
+DELS_API size_t dels_score_f32_workspace_bytes(int rows, int H, int r);
 DELS_API int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t ld_w, const float* w_rank,
                          int64_t ld_wr, const float* Vr, int64_t ld_vr, const float* prior, const float* alpha,
                          const float* beta, int n_pos, const int32_t* row_pos, int rows, int H, int r, int V,
