@@ -389,9 +389,8 @@ int launch_scorer_pair(const TcOperands& op, TcArgs args, int max_pairs, cudaStr
   const long long want = tiles < max_pairs ? tiles * (args.tail_split > 1 ? args.tail_split : 1) : tiles;
   const int pairs = (int)(want < max_pairs ? want : max_pairs);
   if (pairs <= 0) return DELS_OK;
-  tc_scorer_pair_kernel<VB><<<2 * pairs, kTcThreads, PairConfig::kSmemBytes, st>>>(ma0, mb0, ma1, mb1, mb0t, mb1t,
-                                                                                   args);
-  DELS_CHECK_LAUNCH("tc_scorer_pair_kernel launch");
+  DELS_CHECK_PDL("tc_scorer_pair_kernel launch", launch_pdl(tc_scorer_pair_kernel<VB>, dim3(2 * pairs),
+      dim3(kTcThreads), PairConfig::kSmemBytes, st, ma0, mb0, ma1, mb1, mb0t, mb1t, args));
   return DELS_OK;
 }
 

@@ -192,18 +192,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  pdl_wait();
-
-  int m_rows = args.m_rows;
-  if (args.m_rows_dev != nullptr) {
-    const int d = *args.m_rows_dev;
-    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
-  }
-  const int num_m = (m_rows + kBM - 1) / kBM;
-  const int num_n = (args.n_cols + BN - 1) / BN;
-  const int total_kb = args.kb0 + args.kb1;
-  const Schedule sched = make_schedule(num_m, num_n, args.k_splits, args.group_m, args.tail_split, gridDim.x);
-  const int num_units = sched.total_units;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -223,10 +211,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tma_prefetch_map(&map_b0);
     tma_prefetch_map(&map_a1);
     tma_prefetch_map(&map_b1);
-    if (sched.tail_split > 1) {
-      tma_prefetch_map(&map_b0t);
-      tma_prefetch_map(&map_b1t);
-    }
+    tma_prefetch_map(&map_b0t);
+    tma_prefetch_map(&map_b1t);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -236,6 +222,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Set-up above touches no global memory; from here on the inputs of earlier kernels
+  // (rows, keys, device row count) are read.
+  pdl_wait();
+  int m_rows = args.m_rows;
+  if (args.m_rows_dev != nullptr) {
+    const int d = *args.m_rows_dev;
+    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
+  }
+  const int num_m = (m_rows + kBM - 1) / kBM;
+  const int num_n = (args.n_cols + BN - 1) / BN;
+  const int total_kb = args.kb0 + args.kb1;
+  const Schedule sched = make_schedule(num_m, num_n, args.k_splits, args.group_m, args.tail_split, gridDim.x);
+  const int num_units = sched.total_units;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer

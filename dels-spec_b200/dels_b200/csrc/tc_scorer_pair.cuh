@@ -77,17 +77,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
 
-  int m_rows = args.m_rows;
-  if (args.m_rows_dev != nullptr) {
-    const int d = *args.m_rows_dev;
-    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
-  }
-  const int num_m = (m_rows + 2 * kBM - 1) / (2 * kBM);  // pair tiles along the rows
-  const int num_n = (args.n_cols + BN - 1) / BN;
-  const int total_kb = args.kb0 + args.kb1;
-  const Schedule sched = make_schedule(num_m, num_n, 1, args.group_m, args.tail_split, num_pairs);
-  const int num_units = sched.total_units;
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
@@ -117,6 +106,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Set-up above touches no global memory; from here on the inputs of earlier kernels
+  // (rows, keys, device row count) are read.
+  pdl_wait();
+  int m_rows = args.m_rows;
+  if (args.m_rows_dev != nullptr) {
+    const int d = *args.m_rows_dev;
+    m_rows = d < 0 ? 0 : (d < m_rows ? d : m_rows);
+  }
+  const int num_m = (m_rows + 2 * kBM - 1) / (2 * kBM);  // pair tiles along the rows
+  const int num_n = (args.n_cols + BN - 1) / BN;
+  const int total_kb = args.kb0 + args.kb1;
+  const Schedule sched = make_schedule(num_m, num_n, 1, args.group_m, args.tail_split, num_pairs);
+  const int num_units = sched.total_units;
+
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
@@ -325,6 +328,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   }
 
   // ------------------------------------------------------------------ teardown
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // the partner no longer touches this CTA's shared memory / TMEM
