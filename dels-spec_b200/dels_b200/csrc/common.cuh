@@ -72,12 +72,6 @@ __host__ __device__ __forceinline__ float key_score(long long key) {
 
 constexpr long long kKeyEmpty = (long long)0x8000000000000000ull;
 
-// "take" rule of a sequential scan in increasing index order: strictly greater wins,
-// a NaN beats any non-NaN, and the first NaN is kept.
-__device__ __forceinline__ bool scan_takes(float s, float best) {
-  return (s > best) || ((s != s) && (best == best));
-}
-
 // ordered_i32 without branches, for the scoring epilogues: x + 0 turns -0 into +0 and
 // leaves every other value (NaN included) as it is.
 __device__ __forceinline__ int32_t ordered_i32_dev(float f) {
