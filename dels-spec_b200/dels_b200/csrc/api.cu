@@ -37,6 +37,7 @@ bool g_use_pairs = true;
 // (DELS_SCORER_SKINNY=0 in the environment selects the 128-row tile kernel instead).
 bool g_use_skinny = true;
 constexpr int kSkinnyMaxRows = 32;
+constexpr int kSkinnyStageRows = 4;
 // Programmatic dependent launch for the kernels of a rollout step (DELS_PDL=0 in the
 // environment turns it off).
 bool g_use_pdl = true;
@@ -144,6 +145,37 @@ int make_map_f32(CUtensorMap* m, const void* ptr, long long inner, long long out
   return DELS_OK;
 }
 
+// Epilogue-operand maps of the skinny scorer, no swizzle, zero fill outside the extents:
+// base logits [rows, n] bf16 (row stride ld) in boxes of box_n x box_rows, and an fp32
+// vector [n] (one row) in boxes of box_n.
+int make_map_base_bf16(CUtensorMap* m, const void* ptr, long long n, long long rows, long long ld, int box_n,
+                       int box_rows) {
+  cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_n, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DELS_ERR_CUDA, "cuTensorMapEncodeTiled (base) failed (%d) for [%lld x %lld], ld %lld", (int)r, rows, n,
+                ld);
+  return DELS_OK;
+}
+
+int make_map_vec_f32(CUtensorMap* m, const float* ptr, long long n, int box_n) {
+  // one row of n; the row stride is never stepped but must be a multiple of 16 bytes
+  cuuint64_t dims[2] = {(cuuint64_t)n, 1};
+  cuuint64_t strides[1] = {(cuuint64_t)((n * 4 + 15) / 16 * 16)};
+  cuuint32_t box[2] = {(cuuint32_t)box_n, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DELS_ERR_CUDA, "cuTensorMapEncodeTiled (vector) failed (%d) for [%lld]", (int)r, n);
+  return DELS_OK;
+}
+
 // ------------------------------------------------------------------ per-device state
 struct DeviceState {
   bool ready = false;
@@ -194,7 +226,9 @@ int init_device(int dev) {
     SET((tc_scorer_pair_kernel<false>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<true>), PairConfig::kSmemBytes);
     SET((tc_skinny_kernel<16>), SkinnyConfig<16>::kSmemBytes);
+    SET((tc_skinny_staged_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_kernel<32>), SkinnyConfig<32>::kSmemBytes);
+    SET((tc_skinny_staged_kernel<32>), SkinnyConfig<32>::kSmemBytes);
     SET(rnn_recurrence_kernel, kMaxSmem);
     SET(rank_finalize_kernel, 0);
     SET(keys_init_kernel, 0);
@@ -325,7 +359,7 @@ int launch_tc(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) 
 
 // The skinny scorer: weight maps (W, Vr) in 64 x 128 boxes as the MMA's A operand, row
 // maps (h, s) in 64 x NB boxes as its B operand; one persistent CTA per SM.
-template <int NB>
+template <int NB, bool SB>
 int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) {
   int rc = ensure_encode();
   if (rc != DELS_OK) return rc;
@@ -347,11 +381,24 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
   }
   args.kb0 = cdiv(op.K0, kBK);
   args.kb1 = cdiv(op.K1, kBK);
+  // the epilogue operands (base logits when TMA can address them, prior): fetched by the
+  // producer; unused maps are copies of a weight map
+  CUtensorMap mbase = wa1, mprior = wa1;
+  if (SB && args.base != nullptr &&
+      (rc = make_map_base_bf16(&mbase, args.base, op.n_extent, op.m_extent, args.ld_base, kSkinnyBM, NB)) != DELS_OK)
+    return rc;
+  if (SB && args.prior != nullptr && (rc = make_map_vec_f32(&mprior, args.prior, op.n_extent, kSkinnyBM)) != DELS_OK)
+    return rc;
   const int tiles = cdiv(op.n_extent, kSkinnyBM);
   const int grid = tiles < sm_count ? tiles : sm_count;
   if (grid <= 0) return DELS_OK;
-  DELS_CHECK_PDL("tc_skinny_kernel launch", launch_pdl(tc_skinny_kernel<NB>, dim3(grid), dim3(kTcThreads),
-      SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
+  if (SB) {
+    DELS_CHECK_PDL("tc_skinny_staged_kernel launch", launch_pdl(tc_skinny_staged_kernel<NB>, dim3(grid),
+        dim3(kTcThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, mbase, mprior, args));
+  } else {
+    DELS_CHECK_PDL("tc_skinny_kernel launch", launch_pdl(tc_skinny_kernel<NB>, dim3(grid), dim3(kTcThreads),
+        SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
+  }
   return DELS_OK;
 }
 
@@ -540,12 +587,16 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
   a.idx_out = reinterpret_cast<long long*>(idx_out);
   a.score_out = score_out;
   a.counter = hdr.counter;
-  if (rows <= kSkinnyMaxRows && g_use_skinny) {
-    // Decode-shaped call: the vocab tile is the MMA's M side, the rows its N side.
-    if (rows <= 16) return launch_skinny<16>(op, a, ds->sm_count, st);
-    return launch_skinny<32>(op, a, ds->sm_count, st);
-  }
   const bool vec_base = base != nullptr && aligned16(base) && (ld_base % 8) == 0;
+  if (rows <= kSkinnyMaxRows && g_use_skinny) {
+    // Decode-shaped call: the vocab tile is the MMA's M side, the rows its N side.  Above
+    // kSkinnyStageRows rows the producer stages the epilogue operands (base logits when
+    // TMA can address them, prior).
+    const bool stage = rows > kSkinnyStageRows && (base == nullptr || vec_base);
+    if (rows <= 16)
+      return stage ? launch_skinny<16, true>(op, a, ds->sm_count, st) : launch_skinny<16, false>(op, a, ds->sm_count, st);
+    return stage ? launch_skinny<32, true>(op, a, ds->sm_count, st) : launch_skinny<32, false>(op, a, ds->sm_count, st);
+  }
   if (rows > kBM && ds->max_pairs > 0 && g_use_pairs) {
     // More than one 128-row tile: CTA pairs share each LM-head tile across two SMs.
     a.group_m = kScorerGroupM / 2;

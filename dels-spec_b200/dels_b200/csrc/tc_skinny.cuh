@@ -12,6 +12,11 @@
 // stages keep ~150 KB of the weight in flight per SM, and every epilogue thread has
 // work: it adds its vocab row's base logits and prior, packs (score, index) keys and
 // keeps a running maximum per row in registers across all the tiles its CTA scores.
+// With STAGE, the tile's base-logit rows and prior slice are fetched by the TMA producer
+// into a per-accumulator shared-memory buffer a tile or more ahead (own full / empty
+// barriers), so the epilogue never waits on global loads that queue behind the weight
+// stream (at 16 rows that wait was ~3 us per tile); for a few rows the epilogue's own
+// two loads per tile are cheaper than the extra hand-off, and it loads them directly.
 // The maxima meet once per CTA (warp shuffles, then shared memory) before one 64-bit
 // atomicMax per row.
 //
@@ -35,8 +40,12 @@ struct SkinnyConfig {
   static constexpr int kStages = 8;
   static constexpr int kAcc = 4;  // accumulators (tiles) in flight in TMEM
   static constexpr int kTmemCols = kAcc * NB <= 32 ? 32 : (kAcc * NB <= 64 ? 64 : 128);
-  static constexpr int kBarOffset = kStages * (kABytes + kBBytes);
-  static constexpr int kNumBars = 2 * kStages + 2 * kAcc;
+  // per accumulator: the tile's base logits [NB][128] bf16 and prior [128] fp32
+  static constexpr int kEpiBaseBytes = NB * kSkinnyBM * 2;
+  static constexpr int kEpiPriorBytes = kSkinnyBM * 4;
+  static constexpr int kEpiOffset = kStages * (kABytes + kBBytes);
+  static constexpr int kBarOffset = kEpiOffset + kAcc * (kEpiBaseBytes + kEpiPriorBytes);
+  static constexpr int kNumBars = 2 * kStages + 4 * kAcc;
   static constexpr int kRedOffset = kBarOffset + kNumBars * 8 + 16;
   static constexpr int kSmemBytes = kRedOffset + 4 * NB * 8 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -44,12 +53,14 @@ struct SkinnyConfig {
 
 // `map_a0`/`map_a1`: the weights (W [V, H], Vr [V, r]) in 64 x 128 boxes; `map_b0`/`map_b1`:
 // the rows (h [rows, H], alpha-scaled s [rows, r]) in 64 x NB boxes.  args.kb0 / kb1 are
-// the K blocks of the two segments (kb0 = 0 for the base-logit variant).
-template <int NB>
-__global__ void __launch_bounds__(kTcThreads, 1)
-    tc_skinny_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
-                     const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
-                     const TcArgs args) {
+// the K blocks of the two segments (kb0 = 0 for the base-logit variant).  With STAGE:
+// `map_base` = base logits [rows, V slice] in 128 x NB boxes (when args.base is set) and
+// `map_prior` = the prior [V slice] fp32 in 128-element boxes (when args.prior is set).
+template <int NB, bool STAGE>
+__device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUtensorMap* map_b0,
+                                            const CUtensorMap* map_a1, const CUtensorMap* map_b1,
+                                            const CUtensorMap* map_base, const CUtensorMap* map_prior,
+                                            const TcArgs& args) {
   using Cfg = SkinnyConfig<NB>;
   constexpr int S = Cfg::kStages;
   constexpr int NA = Cfg::kAcc;
@@ -70,6 +81,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   auto empty_bar = [&](int s) { return smem_u32(&bars[S + s]); };
   auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * S + a]); };
   auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * S + NA + a]); };
+  auto efull_bar = [&](int a) { return smem_u32(&bars[2 * S + 2 * NA + a]); };
+  auto eempty_bar = [&](int a) { return smem_u32(&bars[2 * S + 3 * NA + a]); };
+  auto epi_base = [&](int a) { return Cfg::kEpiOffset + a * (Cfg::kEpiBaseBytes + Cfg::kEpiPriorBytes); };
+  const bool stage_base = STAGE && args.base != nullptr;
+  const bool stage_prior = STAGE && args.prior != nullptr;
+  const bool stage_epi = stage_base || stage_prior;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -85,16 +102,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int a = 0; a < NA; ++a) {
       mbar_init(tfull_bar(a), 1);
       mbar_init(tempty_bar(a), 4 * 32);
+      mbar_init(efull_bar(a), 1);
+      mbar_init(eempty_bar(a), 4 * 32);
     }
     *abort_flag = 0;
     *last_flag = 0;
     mbar_fence_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_map(&map_a0);
-    tma_prefetch_map(&map_b0);
-    tma_prefetch_map(&map_a1);
-    tma_prefetch_map(&map_b1);
+    tma_prefetch_map(map_a0);
+    tma_prefetch_map(map_b0);
+    tma_prefetch_map(map_a1);
+    tma_prefetch_map(map_b1);
+    if (stage_base) tma_prefetch_map(map_base);
+    if (stage_prior) tma_prefetch_map(map_prior);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -121,8 +142,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int issued = 0;
       bool ok = true;
       constexpr uint32_t tx = (uint32_t)(Cfg::kABytes + Cfg::kBBytes);
+      const uint32_t etx = (stage_base ? (uint32_t)Cfg::kEpiBaseBytes : 0u) +
+                           (stage_prior ? (uint32_t)Cfg::kEpiPriorBytes : 0u);
+      int eacc = 0, eissued = 0;
+      uint32_t ephase = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const int n0 = t * kSkinnyBM;
+        if (stage_epi) {
+          // the tile's epilogue operands, into the buffer of the accumulator it will use
+          if (!mbar_wait(eempty_bar(eacc), ephase ^ 1u, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(efull_bar(eacc), etx);
+          const uint32_t eb = base_addr + (uint32_t)epi_base(eacc);
+          if (stage_base) tma_load_2d(eb, map_base, efull_bar(eacc), n0, 0);
+          if (stage_prior) tma_load_2d(eb + (uint32_t)Cfg::kEpiBaseBytes, map_prior, efull_bar(eacc), n0, 0);
+          ++eissued;
+          if (++eacc == NA) {
+            eacc = 0;
+            ephase ^= 1u;
+          }
+        }
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status)) {
             ok = false;
@@ -132,12 +173,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t a_dst = a_base + stage * Cfg::kABytes;
           const uint32_t b_dst = b_base + stage * Cfg::kBBytes;
           if (kb < args.kb0) {
-            tma_load_2d(a_dst, &map_a0, full_bar(stage), kb * kBK, n0);
-            tma_load_2d(b_dst, &map_b0, full_bar(stage), kb * kBK, 0);
+            tma_load_2d(a_dst, map_a0, full_bar(stage), kb * kBK, n0);
+            tma_load_2d(b_dst, map_b0, full_bar(stage), kb * kBK, 0);
           } else {
             const int k1 = kb - args.kb0;
-            tma_load_2d(a_dst, &map_a1, full_bar(stage), k1 * kBK, n0);
-            tma_load_2d(b_dst, &map_b1, full_bar(stage), k1 * kBK, 0);
+            tma_load_2d(a_dst, map_a1, full_bar(stage), k1 * kBK, n0);
+            tma_load_2d(b_dst, map_b1, full_bar(stage), k1 * kBK, 0);
           }
           ++issued;
           if (++stage == S) {
@@ -158,6 +199,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           const unsigned long long t0 = globaltimer_ns();
           while (!mbar_try_wait(full_bar(s), p) && globaltimer_ns() - t0 < kWaitLimitNs / 20) {
+          }
+        }
+        const int eout = eissued < NA ? eissued : NA;
+        int e = eacc;
+        uint32_t ep = ephase;
+        for (int i = 0; i < eout; ++i) {
+          if (--e < 0) {
+            e = NA - 1;
+            ep ^= 1u;
+          }
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(efull_bar(e), ep) && globaltimer_ns() - t0 < kWaitLimitNs / 20) {
           }
         }
       }
@@ -225,16 +278,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const int v = t * kSkinnyBM + quad * 32 + lane;  // this thread's vocab row in the slice
+      const int vt = quad * 32 + lane;  // this thread's row within the tile
+      const int v = t * kSkinnyBM + vt;  // ... and within the vocab slice
       const bool v_ok = v < args.n_cols;
-      // Operands of the epilogue, loaded before the accumulator wait so their latency
-      // overlaps the tile's MMAs.
-      const float pv = (v_ok && args.prior != nullptr) ? __ldg(args.prior + v) : 0.0f;
       float bv[NB];
+      float pv = 0.0f;
+      if (!STAGE) {
+        // loaded directly, before the accumulator wait so the latency overlaps the MMAs
+        pv = (v_ok && args.prior != nullptr) ? __ldg(args.prior + v) : 0.0f;
 #pragma unroll
-      for (int b = 0; b < NB; ++b)
-        bv[b] = (v_ok && args.base != nullptr && b < nrows) ? __bfloat162float(args.base[(long long)b * args.ld_base + v])
-                                                            : 0.0f;
+        for (int b = 0; b < NB; ++b)
+          bv[b] = (v_ok && args.base != nullptr && b < nrows)
+                      ? __bfloat162float(args.base[(long long)b * args.ld_base + v])
+                      : 0.0f;
+      }
+      if (stage_epi && !mbar_wait(efull_bar(acc), acc_phase, abort_flag, args.status)) break;
+      const uint8_t* eb = smem + epi_base(acc);
+      if (stage_base) {
+        const __nv_bfloat16* bs = reinterpret_cast<const __nv_bfloat16*>(eb);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) bv[b] = __bfloat162float(bs[b * kSkinnyBM + vt]);
+      } else if (STAGE) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) bv[b] = 0.0f;
+      }
+      if (stage_prior) pv = reinterpret_cast<const float*>(eb + Cfg::kEpiBaseBytes)[vt];
+      if (stage_epi) mbar_arrive(eempty_bar(acc));
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * NB);
@@ -316,6 +385,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (threadIdx.x == 0) atomicExch(args.counter, 0u);
     }
   }
+}
+
+// Two entry points over the same body: the staged one takes the two epilogue-operand maps
+// as well; the plain one keeps its parameter block at the four operand maps.
+template <int NB>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_skinny_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                     const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                     const TcArgs args) {
+  skinny_body<NB, false>(&map_a0, &map_b0, &map_a1, &map_b1, nullptr, nullptr, args);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_skinny_staged_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                            const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                            const __grid_constant__ CUtensorMap map_base, const __grid_constant__ CUtensorMap map_prior,
+                            const TcArgs args) {
+  skinny_body<NB, true>(&map_a0, &map_b0, &map_a1, &map_b1, &map_base, &map_prior, args);
 }
 
 }  // namespace dels
