@@ -125,8 +125,28 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Set-up above touches no global memory; from here on the inputs of earlier kernels
-  // (rows, keys, device row count) are read.
+  // The weight tiles of the first S stages do not depend on any earlier kernel: in the
+  // plain variant (a few rows) the producer issues them before the programmatic-
+  // dependency wait, so in a rollout the weight stream starts while the previous step's
+  // kernel finishes (batch-1 runner step -4 %).  Each prefetched stage already carries
+  // its full expected byte count; its row-tile load follows after the wait.  The staged
+  // variant does not prefetch: there the tile's epilogue operands would queue behind the
+  // prefetched weights (measured +4 % at 16 rows).
+  constexpr uint32_t tx = (uint32_t)(Cfg::kABytes + Cfg::kBBytes);
+  const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int n_pre = STAGE ? 0 : min(S, my_tiles * total_kb);
+  if (warp == 0 && lane == 0) {
+    for (int it = 0; it < n_pre; ++it) {
+      const int n0 = ((int)blockIdx.x + (it / total_kb) * (int)gridDim.x) * kSkinnyBM;
+      const int kb = it % total_kb;
+      mbar_arrive_expect_tx(full_bar(it), tx);
+      if (kb < args.kb0)
+        tma_load_2d(a_base + it * Cfg::kABytes, map_a0, full_bar(it), kb * kBK, n0);
+      else
+        tma_load_2d(a_base + it * Cfg::kABytes, map_a1, full_bar(it), (kb - args.kb0) * kBK, n0);
+    }
+  }
+  // From here on the inputs of earlier kernels (rows, keys, device row count) are read.
   pdl_wait();
   int m_rows = args.m_rows;
   if (args.m_rows_dev != nullptr) {
@@ -141,7 +161,6 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      constexpr uint32_t tx = (uint32_t)(Cfg::kABytes + Cfg::kBBytes);
       const uint32_t etx = (stage_base ? (uint32_t)Cfg::kEpiBaseBytes : 0u) +
                            (stage_prior ? (uint32_t)Cfg::kEpiPriorBytes : 0u);
       int eacc = 0, eissued = 0;
@@ -165,19 +184,22 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
           }
         }
         for (int kb = 0; kb < total_kb; ++kb) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status)) {
-            ok = false;
-            break;
+          const bool prefetched = issued < n_pre;  // weight tile already in flight
+          if (!prefetched) {
+            if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(full_bar(stage), tx);
           }
-          mbar_arrive_expect_tx(full_bar(stage), tx);
           const uint32_t a_dst = a_base + stage * Cfg::kABytes;
           const uint32_t b_dst = b_base + stage * Cfg::kBBytes;
           if (kb < args.kb0) {
-            tma_load_2d(a_dst, map_a0, full_bar(stage), kb * kBK, n0);
+            if (!prefetched) tma_load_2d(a_dst, map_a0, full_bar(stage), kb * kBK, n0);
             tma_load_2d(b_dst, map_b0, full_bar(stage), kb * kBK, 0);
           } else {
             const int k1 = kb - args.kb0;
-            tma_load_2d(a_dst, map_a1, full_bar(stage), k1 * kBK, n0);
+            if (!prefetched) tma_load_2d(a_dst, map_a1, full_bar(stage), k1 * kBK, n0);
             tma_load_2d(b_dst, map_b1, full_bar(stage), k1 * kBK, 0);
           }
           ++issued;
