@@ -186,6 +186,80 @@ class PipelinedE2E:
         self.stream.wait_stream(self.d2h)
 
 
+class PipelinedE2ESplit:
+    """PipelinedE2E for a step made of a rank projection and a scorer (single GPU, bf16).
+
+    The step's kernels form a programmatic-dependent-launch chain (projection,
+    finalisation, scorer, next projection, ...); a cross-stream wait or event record
+    between two of them makes the second start only after the first has drained.  Here
+    every such stream operation sits between the finalisation of step i and its scorer,
+    so the scorer of step i still chains into the projection of step i+1:
+
+      compute:  proj(i) fin(i) | record mid(i) | wait in_ready(i+1), read(i-3) | scorer(i)
+      h2d:      wait mid(i-1) (scorer(i-2) done: slot free) -> copy input i+1 -> in_ready(i+1)
+      d2h:      wait mid(i) (scorer(i-1) done) -> copy tokens of step i-1 -> read(i-1)
+
+    Three input / token slots; every step's input is copied host -> device and every
+    step's tokens device -> host inside the timed region (``drain`` reads back the last
+    step's tokens and makes the compute stream wait for it)."""
+
+    SLOTS = 3
+
+    def __init__(self, host_in: torch.Tensor, project, score, rows: int, dev, stream):
+        n = self.SLOTS
+        self.host_in = host_in
+        self.project = project
+        self.score = score
+        self.stream = stream
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.dev_in = [torch.empty_like(host_in, device=dev) for _ in range(n)]
+        self.tokens = [torch.empty(rows, dtype=torch.int64, device=dev) for _ in range(n)]
+        self.host_out = [torch.empty(rows, dtype=torch.int64).pin_memory() for _ in range(n)]
+        self.in_ready = [torch.cuda.Event() for _ in range(n)]
+        self.mid = [torch.cuda.Event() for _ in range(n)]
+        self.read = [torch.cuda.Event() for _ in range(n)]
+        self.last = torch.cuda.Event()
+        for e in self.mid + self.read:
+            e.record(stream)
+        with torch.cuda.stream(self.h2d):
+            self.h2d.wait_stream(stream)
+            self.dev_in[0].copy_(host_in, non_blocking=True)
+            self.in_ready[0].record(self.h2d)
+        stream.wait_event(self.in_ready[0])
+        self.i = 0
+
+    def step(self):
+        n = self.SLOTS
+        i = self.i
+        self.i += 1
+        s, nxt, prev = i % n, (i + 1) % n, (i - 1) % n
+        with torch.cuda.stream(self.h2d):
+            self.h2d.wait_event(self.mid[prev])  # scorer(i-2) done: slot nxt is free
+            self.dev_in[nxt].copy_(self.host_in, non_blocking=True)
+            self.in_ready[nxt].record(self.h2d)
+        self.project(self.dev_in[s], s)
+        self.mid[s].record(self.stream)  # after fin(i): scorer(i-1) has completed
+        if i > 0:
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.mid[s])
+                self.host_out[prev].copy_(self.tokens[prev], non_blocking=True)
+                self.read[prev].record(self.d2h)
+        self.stream.wait_event(self.in_ready[nxt])
+        self.stream.wait_event(self.read[s])  # tokens slot s of step i-3 was read back
+        self.score(self.dev_in[s], s, self.tokens[s])
+
+    def drain(self):
+        if self.i == 0:
+            return
+        prev = (self.i - 1) % self.SLOTS
+        self.last.record(self.stream)
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(self.last)
+            self.host_out[prev].copy_(self.tokens[prev], non_blocking=True)
+        self.stream.wait_stream(self.d2h)
+
+
 def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None, hold_ms: float = 0.0,
           drain=None) -> float:
     """ms for exactly `steps` calls of fn: CUDA events on `stream`, barrier + synchronize on
@@ -315,7 +389,28 @@ def run_ours(args, rank, world, dev):
                 torch.distributed.all_reduce(o.keys, op=torch.distributed.ReduceOp.MAX)
                 ops.keys_decode(o.keys, tokens=tokens, with_scores=False)
 
-        pipe = PipelinedE2E(h_host, e2e_score, rows, dev, stream)
+        if not sharded and not fp32:
+            # projection and scorer as two public calls, so the cross-stream waits sit
+            # between them (PipelinedE2ESplit)
+            n_sl = PipelinedE2ESplit.SLOTS
+            sl_s = [torch.empty(rows, r, dtype=torch.bfloat16, device=dev) for _ in range(n_sl)]
+            sl_ws = [ops.Workspace(need, dev) for _ in range(n_sl)]
+            sl_out = [ops.ScoreOut(tokens=None, scores=None, keys=torch.empty(rows, dtype=torch.int64, device=dev))
+                      for _ in range(n_sl)]
+
+            def e2e_project(h_in, slot):
+                ops.rank_project_bf16(h_in, t["w_rank"], t["alpha"], n_pos=wl.n_pos, s_scaled=sl_s[slot],
+                                      keys=sl_out[slot].keys, want_state=False, ws=sl_ws[slot])
+
+            def e2e_scorer(h_in, slot, tokens):
+                o = sl_out[slot]
+                o.tokens = tokens
+                ops.fused_argmax_bf16(h_in, t["W"], sl_s[slot], t["Vr"], t["prior"], t["beta"], n_pos=wl.n_pos,
+                                      keys_ready=True, out=o, ws=sl_ws[slot])
+
+            pipe = PipelinedE2ESplit(h_host, e2e_project, e2e_scorer, rows, dev, stream)
+        else:
+            pipe = PipelinedE2E(h_host, e2e_score, rows, dev, stream)
         e2e_note = ("per rank: this rank's 1/N row slice (all-gathered over NVLink)" if gather else
                     "per rank: all rows")
         e2e_step = pipe.step

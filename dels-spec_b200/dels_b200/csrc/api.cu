@@ -792,10 +792,11 @@ int dels_draft_score_f32(const float* h, int64_t ld_h, const float* W, int64_t l
     DELS_CHECK_LAUNCH("f32_rank_kernel launch");
   }
   if ((rc = ensure_encode()) != DELS_OK) return rc;
-  // W / Vr: 32-float x 64-row boxes, 128-byte swizzle (the kernel reads 32 rows at one k)
+  // W / Vr: 32-float boxes of one vocabulary tile, 128-byte swizzle (the kernel reads 32
+  // rows at one k)
   CUtensorMap mw, mvr;
-  if ((rc = make_map_f32(&mw, W, H, V, ld_w, 64, true)) != DELS_OK) return rc;
-  if ((rc = make_map_f32(&mvr, Vr, r, V, ld_vr, 64, true)) != DELS_OK) return rc;
+  if ((rc = make_map_f32(&mw, W, H, V, ld_w, f32_score_tile_rows(), true)) != DELS_OK) return rc;
+  if ((rc = make_map_f32(&mvr, Vr, r, V, ld_vr, f32_score_tile_rows(), true)) != DELS_OK) return rc;
   const int kb0 = cdiv(H, 64), kb1 = cdiv(r, 64);
   // the transposed pass buffers: [k][16] rows, 32 k per box
   CUtensorMap mh, ms;

@@ -58,34 +58,41 @@ __global__ void f32_rank_kernel(const float* __restrict__ h, long long ld_h, con
 }
 
 // ------------------------------------------------------------------------------------
-// fp32 scorer.  Persistent: CTA c owns a contiguous run of 64-token vocabulary tiles.
-// Each K block of 64 is staged by TMA: the tile's 64 W rows (two 32-float boxes, 128-B
-// swizzle, so a warp reading 32 different rows at one k hits 8 distinct 16-B banks
-// groups per wavefront) and the pass's 16 data rows transposed ([k][16], two boxes of 32
-// k, read as shared-memory broadcasts).  Compute warp w owns the 4-wide K slice
-// [4w, 4w+4) of every block (one 16-byte chunk of a 128-byte row) and keeps, per lane,
-// 2 vocabulary rows x 16 data rows of partial sums in registers as pairs of data rows:
-// one packed two-lane FMA (__ffma2_rn, the same rounding as two fmaf) updates two data
-// rows, so a K block costs 64 FMA instructions per warp instead of 128, with every
-// partial sum accumulated in exactly the same order.  After the last K block the 16
-// slices are summed through shared memory, the prior term applied, and each thread
-// keeps a running packed (score, index) key for one data row.  Sixteen compute warps give the SM enough warps
-// to hide shared-memory latency; a seventeenth issues the TMA loads (6-stage mbarrier
-// ring, bounded waits).
+// fp32 scorer.  Persistent: CTA c owns a contiguous run of 96-token vocabulary tiles
+// (1583 tiles at V = 151936: at most 11 per CTA on 148 SMs, 3 % above an even split).
+// Each K block of 64 is staged by TMA: the tile's 96 W rows (two 32-float boxes, 128-byte
+// swizzle, so the 32 rows a warp reads at one k fall in 8 distinct 16-byte bank groups)
+// and the pass's 16 data rows transposed ([k][16], two boxes of 32 k, read as
+// shared-memory broadcasts).  Compute warp w owns the 8-wide K slice made of 16-byte
+// chunks 2(w % 4) and 2(w % 4) + 1 of box w / 4, and keeps, per lane, 3 vocabulary rows
+// (lane + 32 j) x 16 data rows of partial sums in registers as pairs of data rows: one
+// packed two-lane FMA (__ffma2_rn, the rounding of two fmaf) updates two data rows.  One
+// 16-byte broadcast of the data rows thus feeds 3 x 2 packed FMAs per lane; with two
+// vocabulary rows per lane (64-row tiles) the broadcasts made the shared-memory pipe
+// the busiest unit (75 % of peak, ncu) and serialised with the FP32 pipe.  After the
+// last K block the 8 slices are summed through shared memory ([warp][row quad][v],
+// conflict-free), the prior term applied, and each thread keeps running packed (score,
+// index) keys for 8 data rows of one vocabulary row.  A ninth warp issues the TMA loads
+// (6-stage mbarrier ring, bounded waits).
 // ------------------------------------------------------------------------------------
 namespace {
-constexpr int kF32TileV = 64;                       // vocabulary rows per tile
+constexpr int kF32TileV = 96;                       // vocabulary rows per tile (3 per lane)
+constexpr int kF32VPerLane = kF32TileV / 32;
 constexpr int kF32Rows = 16;                        // data rows per pass
 constexpr int kF32KB = 64;                          // K per stage
-constexpr int kF32WBox = 32 * kF32TileV * 4;        // one 32-float x 64-row box: 8 KB
+constexpr int kF32WBox = 32 * kF32TileV * 4;        // one 32-float x 96-row box: 12 KB
 constexpr int kF32HBox = 32 * kF32Rows * 4;         // one 32-float x 16-row box: 2 KB
-constexpr int kF32StageBytes = 2 * kF32WBox + 2 * kF32HBox;  // 20 KB
+constexpr int kF32StageBytes = 2 * kF32WBox + 2 * kF32HBox;  // 28 KB
 constexpr int kF32Stages = 6;
-constexpr int kF32ComputeWarps = 16;
-constexpr int kF32RedBytes = kF32ComputeWarps * kF32TileV * kF32Rows * 4;  // 32 KB
+constexpr int kF32ComputeWarps = kF32Threads / 32 - 1;       // 8
+constexpr int kF32EpiThreads = 2 * kF32TileV;                // (vocabulary row, 8 data rows)
+constexpr int kF32RedBytes = kF32ComputeWarps * kF32TileV * kF32Rows * 4;  // 48 KB
+static_assert(kF32ComputeWarps == 8, "8 compute warps x 8-wide K slices cover a 64-wide K block");
+static_assert(kF32EpiThreads <= kF32ComputeWarps * 32, "epilogue threads");
 }  // namespace
 
 int f32_score_smem_bytes() { return kF32Stages * kF32StageBytes + kF32RedBytes + 256 + 1024; }
+int f32_score_tile_rows() { return kF32TileV; }
 
 __global__ void __launch_bounds__(kF32Threads, 1)
     f32_score_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_h,
@@ -153,23 +160,31 @@ __global__ void __launch_bounds__(kF32Threads, 1)
   }
 
   // -------------------------------------------------------------- compute warps
-  const int box = warp >> 3;            // which 32-wide half of the K block
-  const int c = warp & 7;               // this warp's 16-byte chunk of each 128-byte row
-  // epilogue ownership: data row r_own, vocabulary rows v_own + 32 i
-  const int r_own = threadIdx.x & 15;
-  const int v_own = threadIdx.x >> 4;   // 0..31
-  float negb = 0.0f;
-  if (r_own < nrows && prior != nullptr) negb = -beta[row_position(row_pos, row0 + r_own, n_pos)];
-  long long best_key = kKeyEmpty;
+  const int box = warp >> 2;            // which 32-wide half of the K block
+  const int cp = (warp & 3) * 2;        // this warp's first 16-byte chunk of each 128-byte row
+  // epilogue ownership: vocabulary row v_e of the tile, data rows [8 rq, 8 rq + 8)
+  const bool epi = threadIdx.x < kF32EpiThreads;
+  const int v_e = threadIdx.x % kF32TileV;
+  const int rq = threadIdx.x / kF32TileV;
+  float negb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 8 * rq + i;
+    negb[i] = (epi && r < nrows && prior != nullptr) ? -beta[row_position(row_pos, row0 + r, n_pos)] : 0.0f;
+  }
+  long long best[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) best[i] = kKeyEmpty;
   int st = 0;
   uint32_t phase = 0;
   bool ok = true;
+  float4* red4 = reinterpret_cast<float4*>(red);  // [warp][row quad][v]
 
   for (int t = t_lo; t < t_hi && ok; ++t) {
     const int v0 = t * kF32TileV;
-    float2 acc[2][kF32Rows / 2];  // acc[j][p] = partial sums of data rows (2p, 2p + 1)
+    float2 acc[kF32VPerLane][kF32Rows / 2];  // acc[j][p] = partial sums of data rows (2p, 2p + 1)
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < kF32VPerLane; ++j)
 #pragma unroll
       for (int p = 0; p < kF32Rows / 2; ++p) acc[j][p] = make_float2(0.0f, 0.0f);
 
@@ -181,27 +196,30 @@ __global__ void __launch_bounds__(kF32Threads, 1)
       const uint8_t* stage = smem + st * kF32StageBytes;
       const uint8_t* wbox = stage + box * kF32WBox;
       const float* hbox = reinterpret_cast<const float*>(stage + 2 * kF32WBox + box * kF32HBox);  // [32 k][16]
-      {
-        float4 w[2];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = cp + cc;
+        float4 w[kF32VPerLane];
+#pragma unroll
+        for (int j = 0; j < kF32VPerLane; ++j) {
           const int v = lane + 32 * j;
           w[j] = *reinterpret_cast<const float4*>(wbox + v * 128 + ((c ^ (v & 7)) << 4));
         }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const float wk0 = kk == 0 ? w[0].x : (kk == 1 ? w[0].y : (kk == 2 ? w[0].z : w[0].w));
-          const float wk1 = kk == 0 ? w[1].x : (kk == 1 ? w[1].y : (kk == 2 ? w[1].z : w[1].w));
-          const float2 w0 = make_float2(wk0, wk0), w1 = make_float2(wk1, wk1);
           const float4* hk = reinterpret_cast<const float4*>(hbox + (c * 4 + kk) * kF32Rows);
+          float4 hv[kF32Rows / 4];
 #pragma unroll
-          for (int q = 0; q < kF32Rows / 4; ++q) {
-            const float4 hv = hk[q];  // data rows 4q .. 4q+3 at this k
-            const float2 ha = make_float2(hv.x, hv.y), hb = make_float2(hv.z, hv.w);
-            acc[0][2 * q] = __ffma2_rn(w0, ha, acc[0][2 * q]);
-            acc[0][2 * q + 1] = __ffma2_rn(w0, hb, acc[0][2 * q + 1]);
-            acc[1][2 * q] = __ffma2_rn(w1, ha, acc[1][2 * q]);
-            acc[1][2 * q + 1] = __ffma2_rn(w1, hb, acc[1][2 * q + 1]);
+          for (int q = 0; q < kF32Rows / 4; ++q) hv[q] = hk[q];  // data rows 4q .. 4q+3 at this k
+#pragma unroll
+          for (int j = 0; j < kF32VPerLane; ++j) {
+            const float wk = kk == 0 ? w[j].x : (kk == 1 ? w[j].y : (kk == 2 ? w[j].z : w[j].w));
+            const float2 w2 = make_float2(wk, wk);
+#pragma unroll
+            for (int q = 0; q < kF32Rows / 4; ++q) {
+              acc[j][2 * q] = __ffma2_rn(w2, make_float2(hv[q].x, hv[q].y), acc[j][2 * q]);
+              acc[j][2 * q + 1] = __ffma2_rn(w2, make_float2(hv[q].z, hv[q].w), acc[j][2 * q + 1]);
+            }
           }
         }
       }
@@ -214,26 +232,38 @@ __global__ void __launch_bounds__(kF32Threads, 1)
     }
     if (!ok) break;
 
-    // sum the 8 K slices: red[warp][v][r]
+    // sum the 8 K slices: red4[warp][q][v] holds data rows 4q .. 4q+3 of vocabulary row v
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float4* dst = reinterpret_cast<float4*>(red + (warp * kF32TileV + lane + 32 * j) * kF32Rows);
+    for (int j = 0; j < kF32VPerLane; ++j)
 #pragma unroll
       for (int q = 0; q < kF32Rows / 4; ++q)
-        dst[q] = make_float4(acc[j][2 * q].x, acc[j][2 * q].y, acc[j][2 * q + 1].x, acc[j][2 * q + 1].y);
-    }
+        red4[(warp * 4 + q) * kF32TileV + lane + 32 * j] =
+            make_float4(acc[j][2 * q].x, acc[j][2 * q].y, acc[j][2 * q + 1].x, acc[j][2 * q + 1].y);
     asm volatile("bar.sync 1, %0;" ::"r"(kF32ComputeWarps * 32) : "memory");
-    if (r_own < nrows) {
+    if (epi && v0 + v_e < V) {
+      float sum[8];
 #pragma unroll
-      for (int i = 0; i < kF32TileV / 32; ++i) {
-        const int v = v_own + 32 * i;
-        if (v0 + v < V) {
-          float s = 0.0f;
+      for (int i = 0; i < 8; ++i) sum[i] = 0.0f;
 #pragma unroll
-          for (int w8 = 0; w8 < kF32ComputeWarps; ++w8) s += red[(w8 * kF32TileV + v) * kF32Rows + r_own];
-          if (prior != nullptr) s = fmaf(negb, __ldg(prior + v0 + v), s);
-          const long long key = pack_key(s, (uint32_t)(v_begin + v0 + v));
-          best_key = key > best_key ? key : best_key;
+      for (int w8 = 0; w8 < kF32ComputeWarps; ++w8) {
+        const float4 a = red4[(w8 * 4 + 2 * rq) * kF32TileV + v_e];
+        const float4 b = red4[(w8 * 4 + 2 * rq + 1) * kF32TileV + v_e];
+        sum[0] += a.x;
+        sum[1] += a.y;
+        sum[2] += a.z;
+        sum[3] += a.w;
+        sum[4] += b.x;
+        sum[5] += b.y;
+        sum[6] += b.z;
+        sum[7] += b.w;
+      }
+      const float pv = prior != nullptr ? __ldg(prior + v0 + v_e) : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (8 * rq + i < nrows) {
+          const float sc = prior != nullptr ? fmaf(negb[i], pv, sum[i]) : sum[i];
+          const long long key = pack_key(sc, (uint32_t)(v_begin + v0 + v_e));
+          best[i] = key > best[i] ? key : best[i];
         }
       }
     }
@@ -246,16 +276,30 @@ __global__ void __launch_bounds__(kF32Threads, 1)
     while (globaltimer_ns() - t0 < kWaitLimitNs / 40) {
     }
   }
-  // combine the 16 threads that own each data row, one atomic per (row, CTA)
-  const long long other = __shfl_xor_sync(0xFFFFFFFFu, best_key, 16);
-  best_key = other > best_key ? other : best_key;
-  __shared__ long long row_best[kF32ComputeWarps][kF32Rows];
-  if (lane < 16) row_best[warp][lane] = best_key;
+  // Per data row: maximum over the lanes of each warp (a warp's lanes share rq), then
+  // over the three warps that own the row, one atomic per (row, CTA).
+  long long* rb = reinterpret_cast<long long*>(red);  // [warp][8], the sums are no longer needed
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    long long k = best[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const long long other = __shfl_xor_sync(0xFFFFFFFFu, k, o);
+      k = other > k ? other : k;
+    }
+    best[i] = k;
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) rb[warp * 8 + i] = epi ? best[i] : kKeyEmpty;
+  }
   asm volatile("bar.sync 1, %0;" ::"r"(kF32ComputeWarps * 32) : "memory");
-  if (threadIdx.x < kF32Rows && threadIdx.x < nrows) {
-    long long k = row_best[0][threadIdx.x];
-    for (int w8 = 1; w8 < kF32ComputeWarps; ++w8) k = row_best[w8][threadIdx.x] > k ? row_best[w8][threadIdx.x] : k;
-    if (k != kKeyEmpty) atomicMax(&keys[row0 + threadIdx.x], k);
+  if (threadIdx.x < kF32Rows && (int)threadIdx.x < nrows) {
+    const int r = threadIdx.x, q = r >> 3, i = r & 7;
+    constexpr int kWarpsPerQ = kF32TileV / 32;
+    long long k = kKeyEmpty;
+    for (int w8 = q * kWarpsPerQ; w8 < (q + 1) * kWarpsPerQ; ++w8) k = rb[w8 * 8 + i] > k ? rb[w8 * 8 + i] : k;
+    if (k != kKeyEmpty) atomicMax(&keys[row0 + r], k);
   }
 }
 

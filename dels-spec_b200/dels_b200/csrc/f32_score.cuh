@@ -5,7 +5,7 @@
 
 namespace dels {
 
-constexpr int kF32Threads = 544;  // 16 compute warps + 1 TMA producer warp
+constexpr int kF32Threads = 288;  // 8 compute warps + 1 TMA producer warp
 
 
 __global__ void f32_rank_kernel(const float* __restrict__ h, long long ld_h, const float* __restrict__ ut,
@@ -20,9 +20,11 @@ __global__ void f32_transpose_pass_kernel(const float* __restrict__ h, long long
 // Sets the dynamic shared-memory limit of the fp32 scorer and loads it.
 cudaError_t f32_score_setup(int max_smem);
 int f32_score_smem_bytes();
+// Vocabulary rows per tile of the fp32 scorer (the box height of its W / Vr tensor maps).
+int f32_score_tile_rows();
 
 // One pass of the fp32 scorer over data rows [row0, row0 + nrows), nrows <= 16.
-// map_w / map_vr: fp32 [V, H] / [V, r], box 32 x 64 rows, 128-byte swizzle;
+// map_w / map_vr: fp32 [V, H] / [V, r], box 32 x f32_score_tile_rows() rows, 128-byte swizzle;
 // map_h / map_s: the pass's rows transposed, fp32 [H][16] / [r][16], box 16 x 32 k, no
 // swizzle (f32_transpose_pass_kernel).
 cudaError_t f32_score_launch(int grid, cudaStream_t st, const CUtensorMap& map_w, const CUtensorMap& map_h,
