@@ -80,24 +80,72 @@ __device__ __forceinline__ int32_t ordered_i32_dev(float f) {
   return f != f ? 0x7FFFFFFF : o;
 }
 
-// Packed key (pack_key order) of the best of sc[0..valid) with global indices idx0 + j:
-// a 5-level tree of 64-bit maxima, branch-free, so its latency is a few dependent
-// steps rather than one compare-and-select per column.  Entries past `valid` do not
-// take part.
-__device__ __forceinline__ long long chunk_best_key(const float (&sc)[32], int valid, uint32_t idx0) {
-  long long k[32];
+// max(a, b) / max(a, b, c) that return NaN when any input is NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Score threshold of a running key for chunk_fold: -inf for the empty key, +inf once a
+// NaN holds it (only a NaN at a lower index could still win, and NaN chunks always fold).
+__device__ __forceinline__ float key_threshold(long long key) {
+  if (key == kKeyEmpty) return -__int_as_float(0x7f800000);
+  const float f = key_score(key);
+  return f != f ? __int_as_float(0x7f800000) : f;
+}
+
+// Folds the chunk sc[0..valid) (global indices idx0 + j) into the running packed key
+// best_key, i.e. best_key = max(best_key, max_j pack_key(sc[j], idx0 + j)): the largest
+// score, NaN above everything, -0 equal to +0, the lowest index among equal scores.
+//
+// The NaN-propagating maximum m of the chunk comes from a tree of three-input maxima (entries past
+// `valid` read as -inf).  A chunk with m below `thr` -- a score some column of the row
+// already reached: this thread's best so far, or the row's global key read at the start
+// of the tile -- cannot hold the argmax and is done.  Otherwise the lowest column whose
+// score equals m (or is NaN when m is NaN) comes from a 32-bit match mask and ONE key is
+// packed.  Packing and reducing a 64-bit key per column took ~11 instructions per column;
+// issued on the SM sub-partitions that also run the MMA-issuing and TMA warps, that cost
+// the paired scorer ~4 points of tensor-pipe utilisation (ncu).
+__device__ __forceinline__ void chunk_fold(const float (&sc)[32], int valid, uint32_t idx0, long long& best_key,
+                                           float& thr) {
+  float x[32];
+  if (valid >= 32) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const long long key = (long long)(((unsigned long long)(uint32_t)ordered_i32_dev(sc[j]) << 32) |
-                                      (unsigned long long)(0xFFFFFFFFu - (idx0 + (uint32_t)j)));
-    k[j] = j < valid ? key : kKeyEmpty;
+    for (int j = 0; j < 32; ++j) x[j] = sc[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = j < valid ? sc[j] : -__int_as_float(0x7f800000);
   }
+  // 32 -> 12 -> 4 -> 1 with three-input maxima
+  float t[12];
 #pragma unroll
-  for (int w = 1; w < 32; w *= 2) {
+  for (int j = 0; j < 10; ++j) t[j] = fmax3_nan(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+  t[10] = x[30];
+  t[11] = x[31];
+  float u[4];
 #pragma unroll
-    for (int j = 0; j < 32; j += 2 * w) k[j] = k[j + w] > k[j] ? k[j + w] : k[j];
+  for (int j = 0; j < 4; ++j) u[j] = fmax3_nan(t[3 * j], t[3 * j + 1], t[3 * j + 2]);
+  const float m = fmax_nan(fmax3_nan(u[0], u[1], u[2]), u[3]);
+  if (m < thr) return;
+  uint32_t mask = 0u;
+  if (m == m) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mask |= x[j] == m ? (1u << j) : 0u;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mask |= x[j] != x[j] ? (1u << j) : 0u;
   }
-  return k[0];
+  const uint32_t first = (uint32_t)(__ffs((int)mask) - 1);
+  const long long key = (long long)(((unsigned long long)(uint32_t)ordered_i32_dev(m) << 32) |
+                                    (unsigned long long)(0xFFFFFFFFu - (idx0 + first)));
+  best_key = key > best_key ? key : best_key;
+  thr = m == m ? m : __int_as_float(0x7f800000);
 }
 
 // Row position (the draft-block slot that selects alpha_p / beta_p).

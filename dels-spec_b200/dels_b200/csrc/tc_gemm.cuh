@@ -408,6 +408,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           __syncwarp();
         }
         long long best_key = kKeyEmpty;
+        // the row's best score so far on the device: chunk_fold skips chunks below it
+        float thr = row_ok ? key_threshold(__ldcg(&args.keys[row])) : -__int_as_float(0x7f800000);
 #pragma unroll 1
         for (int c = 0; c < (warp_rows ? nchunks : 0); ++c) {
           uint32_t v[32];
@@ -437,10 +439,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                   const float4 p = reinterpret_cast<const float4*>(prior_s + c0)[q];
-                  sc[4 * q + 0] = fmaf(negb, p.x, sc[4 * q + 0]);
-                  sc[4 * q + 1] = fmaf(negb, p.y, sc[4 * q + 1]);
-                  sc[4 * q + 2] = fmaf(negb, p.z, sc[4 * q + 2]);
-                  sc[4 * q + 3] = fmaf(negb, p.w, sc[4 * q + 3]);
+                  // two packed two-lane FMAs: the rounding of four fmaf
+                  const float2 lo = __ffma2_rn(make_float2(negb, negb), make_float2(p.x, p.y),
+                                               make_float2(sc[4 * q + 0], sc[4 * q + 1]));
+                  const float2 hi = __ffma2_rn(make_float2(negb, negb), make_float2(p.z, p.w),
+                                               make_float2(sc[4 * q + 2], sc[4 * q + 3]));
+                  sc[4 * q + 0] = lo.x;
+                  sc[4 * q + 1] = lo.y;
+                  sc[4 * q + 2] = hi.x;
+                  sc[4 * q + 3] = hi.y;
                 }
               }
             } else {
@@ -469,10 +476,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                   for (int q = 0; q < 8; ++q) {
                     const float4 p = __ldg(reinterpret_cast<const float4*>(prow + c0) + q);
-                    sc[4 * q + 0] = fmaf(negb, p.x, sc[4 * q + 0]);
-                    sc[4 * q + 1] = fmaf(negb, p.y, sc[4 * q + 1]);
-                    sc[4 * q + 2] = fmaf(negb, p.z, sc[4 * q + 2]);
-                    sc[4 * q + 3] = fmaf(negb, p.w, sc[4 * q + 3]);
+                    // two packed two-lane FMAs: the rounding of four fmaf
+                    const float2 lo = __ffma2_rn(make_float2(negb, negb), make_float2(p.x, p.y),
+                                                 make_float2(sc[4 * q + 0], sc[4 * q + 1]));
+                    const float2 hi = __ffma2_rn(make_float2(negb, negb), make_float2(p.z, p.w),
+                                                 make_float2(sc[4 * q + 2], sc[4 * q + 3]));
+                    sc[4 * q + 0] = lo.x;
+                    sc[4 * q + 1] = lo.y;
+                    sc[4 * q + 2] = hi.x;
+                    sc[4 * q + 3] = hi.y;
                   }
                 } else {
 #pragma unroll
@@ -481,8 +493,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
               }
             }
-            const long long ck = chunk_best_key(sc, ncols - c0, (uint32_t)(args.v_begin + n0 + c0));
-            best_key = ck > best_key ? ck : best_key;
+            chunk_fold(sc, ncols - c0, (uint32_t)(args.v_begin + n0 + c0), best_key, thr);
           }
         }
         tc_fence_before();

@@ -253,6 +253,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           (args.base != nullptr && row_ok) ? args.base + (long long)row * args.ld_base + n0 : nullptr;
       const float* prow = args.prior != nullptr ? args.prior + n0 : nullptr;
       long long best_key = kKeyEmpty;
+      // the row's best score so far on the device: chunk_fold skips chunks below it
+      float thr = row_ok ? key_threshold(__ldcg(&args.keys[row])) : -__int_as_float(0x7f800000);
       // A warp whose 32 rows are all past the end skips the tile (warp-uniform, so the
       // collective tensor-memory loads stay aligned); lanes past the end skip the
       // arithmetic.
@@ -293,10 +295,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 const float4 p = __ldg(reinterpret_cast<const float4*>(prow + c0) + q);
-                sc[4 * q + 0] = fmaf(negb, p.x, sc[4 * q + 0]);
-                sc[4 * q + 1] = fmaf(negb, p.y, sc[4 * q + 1]);
-                sc[4 * q + 2] = fmaf(negb, p.z, sc[4 * q + 2]);
-                sc[4 * q + 3] = fmaf(negb, p.w, sc[4 * q + 3]);
+                // two packed two-lane FMAs: the rounding of four fmaf
+                const float2 lo = __ffma2_rn(make_float2(negb, negb), make_float2(p.x, p.y),
+                                             make_float2(sc[4 * q + 0], sc[4 * q + 1]));
+                const float2 hi = __ffma2_rn(make_float2(negb, negb), make_float2(p.z, p.w),
+                                             make_float2(sc[4 * q + 2], sc[4 * q + 3]));
+                sc[4 * q + 0] = lo.x;
+                sc[4 * q + 1] = lo.y;
+                sc[4 * q + 2] = hi.x;
+                sc[4 * q + 3] = hi.y;
               }
             } else {
 #pragma unroll
@@ -304,8 +311,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                 if (c0 + j < ncols) sc[j] = fmaf(negb, __ldg(prow + c0 + j), sc[j]);
             }
           }
-          const long long ck = chunk_best_key(sc, ncols - c0, (uint32_t)(args.v_begin + n0 + c0));
-          best_key = ck > best_key ? ck : best_key;
+          chunk_fold(sc, ncols - c0, (uint32_t)(args.v_begin + n0 + c0), best_key, thr);
         }
       }
       tc_fence_before();

@@ -2,8 +2,9 @@
 
     python dels-spec_b200/dels_b200/profile_step.py --workload cfg2 --kernel scorer --launches 4
 
-``--kernel scorer`` launches the fused tcgen05 scorer (keys pre-initialised, so each
-call is exactly one kernel); ``--kernel step`` runs whole draft-scoring steps
+``--kernel scorer`` launches the fused tcgen05 scorer, each call after a small
+keys-reset kernel (the scorer's epilogue skips chunks below the row's best key so far,
+so every profiled launch starts from empty keys); ``--kernel step`` runs whole draft-scoring steps
 (projection + finalisation + scorer); ``--kernel f32`` runs the fp32 scorer step.
 All inputs are generated and the rank operand computed before the first profiled
 launch, so with ``ncu -k regex:<name> -s <launches-1> -c 1`` the capture is a single
@@ -56,7 +57,7 @@ def main() -> None:
     for _ in range(args.launches):
         if args.kernel == "scorer":
             ops.fused_argmax_bf16(h, t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=wl.n_pos,
-                                  keys_ready=True, out=out, ws=ws)
+                                  keys_ready=False, out=out, ws=ws)
         elif args.kernel == "step":
             ops.draft_score_bf16(h, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
                                  out=out, ws=ws)
