@@ -249,6 +249,31 @@ def test_edge_cases(cuda_device, rows):
     torch.cuda.synchronize()
 
 
+@pytest.mark.parametrize("rows", [3, 40, 150, 300], ids=["skinny", "tile", "pair", "pair2"])
+def test_integer_score_ties(cuda_device, rows):
+    """Scores that are small integers, so most rows have their maximum at many columns spread
+    over chunks, tiles and CTAs: the token must be the first of them exactly (torch.argmax).
+    V = 5003 leaves a partial last chunk and tile."""
+    from dels_b200 import ops
+
+    dev = cuda_device
+    g = torch.Generator(device="cpu").manual_seed(11)
+    H, r, V = 64, 64, 5003
+    h = (torch.rand(rows, H, generator=g) < 0.15).float()
+    W = torch.randint(-1, 2, (V, H), generator=g).float()
+    prior = torch.randint(0, 2, (V,), generator=g).float()
+    Ut = torch.zeros(r, H)
+    Vr = torch.randint(-1, 2, (V, r), generator=g).float()
+    ref = h.double() @ W.double().T - prior.double()[None, :]  # exact: small integers
+    expect = ref.argmax(dim=1)
+    assert ((ref == ref.max(dim=1, keepdim=True).values).sum(dim=1) > 1).float().mean() > 0.5  # ties are common
+    bf = lambda t: t.to(dev, torch.bfloat16)  # noqa: E731
+    one = torch.ones(1, device=dev)
+    out = ops.draft_score_bf16(bf(h), bf(W), bf(Ut), bf(Vr), prior.to(dev), one, one, with_scores=True)
+    assert out.tokens.cpu().tolist() == expect.tolist()
+    assert out.scores.cpu().double().tolist() == ref.max(dim=1).values.tolist()
+
+
 def test_keys_only_vocab_shards_combine(cuda_device):
     """Vocab-sharded scoring emulated on one GPU: per-slice keys + max = full result."""
     from dels_b200 import ops, workloads
