@@ -148,6 +148,39 @@ def test_runner_full_vocab_b1(cuda_device):
     assert _compare(out.cpu().numpy(), gaps, toks, 1e-2) >= 3
 
 
+@pytest.mark.parametrize("B", [5, 20, 48, 64])
+def test_runner_batches(cuda_device, B):
+    """Batch sizes past the fixtures': the plain (<= 4 rows) and staged skinny scorers (16- and
+    32-column row tiles), the 128-row tile scorer (33..128 rows) and the GRU step's loop over
+    16-row chunks, each against the oracle rollout."""
+    from kernel.dels import DeLSGraphRunner
+
+    rng = np.random.default_rng(100 + B)
+    V, E, G, r, steps = 2003, 40, 64, 32, 4
+    w = {
+        "embed": O.bf16_round((rng.standard_normal((V, E)) * 0.5).astype(np.float32)),
+        "w_ih": O.bf16_round((rng.standard_normal((3 * G, E)) * 0.2).astype(np.float32)),
+        "w_hh": O.bf16_round((rng.standard_normal((3 * G, G)) * 0.2).astype(np.float32)),
+        "w_rank": O.bf16_round((rng.standard_normal((r, G)) * 0.3).astype(np.float32)),
+        "Vr": O.bf16_round((rng.standard_normal((V, r)) * 0.3).astype(np.float32)),
+    }
+    head = _head(cuda_device, V, E, G, r, "identity", w)
+    prior = O.bf16_round(O.zipf_log_prior(V).astype(np.float32))
+    alpha = list(np.linspace(0.9, 0.5, steps))
+    beta = list(np.linspace(0.3, 0.1, steps))
+    runner = DeLSGraphRunner(local_head=head, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha,
+                             beta_values=beta, baseline_logits=torch.from_numpy(prior).to(cuda_device),
+                             device=cuda_device)
+    base = O.bf16_round(rng.standard_normal((B, steps, V)).astype(np.float32))
+    prefix = rng.integers(0, V, (B, 1))
+    out = runner(torch.from_numpy(prefix).to(cuda_device),
+                 torch.from_numpy(base).to(cuda_device).to(torch.bfloat16)).cpu().numpy()
+    toks, gaps = O.dels_runner_rollout(prefix, base, embed=w["embed"], w_ih=w["w_ih"], w_hh=w["w_hh"],
+                                       w_rank=w["w_rank"], Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta,
+                                       bf16=True)
+    assert _compare(out, gaps, toks, 1e-2) >= B * steps // 2
+
+
 def test_fused_long_logit_runner_matches_oracle(cuda_device):
     """DeLSFusedGraphRunner: long logits computed inside the scorer from the hidden states."""
     from kernel.dels import DeLSFusedGraphRunner
