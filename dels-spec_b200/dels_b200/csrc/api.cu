@@ -241,6 +241,7 @@ int init_device(int dev) {
     SET(rank_gemv_kernel, kMaxSmem);
     SET(linear_finalize_kernel, 0);
     SET(gather_scaled_kernel, 0);
+    SET(gru_gates_kernel, 0);
     SET(wait_selftest_kernel, 0);
 #undef SET
   }
@@ -969,6 +970,29 @@ int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi
       reinterpret_cast<const __nv_bfloat16*>(w_hh), reinterpret_cast<const __nv_bfloat16*>(b_hh),
       reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V,
       status));
+  return DELS_OK;
+}
+
+int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+                        const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V, void* ws,
+                        void* stream) {
+  if (B < 0 || G <= 0 || V <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d V=%d", B, G, V);
+  if (tokens == nullptr || gi_table == nullptr || gh == nullptr || h_out == nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if (ld_table < 3LL * G) return fail(DELS_ERR_INVALID_ARG, "gi table leading dimension < 3G");
+  if (ld_gh < 3LL * G) return fail(DELS_ERR_INVALID_ARG, "gh leading dimension < 3G");
+  int* status = ws != nullptr ? reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + 4) : nullptr;
+  DeviceState* ds = nullptr;
+  int rc;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (B == 0) return DELS_OK;
+  const long long total = (long long)B * G;
+  const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
+  DELS_CHECK_PDL("gru_gates_kernel launch", launch_pdl(gru_gates_kernel, dim3(grid), dim3(256), 0,
+      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<const long long*>(tokens), tok_stride,
+      reinterpret_cast<const __nv_bfloat16*>(gi_table), ld_table, reinterpret_cast<const __nv_bfloat16*>(gh),
+      (long long)ld_gh, reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G,
+      V, status));
   return DELS_OK;
 }
 

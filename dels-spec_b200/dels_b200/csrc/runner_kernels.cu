@@ -238,6 +238,33 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
   pdl_trigger();
 }
 
+// The GRU gates for batches where gh = bf16(W_hh h + b_hh) came from the tensor-core
+// projection (dels_linear_bf16): one thread per (row, unit), the same gate arithmetic as
+// gru_step_kernel.
+__global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long tok_stride,
+                                 const __nv_bfloat16* __restrict__ table, long long ld_table,
+                                 const __nv_bfloat16* __restrict__ gh, long long ld_gh, const __nv_bfloat16* h_in,
+                                 __nv_bfloat16* h_out, int B, int G, int V, int* status) {
+  pdl_wait();
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < (long long)B * G;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(e / G), g = (int)(e % G);
+    long long tok = tokens[(long long)b * tok_stride];
+    if (tok < 0 || tok >= V) {
+      if (status != nullptr) atomicCAS(status, 0, DELS_ERR_INVALID_ARG);
+      tok = tok < 0 ? 0 : V - 1;
+    }
+    const __nv_bfloat16* gi = table + tok * ld_table;
+    const __nv_bfloat16* ghb = gh + (long long)b * ld_gh;
+    const float h = h_in != nullptr ? __bfloat162float(h_in[(long long)b * G + g]) : 0.0f;
+    const float rg = sigmoidf_(__bfloat162float(gi[g]) + __bfloat162float(ghb[g]));
+    const float zg = sigmoidf_(__bfloat162float(gi[G + g]) + __bfloat162float(ghb[G + g]));
+    const float ng = tanhf(__bfloat162float(gi[2 * G + g]) + rg * __bfloat162float(ghb[2 * G + g]));
+    h_out[(long long)b * G + g] = __float2bfloat16_rn((1.0f - zg) * ng + zg * h);
+  }
+  pdl_trigger();
+}
+
 __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride,
                                      const __nv_bfloat16* __restrict__ emb, long long ld_emb,
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,

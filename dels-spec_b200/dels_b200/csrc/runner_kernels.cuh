@@ -27,6 +27,11 @@ __global__ void rank_gemv_kernel(const __nv_bfloat16* __restrict__ x, long long 
                                  const float* __restrict__ alpha, int n_pos, const int* __restrict__ row_pos,
                                  __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter);
 
+__global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long tok_stride,
+                                 const __nv_bfloat16* __restrict__ table, long long ld_table,
+                                 const __nv_bfloat16* __restrict__ gh, long long ld_gh, const __nv_bfloat16* h_in,
+                                 __nv_bfloat16* h_out, int B, int G, int V, int* status);
+
 __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride,
                                      const __nv_bfloat16* __restrict__ emb, long long ld_emb,
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,

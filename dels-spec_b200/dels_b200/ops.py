@@ -526,6 +526,33 @@ def gru_step(
     return h_out
 
 
+def gru_gates(
+    tokens: torch.Tensor,
+    gi_table: torch.Tensor,
+    gh: torch.Tensor,
+    h_in: torch.Tensor | None,
+    h_out: torch.Tensor,
+    *,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """h_out = GRU gates(gi_table[tokens], gh, h_in) for a precomputed gh = bf16(W_hh h + b_hh)."""
+    _require_cuda("tokens", tokens, torch.int64)
+    _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
+    _require_cuda("gh", gh, torch.bfloat16, 2)
+    _require_cuda("h_out", h_out, torch.bfloat16, 2)
+    B, G = h_out.shape
+    V = gi_table.shape[0]
+    if gh.shape != (B, 3 * G) or gh.stride(1) != 1 or gi_table.shape[1] != 3 * G or not h_out.is_contiguous():
+        raise ValueError("GRU gate operands do not match the hidden size")
+    if h_in is not None and (h_in.shape != (B, G) or not h_in.is_contiguous()):
+        raise ValueError("h_in must be a contiguous [B, G] tensor")
+    tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
+    _lib.call("dels_gru_gates_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+              _ptr(gh), gh.stride(0), _ptr(h_in), _ptr(h_out), B, G, V, None if ws is None else ws.ptr,
+              _stream(h_out.device))
+    return h_out
+
+
 def rank_gemv(
     x: torch.Tensor,
     w: torch.Tensor,
@@ -574,6 +601,14 @@ def gather_scaled_rows(
               _ptr(alpha), int(n_pos), B, r, emb.shape[0], _ptr(s_scaled), _ptr(keys),
               None if ws is None else ws.ptr, _stream(s_scaled.device))
     return s_scaled
+
+
+def linear_workspace_bytes(rows: int, K: int, N: int) -> int:
+    return int(_lib.query("dels_linear_workspace_bytes", rows, K, N))
+
+
+def rank_workspace_bytes(rows: int, K: int, r: int) -> int:
+    return int(_lib.query("dels_rank_workspace_bytes", rows, K, r))
 
 
 def linear_bf16(

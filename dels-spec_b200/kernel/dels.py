@@ -21,6 +21,8 @@ code/benchmark.py:303-309); other dtypes raise ``ValueError``.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from dels_b200 import ops
@@ -137,6 +139,19 @@ class DeLSGraphRunner:
         self._keys = torch.empty(B, dtype=torch.int64, device=device)
         self._ws = ops.Workspace(1 << 12, device)
         self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
+        # From DELS_RUNNER_TC_ROWS rows up (default 16) the GRU's W_hh product and the rank
+        # projection run as tensor-core split-K GEMMs (then the gates / the rank
+        # finalisation); below it one warp per weight row does each in a single launch.
+        tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
+        self._tc = B >= tc_rows and self.rank_bias is None
+        if self._tc:
+            need = max(ops.linear_workspace_bytes(B, G, 3 * G), ops.rank_workspace_bytes(B, G, r))
+            self._tc_ws = ops.Workspace(need, device)
+            self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
+            # the first step's h is zero, so its gh is the bias alone
+            self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
+            if self.gru_b_hh is not None:
+                self._gh0.copy_(self.gru_b_hh.to(dtype)[None, :].expand(B, -1))
 
         ops.init(device)
         stream = torch.cuda.Stream(device=device)
@@ -150,18 +165,34 @@ class DeLSGraphRunner:
         with torch.inference_mode(), torch.cuda.graph(self.graph):
             self._forward_impl()
 
-    def _forward_impl(self):
-        prefix = self.static_prefix_ids[:, 0]
-        h_cur = ops.gru_step(prefix, self._gru_input_proj_table, self.gru_w_hh, None, self._h[0],
-                             b_hh=self.gru_b_hh, ws=self._ws)
-        nxt = 1
-        for step in range(self.steps):
+    def _gru(self, tokens, h_in, h_out):
+        if not self._tc:
+            return ops.gru_step(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out, b_hh=self.gru_b_hh,
+                                ws=self._ws)
+        if h_in is None:
+            gh = self._gh0
+        else:
+            gh = ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh, ws=self._tc_ws)
+        return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws)
+
+    def _rank(self, h_cur, step: int):
+        if not self._tc:
             ops.rank_gemv(h_cur, self.rank_weight, self._alpha[step : step + 1], self._s_scaled,
                           bias=self.rank_bias, activation=self._activation, keys=self._keys, ws=self._ws)
+        else:
+            ops.rank_project_bf16(h_cur, self.rank_weight, self._alpha[step : step + 1], n_pos=1,
+                                  activation=self._activation, s_scaled=self._s_scaled, keys=self._keys,
+                                  want_state=False, ws=self._tc_ws)
+
+    def _forward_impl(self):
+        prefix = self.static_prefix_ids[:, 0]
+        h_cur = self._gru(prefix, None, self._h[0])
+        nxt = 1
+        for step in range(self.steps):
+            self._rank(h_cur, step)
             self._score(step)
             if step + 1 < self.steps:
-                h_cur = ops.gru_step(self._tokens[step], self._gru_input_proj_table, self.gru_w_hh, h_cur,
-                                     self._h[nxt], b_hh=self.gru_b_hh, ws=self._ws)
+                h_cur = self._gru(self._tokens[step], h_cur, self._h[nxt])
                 nxt ^= 1
         self.static_out.copy_(self._tokens.t())
 

@@ -214,6 +214,16 @@ DELS_API int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const
                                 const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G,
                                 int V, void* ws, void* stream);
 
+/* The gates of the same GRU step when gh = bf16(W_hh . h_in + b_hh) [B, 3G] (row stride
+ * ld_gh) was computed separately, e.g. by dels_linear_bf16 for larger batches, where the
+ * tensor-core projection beats one warp per gate row (code/kernel/dels.py:368-373):
+ *   r, z = sigmoid(gi + gh), n = tanh(gi_n + r * gh_n), h_out[b] = bf16((1 - z) n + z h_in[b]),
+ * gi = gi_table[tokens[b * tok_stride]], h_in NULL = zero state.  Out-of-range ids are
+ * clamped and flagged as in dels_gru_step_bf16. */
+DELS_API int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+                                 const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V,
+                                 void* ws, void* stream);
+
 /* Rank projection for small batches (code/kernel/dels.py:437-443):
  *   s = bf16(act(bf16(x . w^T + bias))), s_scaled = bf16(alpha_p * s), keys[0..B) reset,
  * one warp per output feature.  K % 8 == 0.  ws (optional) supplies the counter that
