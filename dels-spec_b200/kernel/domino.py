@@ -24,6 +24,8 @@ must be bf16.  Other forms raise ``ValueError``.
 
 from __future__ import annotations
 
+import os
+
 from typing import Tuple
 
 import torch
@@ -155,6 +157,15 @@ class DraftCorrectionGraphRunner:
         self._ws = ops.Workspace(1 << 12, device)
         self._ws_lin = ops.Workspace(1 << 12, device)
         self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
+        # From DELS_RUNNER_TC_ROWS rows up (default 16) the GRU's W_hh product runs as the
+        # tensor-core split-K GEMM, then the gates (as in kernel/dels.py).
+        self._tc = B >= int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
+        if self._tc:
+            self._tc_ws = ops.Workspace(ops.linear_workspace_bytes(B, G, 3 * G), device)
+            self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
+            self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
+            if self.gru_b_hh is not None:
+                self._gh0.copy_(self.gru_b_hh[None, :].expand(B, -1))
 
         ops.init(device)
         stream = torch.cuda.Stream(device=device)
@@ -168,6 +179,14 @@ class DraftCorrectionGraphRunner:
         with torch.inference_mode(), torch.cuda.graph(self.graph):
             self._forward_impl()
 
+    def _gru(self, tokens, h_in, h_out):
+        if not self._tc:
+            return ops.gru_step(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out, b_hh=self.gru_b_hh,
+                                ws=self._ws)
+        gh = self._gh0 if h_in is None else ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh,
+                                                           ws=self._tc_ws)
+        return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws)
+
     def _forward_impl(self):
         B, S, H, M = self.batch_size, self.steps, self.hidden_dim, self._m
         if S > 0:
@@ -177,8 +196,7 @@ class DraftCorrectionGraphRunner:
         h = None
         cur = 0
         for p in range(self.prefix_token_count):
-            h = ops.gru_step(self.static_prefix_ids[:, p], self._gru_input_proj_table, self.gru_w_hh, h,
-                             self._h[cur], b_hh=self.gru_b_hh, ws=self._ws)
+            h = self._gru(self.static_prefix_ids[:, p], h, self._h[cur])
             cur ^= 1
         for t in range(S):
             ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys, ws=self._ws)
@@ -187,8 +205,7 @@ class DraftCorrectionGraphRunner:
                 n_pos=1, keys_ready=True, out=self._outs[t], ws=self._ws,
             )
             if t + 1 < S:
-                h = ops.gru_step(self._tokens[t], self._gru_input_proj_table, self.gru_w_hh, h, self._h[cur],
-                                 b_hh=self.gru_b_hh, ws=self._ws)
+                h = self._gru(self._tokens[t], h, self._h[cur])
                 cur ^= 1
         if S > 0:
             self.static_out.copy_(self._tokens[:S].t())
