@@ -498,7 +498,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(tempty_bar(acc));
-        if (row_ok) {
+        if (row_ok && best_key != kKeyEmpty) {  // empty: every chunk fell below the row's best
           atomicMax(&args.keys[row], best_key);
           __threadfence();
         }

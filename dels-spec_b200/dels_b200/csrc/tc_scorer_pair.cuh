@@ -322,7 +322,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         else
           mbar_arrive_remote(acc == 0 ? tempty_leader0 : tempty_leader1);
       }
-      if (row_ok) {
+      if (row_ok && best_key != kKeyEmpty) {  // empty: every chunk fell below the row's best
         atomicMax(&args.keys[row], best_key);
         __threadfence();
       }
