@@ -240,6 +240,7 @@ int init_device(int dev) {
     SET(gru_step_kernel, kMaxSmem);
     SET(rank_gemv_kernel, kMaxSmem);
     SET(linear_finalize_kernel, 0);
+    SET(correction_finalize_kernel, 0);
     SET(gather_scaled_kernel, 0);
     SET(gru_gates_kernel, 0);
     SET(wait_selftest_kernel, 0);
@@ -1068,6 +1069,35 @@ int dels_linear_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, c
   DELS_CHECK_PDL("linear_finalize_kernel launch", launch_pdl(linear_finalize_kernel, dim3(grid), dim3(256), 0, st,
       partials, plan.splits, (long long)rows * plan.ld_out, (long long)plan.ld_out, rows, N,
       reinterpret_cast<const __nv_bfloat16*>(bias), reinterpret_cast<__nv_bfloat16*>(out), (long long)ld_out));
+  return DELS_OK;
+}
+
+int dels_correction_mid_tc_bf16(const void* h, int64_t ld_h, const void* w_s, int64_t ld_ws, const void* z,
+                                int64_t ld_z, int B, int G, int M, const float* alpha, void* s_scaled, int64_t* keys,
+                                void* ws, size_t ws_bytes, void* stream) {
+  int rc;
+  if (B < 0 || G <= 0 || M <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d M=%d", B, G, M);
+  if (z == nullptr || s_scaled == nullptr || alpha == nullptr) return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if (ld_z < M) return fail(DELS_ERR_INVALID_ARG, "z leading dimension %lld < %d", (long long)ld_z, M);
+  if ((rc = check_bf16_matrix("h", h, ld_h, G)) != DELS_OK) return rc;
+  if ((rc = check_bf16_matrix("w_s", w_s, ld_ws, G)) != DELS_OK) return rc;
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, dels_linear_workspace_bytes(B, G, M), &hdr)) != DELS_OK) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (B == 0) return DELS_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + DELS_WS_HEADER_BYTES);
+  SplitPlan plan;
+  if ((rc = launch_projection(h, ld_h, w_s, ld_ws, B, G, M, partials, hdr.status, ds->sm_count, st, &plan)) !=
+      DELS_OK)
+    return rc;
+  const long long total = (long long)B * M;
+  const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
+  DELS_CHECK_PDL("correction_finalize_kernel launch", launch_pdl(correction_finalize_kernel, dim3(grid), dim3(256),
+      0, st, partials, plan.splits, (long long)B * plan.ld_out, (long long)plan.ld_out, B, M,
+      reinterpret_cast<const __nv_bfloat16*>(z), (long long)ld_z, alpha, reinterpret_cast<__nv_bfloat16*>(s_scaled),
+      reinterpret_cast<long long*>(keys), hdr.counter));
   return DELS_OK;
 }
 

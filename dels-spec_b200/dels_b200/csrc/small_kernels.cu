@@ -43,6 +43,33 @@ __global__ void rank_finalize_kernel(const float* __restrict__ partials, int spl
 }
 
 // -----------------------------------------------------------------------------------
+// Domino correction-MLP hidden layer after the split-K projection s = W_s h:
+// s_scaled = bf16(alpha[0] * SiLU(z + bf16(s))), SiLU in fp32 (code/kernel/domino.py:92-97,
+// :113, :422), the same arithmetic as rank_gemv_kernel's addend path; keys reset.
+// -----------------------------------------------------------------------------------
+__global__ void correction_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
+                                           long long ld_part, int rows, int m, const __nv_bfloat16* __restrict__ z,
+                                           long long ld_z, const float* __restrict__ alpha, __nv_bfloat16* s_scaled,
+                                           long long* keys, unsigned* counter) {
+  pdl_wait();
+  const long long total = (long long)rows * m;
+  const float a = alpha != nullptr ? alpha[0] : 1.0f;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / m);
+    const int col = (int)(i - (long long)row * m);
+    const long long pi = (long long)row * ld_part + col;
+    float acc = 0.0f;
+    for (int sp = 0; sp < splits; ++sp) acc += partials[sp * split_stride + pi];
+    const float pre = __bfloat162float(z[(long long)row * ld_z + col]) + __bfloat162float(__float2bfloat16_rn(acc));
+    s_scaled[i] = __float2bfloat16_rn(a * (pre / (1.0f + expf(-pre))));
+    if (keys != nullptr && col == 0) keys[row] = kKeyEmpty;
+  }
+  if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
+  pdl_trigger();
+}
+
+// -----------------------------------------------------------------------------------
 // F.linear epilogue: out[row, n] = bf16(sum of the split-K partials + bias[n]).  The bias
 // joins the fp32 accumulator before the single rounding, like the bias epilogue of the
 // bf16 GEMM behind F.linear (code/kernel/domino.py:404-408, :325-327).

@@ -12,6 +12,10 @@ __global__ void rank_finalize_kernel(const float* __restrict__ partials, int spl
                                      int n_pos, const int* __restrict__ row_pos, __nv_bfloat16* s_out,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter);
 
+__global__ void correction_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
+                                           long long ld_part, int rows, int m, const __nv_bfloat16* __restrict__ z,
+                                           long long ld_z, const float* __restrict__ alpha, __nv_bfloat16* s_scaled,
+                                           long long* keys, unsigned* counter);
 __global__ void linear_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
                                        long long ld_part, int rows, int n, const __nv_bfloat16* __restrict__ bias,
                                        __nv_bfloat16* out, long long ld_out);

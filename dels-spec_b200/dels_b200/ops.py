@@ -666,6 +666,32 @@ def correction_mid(
     return s_scaled
 
 
+def correction_mid_tc(
+    h: torch.Tensor,
+    w_s: torch.Tensor,
+    z: torch.Tensor,
+    alpha: torch.Tensor,
+    s_scaled: torch.Tensor,
+    *,
+    keys: torch.Tensor | None = None,
+    ws: Workspace,
+) -> torch.Tensor:
+    """correction_mid with W_s h on the tensor-core split-K GEMM (larger batches);
+    ``ws`` needs linear_workspace_bytes(B, G, M)."""
+    _require_cuda("h", h, torch.bfloat16, 2)
+    _require_cuda("w_s", w_s, torch.bfloat16, 2)
+    _require_cuda("z", z, torch.bfloat16, 2)
+    B, G = h.shape
+    M = w_s.shape[0]
+    if w_s.shape[1] != G or z.shape != (B, M) or z.stride(1) != 1 or s_scaled.shape != (B, M) \
+            or not s_scaled.is_contiguous():
+        raise ValueError("correction MLP shapes do not match")
+    _lib.call("dels_correction_mid_tc_bf16", _ptr(h), _row_major("h", h), _ptr(w_s), _row_major("w_s", w_s),
+              _ptr(z), _row_major("z", z), B, G, M, _ptr(_f32_vec("alpha", alpha, h.device)), _ptr(s_scaled),
+              _ptr(keys), ws.ptr, ws.nbytes, _stream(h.device))
+    return s_scaled
+
+
 def zero_pad(t: torch.Tensor | None, rows: int | None = None, cols: int | None = None) -> torch.Tensor | None:
     """``t`` zero-padded to ``rows`` (dim 0) x ``cols`` (dim 1).  The runners carry weight
     widths as multiples of 8 because TMA tiles need 16-byte row pitches; the zero entries

@@ -157,11 +157,13 @@ class DraftCorrectionGraphRunner:
         self._ws = ops.Workspace(1 << 12, device)
         self._ws_lin = ops.Workspace(1 << 12, device)
         self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
-        # From DELS_RUNNER_TC_ROWS rows up (default 16) the GRU's W_hh product runs as the
-        # tensor-core split-K GEMM, then the gates (as in kernel/dels.py).
+        # From DELS_RUNNER_TC_ROWS rows up (default 16) the GRU's W_hh product and the
+        # correction MLP's W_s product run as tensor-core split-K GEMMs, then the gates /
+        # the SiLU epilogue (as in kernel/dels.py).
         self._tc = B >= int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
         if self._tc:
-            self._tc_ws = ops.Workspace(ops.linear_workspace_bytes(B, G, 3 * G), device)
+            self._tc_ws = ops.Workspace(max(ops.linear_workspace_bytes(B, G, 3 * G),
+                                            ops.linear_workspace_bytes(B, G, M)), device)
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
             if self.gru_b_hh is not None:
@@ -199,7 +201,12 @@ class DraftCorrectionGraphRunner:
             h = self._gru(self.static_prefix_ids[:, p], h, self._h[cur])
             cur ^= 1
         for t in range(S):
-            ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys, ws=self._ws)
+            if self._tc:
+                ops.correction_mid_tc(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
+                                      ws=self._tc_ws)
+            else:
+                ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
+                                   ws=self._ws)
             ops.fused_argmax_base_bf16(
                 self.static_base_logits[:, t, :], self._s_scaled, self.fc2_weight, self._prior_f32, self._beta,
                 n_pos=1, keys_ready=True, out=self._outs[t], ws=self._ws,

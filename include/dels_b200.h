@@ -267,6 +267,14 @@ DELS_API int dels_correction_mid_bf16(const void* h, int64_t ld_h, const void* w
                                       int64_t ld_z, int B, int G, int M, const float* alpha, void* s_scaled,
                                       int64_t* keys, void* ws, void* stream);
 
+/* The same layer for larger batches, where one warp per output row does not scale: s =
+ * W_s . h[b] by the tensor-core split-K projection GEMM, then the same epilogue
+ * (s_scaled[b] = bf16(alpha[0] * SiLU(z[b] + bf16(s))), keys[0..B) reset).  G % 8 == 0;
+ * ws >= dels_linear_workspace_bytes(B, G, M). */
+DELS_API int dels_correction_mid_tc_bf16(const void* h, int64_t ld_h, const void* w_s, int64_t ld_ws, const void* z,
+                                         int64_t ld_z, int B, int G, int M, const float* alpha, void* s_scaled,
+                                         int64_t* keys, void* ws, size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Allocation-free variant of dels_draft_score_bf16 (no counterpart in the reference).
  * For callers that cannot hand the library device memory — an FFI host without a

@@ -89,6 +89,29 @@ def test_correction_mid_matches_oracle(cuda_device):
     assert (keys.cpu().numpy() == np.iinfo(np.int64).min).all()
 
 
+def test_correction_mid_tc_matches_oracle(cuda_device):
+    """The tensor-core variant (split-K W_s h, then the SiLU epilogue) at 40 rows."""
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(33)
+    B, G, M = 40, 64, 48
+    h = O.bf16_round(rng.standard_normal((B, G)).astype(np.float32))
+    w_s = O.bf16_round((rng.standard_normal((M, G)) * 0.2).astype(np.float32))
+    z = O.bf16_round(rng.standard_normal((B, M)).astype(np.float32))
+    alpha = 0.6
+    dev = cuda_device
+    out = torch.empty(B, M, dtype=torch.bfloat16, device=dev)
+    keys = torch.zeros(B, dtype=torch.int64, device=dev)
+    ws = ops.Workspace(ops.linear_workspace_bytes(B, G, M), dev)
+    ops.correction_mid_tc(_bf16(h, dev), _bf16(w_s, dev), _bf16(z, dev), torch.tensor([alpha], device=dev), out,
+                          keys=keys, ws=ws)
+    s = O.bf16_round((h.astype(np.float64) @ w_s.astype(np.float64).T).astype(np.float32)).astype(np.float64)
+    pre = z.astype(np.float64) + s
+    ref = O.bf16_round((alpha * pre / (1.0 + np.exp(-pre))).astype(np.float32))
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, rtol=2 ** -7, atol=1e-6)
+    assert (keys.cpu().numpy() == np.iinfo(np.int64).min).all()
+
+
 def test_domino_runner_matches_reference_fixture(cuda_device, golden_dir):
     from kernel.domino import DraftCorrectionGraphRunner
 
