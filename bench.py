@@ -261,21 +261,23 @@ class PipelinedE2ESplit:
 
 
 class PipelinedCall:
-    """End-to-end loop around a runner call (``runner(*device_inputs) -> tokens``).
+    """End-to-end loop around a call ``fn(*device_inputs) -> tensor or tuple of tensors``.
 
     Each step copies its host inputs (pinned) to one of two device slots on an H2D stream
-    while the previous call runs, calls the runner on the compute stream once they have
-    landed, and copies the returned tokens back on a D2H stream; ``drain`` makes the compute
-    stream wait for the last read-back.  All copies stay inside the timed region."""
+    while the previous call runs, makes the call on the compute stream once they have
+    landed, and copies what it returns back to pinned host memory on a D2H stream (the
+    returned tensors must not be overwritten by the next call: return clones, or the
+    runners' own fresh outputs); ``drain`` makes the compute stream wait for the last
+    read-back.  All copies stay inside the timed region."""
 
-    def __init__(self, host_inputs, runner, out_shape, dev, stream):
+    def __init__(self, host_inputs, fn, dev, stream):
         self.host = host_inputs
-        self.runner = runner
+        self.fn = fn
         self.stream = stream
         self.h2d = torch.cuda.Stream(dev)
         self.d2h = torch.cuda.Stream(dev)
         self.dev_in = [[torch.empty_like(t, device=dev) for t in host_inputs] for _ in range(2)]
-        self.host_out = [torch.empty(out_shape, dtype=torch.int64).pin_memory() for _ in range(2)]
+        self.host_out = [None, None]
         self.in_ready = [torch.cuda.Event() for _ in range(2)]
         self.done = [torch.cuda.Event() for _ in range(2)]
         for e in self.done:
@@ -291,12 +293,16 @@ class PipelinedCall:
                 d.copy_(h, non_blocking=True)
             self.in_ready[slot].record(self.h2d)
         self.stream.wait_event(self.in_ready[slot])
-        out = self.runner(*self.dev_in[slot])
+        outs = self.fn(*self.dev_in[slot])
+        outs = [outs] if isinstance(outs, torch.Tensor) else list(outs)
         self.done[slot].record(self.stream)
+        if self.host_out[slot] is None:
+            self.host_out[slot] = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
         with torch.cuda.stream(self.d2h):
             self.d2h.wait_event(self.done[slot])
-            self.host_out[slot].copy_(out, non_blocking=True)
-            out.record_stream(self.d2h)
+            for h, o in zip(self.host_out[slot], outs):
+                h.copy_(o, non_blocking=True)
+                o.record_stream(self.d2h)
 
     def drain(self):
         self.stream.wait_stream(self.d2h)
@@ -578,18 +584,13 @@ def run_ragged(args, rank, world, dev):
     ms = timed(step, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
     hh = {k: t[k].cpu().pin_memory() for k in ("draft", "target", "hidden")}
-    dd = {k: torch.empty_like(t[k]) for k in hh}
-    tok_host = torch.empty(n_seq * P, dtype=torch.int64).pin_memory()
-    acc_host = torch.empty(n_seq, dtype=torch.int32).pin_memory()
 
-    def e2e_step():
-        for k in hh:
-            dd[k].copy_(hh[k], non_blocking=True)
-        step(dd["draft"], dd["target"], dd["hidden"])
-        tok_host.copy_(out.tokens, non_blocking=True)
-        acc_host.copy_(acc, non_blocking=True)
+    def e2e_call(draft, target, hidden):
+        step(draft, target, hidden)
+        return out.tokens.clone(), acc.clone()
 
-    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0)
+    pipe = PipelinedCall([hh["draft"], hh["target"], hh["hidden"]], e2e_call, dev, stream)
+    ms_e2e = timed(pipe.step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0, drain=pipe.drain)
     flops = 2.0 * total * wl.V * (wl.H + wl.r)
     _, s_scaled = ops.rank_project_bf16(packed[:total], t["w_rank"], t["alpha"], n_pos=P, row_pos=row_pos[:total],
                                         want_state=False)
@@ -611,7 +612,7 @@ def run_ragged(args, rank, world, dev):
                    "V": wl.V, "l2": "W alone is larger than L2"},
         "e2e": {"value": total * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in hh.values()),
-                "d2h_bytes_per_step": tok_host.numel() * 8 + acc_host.numel() * 4},
+                "d2h_bytes_per_step": n_seq * P * 8 + n_seq * 4},
         "gpu_launches": 5 * args.steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks_sustained(), "unit": "TFLOP/s",
                      "frac": achieved / peaks_sustained(), "traffic": None, "peak_source": f"{pk_src} (sustained)",
@@ -647,15 +648,13 @@ def run_rnn(args, rank, world, dev):
     ms = timed(step, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
     x_host = t["x"].cpu().pin_memory()
-    x_dev = torch.empty_like(t["x"])
-    tok_host = torch.empty(rows, dtype=torch.int64).pin_memory()
 
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        step(x_dev)
-        tok_host.copy_(out.tokens, non_blocking=True)
+    def e2e_call(x):
+        step(x)
+        return out.tokens.clone()
 
-    ms_e2e = timed(e2e_step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0)
+    pipe = PipelinedCall([x_host], e2e_call, dev, stream)
+    ms_e2e = timed(pipe.step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0, drain=pipe.drain)
     ms_main = timed(lambda: ops.fused_argmax_bf16(t["x"], t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=16,
                                                   keys_ready=False, out=out, ws=mws),
                     args.steps, args.warmup, 1, stream, dev, hold_ms=500.0) / args.steps
@@ -719,7 +718,7 @@ def run_runner(args, rank, world, dev):
     clk = clocks.stop()
     base_host = base.cpu().pin_memory()
     prefix_host = prefix.cpu().pin_memory()
-    pipe = PipelinedCall([prefix_host, base_host], runner, (B, steps), dev, stream)
+    pipe = PipelinedCall([prefix_host, base_host], runner, dev, stream)
     ms_e2e = timed(pipe.step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0, drain=pipe.drain)
     _, pk_gbs, pk_src = peaks()
     per_step = (r * V + 3 * G * G + r * G + B * V + B * 3 * G) * 2  # Vr, W_hh, W_rank, base row, table rows
@@ -804,7 +803,7 @@ def run_domino(args, rank, world, dev):
     ms = timed(call, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
     host = [t.cpu().pin_memory() for t in (prefix, hiddens, base)]
-    pipe = PipelinedCall(host, runner, (B, steps), dev, stream)
+    pipe = PipelinedCall(host, runner, dev, stream)
     ms_e2e = timed(pipe.step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0, drain=pipe.drain)
     _, pk_gbs, pk_src = peaks()
     # per step: fc2 [V, M], W_s [M, G], W_hh [3G, G], base row, table rows; per call: W_z, hiddens,
