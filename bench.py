@@ -707,22 +707,49 @@ def run_runner(args, rank, world, dev):
     prior = workloads.zipf_log_prior(V, device=dev).to(torch.bfloat16)
     alpha = workloads.linspace(0.9, 0.3, steps)
     beta = workloads.linspace(0.3, 0.1, steps)
-    runner = DeLSGraphRunner(local_head=head, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha,
-                             beta_values=beta, baseline_logits=prior, device=dev)
-    base = (torch.randn(B, steps, V, generator=g, device=dev)).to(torch.bfloat16)
+    kw = dict(local_head=head, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha, beta_values=beta,
+              baseline_logits=prior, device=dev)
     prefix = torch.randint(0, V, (B, 1), generator=g, device=dev)
     stream = torch.cuda.current_stream(dev)
-    call = lambda: runner(prefix, base)  # noqa: E731
+    per_step = (r * V + 3 * G * G + r * G + B * V + B * 3 * G) * 2  # Vr, W_hh, W_rank, base row, table rows
+    extra = {}
+    if args.runner_hidden:
+        # DeLSFusedGraphRunner: the call takes the draft hidden states [B, steps, H] and the
+        # runner owns the target LM head (Qwen3-8B shape, H = 4096)
+        from kernel.dels import DeLSFusedGraphRunner
+
+        H = 4096
+        W = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        runner = DeLSFusedGraphRunner(target_lm_head_weight=W, **kw)
+        x = torch.randn(B, steps, H, generator=g, device=dev).to(torch.bfloat16)
+        name = f"runner_hidden_b{B}_steps{steps}"
+        if runner._fused:  # W streamed by every step's scorer
+            bytes_call = steps * (per_step - B * V * 2 + V * H * 2 + B * H * 2)
+        else:  # one GEMM over all rows writes the logits, the steps read them back
+            bytes_call = V * H * 2 + B * steps * H * 2 + B * steps * V * 2 + steps * per_step
+        # the reference's flow for comparison: lm_head by torch (cuBLAS), slice copy into
+        # the base-logit runner (code/dflash.py:468, :482-485)
+        plain = DeLSGraphRunner(**kw)
+        unfused = lambda: plain(prefix, torch.nn.functional.linear(x, W))  # noqa: E731
+        ms_unfused = timed(unfused, args.steps, args.warmup, 1, stream, dev, hold_ms=300.0)
+        extra = {"schedule": "fused per-step scorer" if runner._fused else "one long-logit GEMM per call",
+                 "ms_per_call_torch_lm_head_then_base_runner": ms_unfused / args.steps}
+        del plain
+        inputs = [prefix, x]
+    else:
+        runner = DeLSGraphRunner(**kw)
+        base = (torch.randn(B, steps, V, generator=g, device=dev)).to(torch.bfloat16)
+        name = f"runner_b{B}_steps{steps}"
+        bytes_call = steps * per_step + B * steps * V * 2 * 2  # + copy-in of the base logits (read + write)
+        inputs = [prefix, base]
+    call = lambda: runner(*inputs)  # noqa: E731
     clocks = ClockSampler(dev)
     ms = timed(call, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
     clk = clocks.stop()
-    base_host = base.cpu().pin_memory()
-    prefix_host = prefix.cpu().pin_memory()
-    pipe = PipelinedCall([prefix_host, base_host], runner, dev, stream)
+    host = [t.cpu().pin_memory() for t in inputs]
+    pipe = PipelinedCall(host, runner, dev, stream)
     ms_e2e = timed(pipe.step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0, drain=pipe.drain)
     _, pk_gbs, pk_src = peaks()
-    per_step = (r * V + 3 * G * G + r * G + B * V + B * 3 * G) * 2  # Vr, W_hh, W_rank, base row, table rows
-    bytes_call = steps * per_step + B * steps * V * 2 * 2  # + copy-in of the base logits (read + write)
     achieved = bytes_call / (ms / args.steps * 1e-3) / 1e9
     rows = B * steps
     res = {
@@ -730,11 +757,12 @@ def run_runner(args, rank, world, dev):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, random-init local head at the released shapes)",
-        "config": {"workload": f"runner_b{B}_steps{steps}", "V": V, "E": E, "G": G, "r": r,
-                   "note": "one step = one DeLSGraphRunner call (14 scored positions per sequence)"},
+        "config": {"workload": name, "V": V, "E": E, "G": G, "r": r,
+                   "note": "one step = one runner call (14 scored positions per sequence)", **extra},
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
-                "h2d_bytes_per_step": base_host.numel() * 2 + B * 8, "d2h_bytes_per_step": B * steps * 8},
-        "gpu_launches": (1 + 3 * steps - 1) * args.steps,
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
+                "d2h_bytes_per_step": B * steps * 8},
+        "gpu_launches": (1 + 3 * steps - 1 + (1 if args.runner_hidden and not runner._fused else 0)) * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
                      "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call,
                      "note": "Vr (77.8 MB) can stay L2-resident across the 14 steps, so this bound can be beaten"},
@@ -745,7 +773,8 @@ def run_runner(args, rank, world, dev):
 
         torch.set_num_threads(os.cpu_count() or 1)
         table = torch.nn.functional.linear(head.embed_tokens.weight, head.prefix_gru.weight_ih_l0).cpu()
-        cpu_args = (prefix[:1].cpu(), base[:1].cpu(), table, head.prefix_gru.weight_hh_l0.detach().cpu(),
+        base1 = (torch.nn.functional.linear(x[:1], W) if args.runner_hidden else base[:1]).cpu()
+        cpu_args = (prefix[:1].cpu(), base1, table, head.prefix_gru.weight_hh_l0.detach().cpu(),
                     head.rank_proj.weight.detach().cpu(), head.low_rank_lm_head.weight.detach().cpu(), prior.cpu(),
                     alpha, beta)
         runner_rollout(*cpu_args)
@@ -887,6 +916,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="auto", choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "runner", "domino"])
     ap.add_argument("--runner-batch", type=int, default=1, help="batch of the runner workload")
+    ap.add_argument("--runner-hidden", action="store_true",
+                    help="runner workload: DeLSFusedGraphRunner fed the draft hidden states")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -225,6 +225,7 @@ int init_device(int dev) {
     if (rc == DELS_OK && (e = f32_score_setup(kMaxSmem)) != cudaSuccess) rc = cuda_fail(e, "kernel setup: f32_score");
     SET((tc_scorer_pair_kernel<false>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<true>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<false, true>), PairConfig::kSmemBytes);
     SET((tc_skinny_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_staged_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_kernel<32>), SkinnyConfig<32>::kSmemBytes);
@@ -406,7 +407,7 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
 
 // The paired (cta_group::2) scorer: 256-row pair tiles, each CTA stages 128 rows of A
 // and half of the 256-token B tile (128 rows; 32 rows for the split tail units).
-template <bool VB>
+template <bool VB, bool STORE = false>
 int launch_scorer_pair(const TcOperands& op, TcArgs args, int max_pairs, cudaStream_t st) {
   int rc = ensure_encode();
   if (rc != DELS_OK) return rc;
@@ -438,7 +439,7 @@ int launch_scorer_pair(const TcOperands& op, TcArgs args, int max_pairs, cudaStr
   const long long want = tiles < max_pairs ? tiles * (args.tail_split > 1 ? args.tail_split : 1) : tiles;
   const int pairs = (int)(want < max_pairs ? want : max_pairs);
   if (pairs <= 0) return DELS_OK;
-  DELS_CHECK_PDL("tc_scorer_pair_kernel launch", launch_pdl(tc_scorer_pair_kernel<VB>, dim3(2 * pairs),
+  DELS_CHECK_PDL("tc_scorer_pair_kernel launch", launch_pdl(tc_scorer_pair_kernel<VB, STORE>, dim3(2 * pairs),
       dim3(kTcThreads), PairConfig::kSmemBytes, st, ma0, mb0, ma1, mb1, mb0t, mb1t, args));
   return DELS_OK;
 }
@@ -480,7 +481,9 @@ size_t projection_partials_bytes(int rows, int K, int n) {
 
 // partial[split][row][n] = x[row, k-slice] . w[n, k-slice]
 int launch_projection(const void* x, long long ld_x, const void* w, long long ld_w, int rows, int K, int n,
-                      float* partials, int* status, int sm_count, cudaStream_t st, SplitPlan* plan_out) {
+                      float* partials, int* status, int sm_count, cudaStream_t st, SplitPlan* plan_out,
+                      __nv_bfloat16* out_bf16 = nullptr, long long ld_bf16 = 0,
+                      const __nv_bfloat16* bias_bf16 = nullptr, bool out_vec = false) {
   const SplitPlan p = plan_projection(rows, K, n);
   TcOperands op;
   op.a0 = x;
@@ -499,6 +502,20 @@ int launch_projection(const void* x, long long ld_x, const void* w, long long ld
   a.out = partials;
   a.ld_out = p.ld_out;
   a.split_stride = (long long)rows * p.ld_out;
+  if (out_bf16 != nullptr) {
+    if (p.splits != 1) return fail(DELS_ERR_UNSUPPORTED, "bf16 GEMM output needs a single K split");
+    // a wide B operand (an LM head): row tiles sweep it in groups so that it streams from
+    // HBM once per group, and the last partial wave is split along N like the scorer's
+    a.group_m = kScorerGroupM;
+    // 32-column units for the last partial wave (the epilogue's chunk width): with few
+    // rows the GEMM streams B at HBM speed, so the wave's time follows its widest unit
+    a.tail_split = p.bn / 32;
+    a.out = nullptr;
+    a.out_bf16 = out_bf16;
+    a.ld_out = ld_bf16;
+    a.bias_bf16 = bias_bf16;
+    a.out_vec = out_vec ? 1 : 0;
+  }
   if (plan_out) *plan_out = p;
   switch (p.bn) {
     case 32: return launch_tc<32, kStore, false>(op, a, sm_count, st);
@@ -1043,6 +1060,8 @@ int dels_correction_mid_bf16(const void* h, int64_t ld_h, const void* w_s, int64
 
 size_t dels_linear_workspace_bytes(int rows, int K, int N) {
   if (rows <= 0 || K <= 0 || N <= 0) return DELS_WS_HEADER_BYTES;
+  // one K split: the GEMM writes the bf16 result itself, no partial sums
+  if (plan_projection(rows, K, N).splits == 1) return DELS_WS_HEADER_BYTES;
   return DELS_WS_HEADER_BYTES + projection_partials_bytes(rows, K, N);
 }
 
@@ -1059,6 +1078,38 @@ int dels_linear_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, c
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (rows == 0) return DELS_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (plan_projection(rows, K, N).splits == 1) {
+    // enough output tiles to fill the device without splitting K (vocabulary-sized N):
+    // one launch, bf16 written by the GEMM's epilogue
+    const bool vec = aligned16(out) && (ld_out % 8) == 0 && (bias == nullptr || aligned16(bias));
+    if (rows > kBM && ds->max_pairs > 0 && g_use_pairs) {
+      // more than one 128-row tile: CTA pairs (256-row tiles, each SM stages half of
+      // every B tile), as the scorer does for the same shapes
+      TcOperands op;
+      op.a0 = x;
+      op.lda0 = ld_x;
+      op.b0 = w;
+      op.ldb0 = ld_w;
+      op.K0 = K;
+      op.m_extent = rows;
+      op.n_extent = N;
+      TcArgs a = blank_args();
+      a.m_rows = rows;
+      a.n_cols = N;
+      a.kb_per_split = cdiv(K, kBK);
+      a.group_m = kScorerGroupM / 2;
+      a.tail_split = kScorerTailSplit;
+      a.status = hdr.status;
+      a.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out);
+      a.ld_out = ld_out;
+      a.bias_bf16 = reinterpret_cast<const __nv_bfloat16*>(bias);
+      a.out_vec = vec ? 1 : 0;
+      return launch_scorer_pair<false, true>(op, a, ds->max_pairs, st);
+    }
+    return launch_projection(x, ld_x, w, ld_w, rows, K, N, nullptr, hdr.status, ds->sm_count, st, nullptr,
+                             reinterpret_cast<__nv_bfloat16*>(out), ld_out,
+                             reinterpret_cast<const __nv_bfloat16*>(bias), vec);
+  }
   float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + DELS_WS_HEADER_BYTES);
   SplitPlan plan;
   if ((rc = launch_projection(x, ld_x, w, ld_w, rows, K, N, partials, hdr.status, ds->sm_count, st, &plan)) !=
@@ -1072,6 +1123,12 @@ int dels_linear_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, c
   return DELS_OK;
 }
 
+size_t dels_correction_mid_tc_workspace_bytes(int B, int G, int M) {
+  // always split-K partials: the SiLU epilogue runs in the finalisation kernel
+  if (B <= 0 || G <= 0 || M <= 0) return DELS_WS_HEADER_BYTES;
+  return DELS_WS_HEADER_BYTES + projection_partials_bytes(B, G, M);
+}
+
 int dels_correction_mid_tc_bf16(const void* h, int64_t ld_h, const void* w_s, int64_t ld_ws, const void* z,
                                 int64_t ld_z, int B, int G, int M, const float* alpha, void* s_scaled, int64_t* keys,
                                 void* ws, size_t ws_bytes, void* stream) {
@@ -1082,7 +1139,7 @@ int dels_correction_mid_tc_bf16(const void* h, int64_t ld_h, const void* w_s, in
   if ((rc = check_bf16_matrix("h", h, ld_h, G)) != DELS_OK) return rc;
   if ((rc = check_bf16_matrix("w_s", w_s, ld_ws, G)) != DELS_OK) return rc;
   WsHeader hdr;
-  if ((rc = ws_header(ws, ws_bytes, dels_linear_workspace_bytes(B, G, M), &hdr)) != DELS_OK) return rc;
+  if ((rc = ws_header(ws, ws_bytes, dels_correction_mid_tc_workspace_bytes(B, G, M), &hdr)) != DELS_OK) return rc;
   DeviceState* ds = nullptr;
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;

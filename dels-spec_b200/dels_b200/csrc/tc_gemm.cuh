@@ -26,7 +26,10 @@
 //             maximum in registers, then one 64-bit atomicMax per (row, tile).  The last CTA to finish decodes the
 //             keys into int64 token ids (optional).
 //   kStore  : write the fp32 accumulator tile to out[split][row][n] (split-K partial
-//             sums; used by the rank projection and the RNN input projection).
+//             sums; used by the rank projection and the RNN input projection), or, with
+//             out_bf16 set (one K split), bf16(acc + bias[n]) straight to out_bf16[row][n]
+//             (F.linear with a bf16 result, e.g. the long logits h . W^T of
+//             code/dflash.py:468).
 #pragma once
 
 #include "common.cuh"
@@ -65,6 +68,9 @@ struct TcArgs {
   float* out;
   long long ld_out;
   long long split_stride;
+  __nv_bfloat16* out_bf16;         // non-null: bf16 result (k_splits == 1), row stride ld_out
+  const __nv_bfloat16* bias_bf16;  // [n_cols] or null (out_bf16 only)
+  int out_vec;                     // out_bf16 and ld_out allow 16-byte stores
 };
 
 // STAGED: the argmax epilogue with base logits prefetches each tile's base rows and
@@ -93,6 +99,49 @@ struct TcConfig {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
+
+// One 32-column chunk of an accumulator row as bf16(0 + acc + bias): the same value (and
+// sign of zero) as the split-K finalisation of a single split.  dst and bias point at the
+// chunk's first column; `valid` columns are written; vec: 16-byte aligned dst and bias.
+__device__ __forceinline__ void store_chunk_bf16(const uint32_t (&v)[32], int valid, __nv_bfloat16* dst,
+                                                 const __nv_bfloat16* bias, int vec) {
+  float x[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = 0.0f + __uint_as_float(v[j]);
+  if (vec && valid >= 32) {
+    if (bias != nullptr) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(bias) + q);
+        x[8 * q + 0] += bf16_lo(w.x);
+        x[8 * q + 1] += bf16_hi(w.x);
+        x[8 * q + 2] += bf16_lo(w.y);
+        x[8 * q + 3] += bf16_hi(w.y);
+        x[8 * q + 4] += bf16_lo(w.z);
+        x[8 * q + 5] += bf16_hi(w.z);
+        x[8 * q + 6] += bf16_lo(w.w);
+        x[8 * q + 7] += bf16_hi(w.w);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 o;
+      o.x = pack_bf16x2(x[8 * q + 0], x[8 * q + 1]);
+      o.y = pack_bf16x2(x[8 * q + 2], x[8 * q + 3]);
+      o.z = pack_bf16x2(x[8 * q + 4], x[8 * q + 5]);
+      o.w = pack_bf16x2(x[8 * q + 6], x[8 * q + 7]);
+      reinterpret_cast<uint4*>(dst)[q] = o;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) {
+        float y = x[j];
+        if (bias != nullptr) y += __bfloat162float(bias[j]);
+        dst[j] = __float2bfloat16_rn(y);
+      }
+  }
+}
 
 struct TileCoord {
   int m_tile, n_tile, split;
@@ -502,6 +551,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           atomicMax(&args.keys[row], best_key);
           __threadfence();
         }
+      } else if (args.out_bf16 != nullptr) {
+        __nv_bfloat16* dst = args.out_bf16 + (long long)row * args.ld_out + n0;
+        const __nv_bfloat16* bias = args.bias_bf16 != nullptr ? args.bias_bf16 + n0 : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t v[32];
+          tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
+          tmem_ld_wait(v);
+          const int c0 = c * 32;
+          if (row_ok && c0 < ncols)
+            store_chunk_bf16(v, ncols - c0, dst + c0, bias != nullptr ? bias + c0 : nullptr, args.out_vec);
+        }
+        tc_fence_before();
+        mbar_arrive(tempty_bar(acc));
       } else {
         float* dst = args.out + (long long)tc.split * args.split_stride + (long long)row * args.ld_out + n0;
 #pragma unroll 1

@@ -44,7 +44,9 @@ struct PairConfig {
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-template <bool VEC_BASE>
+// STORE: instead of the argmax, write each accumulator row as bf16 to args.out_bf16
+// (store_chunk_bf16; the long logits h . W^T when a caller wants them materialised).
+template <bool VEC_BASE, bool STORE = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     tc_scorer_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                           const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
@@ -246,6 +248,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      // A warp whose 32 rows are all past the end skips the tile (warp-uniform, so the
+      // collective tensor-memory loads stay aligned); lanes past the end skip the
+      // arithmetic.
+      const bool warp_rows = (wu.c.m_tile * 2 * kBM + (int)rank * kBM + quad * 32) < m_rows;
+
+      if constexpr (STORE) {
+        __nv_bfloat16* dst = args.out_bf16 + (long long)row * args.ld_out + n0;
+        const __nv_bfloat16* bias = args.bias_bf16 != nullptr ? args.bias_bf16 + n0 : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < (warp_rows ? nchunks : 0); ++c) {
+          uint32_t v[32];
+          tmem_ld_32cols(t_row + (uint32_t)(c * 32), v);
+          tmem_ld_wait(v);
+          const int c0 = c * 32;
+          if (row_ok && c0 < ncols)
+            store_chunk_bf16(v, ncols - c0, dst + c0, bias != nullptr ? bias + c0 : nullptr, args.out_vec);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader)
+            mbar_arrive(tempty_bar(acc));
+          else
+            mbar_arrive_remote(acc == 0 ? tempty_leader0 : tempty_leader1);
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+        continue;
+      }
 
       float negb = 0.0f;
       if (row_ok && args.prior != nullptr) negb = -__ldg(&args.beta[row_position(args.row_pos, row, args.n_pos)]);
@@ -255,10 +288,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       long long best_key = kKeyEmpty;
       // the row's best score so far on the device: chunk_fold skips chunks below it
       float thr = row_ok ? key_threshold(__ldcg(&args.keys[row])) : -__int_as_float(0x7f800000);
-      // A warp whose 32 rows are all past the end skips the tile (warp-uniform, so the
-      // collective tensor-memory loads stay aligned); lanes past the end skip the
-      // arithmetic.
-      const bool warp_rows = (wu.c.m_tile * 2 * kBM + (int)rank * kBM + quad * 32) < m_rows;
 #pragma unroll 1
       for (int c = 0; c < (warp_rows ? nchunks : 0); ++c) {
         uint32_t v[32];
@@ -343,7 +372,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
   }
 
-  if (args.idx_out != nullptr) {
+  if (!STORE && args.idx_out != nullptr) {
     if (threadIdx.x == 0) {
       __threadfence();
       const unsigned prev = atomicAdd(args.counter, 1u);

@@ -607,6 +607,10 @@ def linear_workspace_bytes(rows: int, K: int, N: int) -> int:
     return int(_lib.query("dels_linear_workspace_bytes", rows, K, N))
 
 
+def correction_mid_tc_workspace_bytes(B: int, G: int, M: int) -> int:
+    return int(_lib.query("dels_correction_mid_tc_workspace_bytes", B, G, M))
+
+
 def rank_workspace_bytes(rows: int, K: int, r: int) -> int:
     return int(_lib.query("dels_rank_workspace_bytes", rows, K, r))
 
@@ -677,7 +681,7 @@ def correction_mid_tc(
     ws: Workspace,
 ) -> torch.Tensor:
     """correction_mid with W_s h on the tensor-core split-K GEMM (larger batches);
-    ``ws`` needs linear_workspace_bytes(B, G, M)."""
+    ``ws`` needs correction_mid_tc_workspace_bytes(B, G, M)."""
     _require_cuda("h", h, torch.bfloat16, 2)
     _require_cuda("w_s", w_s, torch.bfloat16, 2)
     _require_cuda("z", z, torch.bfloat16, 2)

@@ -196,7 +196,7 @@ class DeLSGraphRunner:
                 nxt ^= 1
         self.static_out.copy_(self._tokens.t())
 
-    # -- the per-step inputs and scorer; DeLSFusedGraphRunner swaps these two ----------
+    # -- the per-step inputs and scorer; DeLSFusedGraphRunner overrides these ----------
     def _alloc_step_inputs(self, dtype, device):
         self.static_base_logits = torch.zeros(self.batch_size, self.steps, self.vocab_size, dtype=dtype,
                                               device=device)
@@ -224,16 +224,24 @@ class DeLSFusedGraphRunner(DeLSGraphRunner):
     """DeLS rollout that takes the DFlash draft hidden states instead of the long logits.
 
     The reference materialises ``base_logits = target.lm_head(parallel_hiddens)``
-    ([B, 15, V], code/dflash.py:468) and copies positions 1..steps into the runner
-    (:482-485).  Here every step scores
-        h_t . W_lm + alpha_t * act(W_rank g_t) . Vr - beta_t * prior
-    inside the tensor-core scorer (``dels_fused_argmax_bf16``), so the long logits are
-    never written.  Each step streams the LM head once, so this pays off when B x (one
-    step's rows) is large enough for the scorer to be tensor-bound (a few hundred rows);
-    at batch 1 the materialising runner above is cheaper.
+    ([B, 15, V], code/dflash.py:468), slices positions 1..steps into a contiguous copy and
+    copies that into the runner (:482-485).  Here the runner owns the LM head and takes
+    ``__call__(prefix_ids [B, 1], parallel_hiddens [B, steps, H])`` (the hidden states of
+    the positions the reference feeds as base logits).  Two schedules, picked by batch:
 
-    ``__call__(prefix_ids [B, 1], parallel_hiddens [B, steps, H])`` with the hidden
-    states of the same positions the reference feeds as base logits."""
+    * ``B >= DELS_FUSED_RUNNER_ROWS`` (default 192): every step scores
+          h_t . W_lm + alpha_t * act(W_rank g_t) . Vr - beta_t * prior
+      inside the tensor-core scorer (``dels_fused_argmax_bf16``), so the long logits are
+      never written.  A step streams the LM head once; with a few hundred rows per step the
+      scorer is tensor-bound, the FLOPs equal those of one big GEMM over all positions,
+      and the [B, steps, V] round trip disappears.
+    * smaller batches: the rollout's steps depend on each other, so a per-step scorer
+      would stream the whole LM head ``steps`` times for a handful of rows.  Instead the
+      graph starts with one GEMM over all B x steps hidden rows (``dels_linear_bf16``,
+      which writes bf16 logits straight from its epilogue into the runner's own buffer:
+      one pass over W, no slice copy, no copy-in), then runs the base-logit rollout.
+      Base logits are bf16-rounded here, as in the reference.
+    """
 
     def __init__(self, *, target_lm_head_weight: torch.Tensor, **kwargs):
         w = target_lm_head_weight.detach()
@@ -243,13 +251,27 @@ class DeLSFusedGraphRunner(DeLSGraphRunner):
             )
         self._lm_weight = w.to(device=kwargs["device"], dtype=torch.bfloat16).contiguous()
         self.hidden_size = int(w.shape[1])
+        self._fused = int(kwargs["batch_size"]) >= int(os.environ.get("DELS_FUSED_RUNNER_ROWS", "192"))
         super().__init__(**kwargs)
 
     def _alloc_step_inputs(self, dtype, device):
-        self.static_parallel_hiddens = torch.zeros(self.batch_size, self.steps, self.hidden_size, dtype=dtype,
-                                                   device=device)
+        B, S = self.batch_size, self.steps
+        self.static_parallel_hiddens = torch.zeros(B, S, self.hidden_size, dtype=dtype, device=device)
+        if not self._fused:
+            self.static_base_logits = torch.zeros(B, S, self.vocab_size, dtype=dtype, device=device)
+            self._lm_ws = ops.Workspace(ops.linear_workspace_bytes(B * S, self.hidden_size, self.vocab_size),
+                                        device)
+
+    def _forward_impl(self):
+        if not self._fused:
+            B, S = self.batch_size, self.steps
+            ops.linear_bf16(self.static_parallel_hiddens.view(B * S, self.hidden_size), self._lm_weight,
+                            out=self.static_base_logits.view(B * S, self.vocab_size), ws=self._lm_ws)
+        super()._forward_impl()
 
     def _score(self, step: int):
+        if not self._fused:
+            return super()._score(step)
         ops.fused_argmax_bf16(
             self.static_parallel_hiddens[:, step, :], self._lm_weight, self._s_scaled, self.lm_head_weight,
             self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],

@@ -163,7 +163,7 @@ class DraftCorrectionGraphRunner:
         self._tc = B >= int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
         if self._tc:
             self._tc_ws = ops.Workspace(max(ops.linear_workspace_bytes(B, G, 3 * G),
-                                            ops.linear_workspace_bytes(B, G, M)), device)
+                                            ops.correction_mid_tc_workspace_bytes(B, G, M)), device)
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
             if self.gru_b_hh is not None:

@@ -249,11 +249,14 @@ DELS_API int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_str
  * --------------------------------------------------------------------------------- */
 
 /* F.linear with an optional bias (code/kernel/domino.py:404-408 z = F.linear(hiddens,
- * W_z, b1); :325-327 and code/kernel/dels.py:265-268, the GRU input table):
+ * W_z, b1); :325-327 and code/kernel/dels.py:265-268, the GRU input table;
+ * code/dflash.py:468, the long logits lm_head(parallel_hiddens)):
  *   out[row] = bf16(x[row] . w^T + bias)     x [rows, K], w [N, K], bias [N] bf16 or NULL,
  * one rounding of the fp32 accumulator (bias included), like the bf16 GEMM's bias
  * epilogue.  tcgen05 split-K GEMM with deterministic fp32 partials in ws, then the
- * finalisation.  ws >= dels_linear_workspace_bytes(rows, K, N). */
+ * finalisation; when the output tiles alone fill the device (vocabulary-sized N) K is not
+ * split and the GEMM writes the bf16 result itself (same values, one launch, ws = the
+ * header only).  ws >= dels_linear_workspace_bytes(rows, K, N). */
 DELS_API size_t dels_linear_workspace_bytes(int rows, int K, int N);
 DELS_API int dels_linear_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias, int rows,
                               int K, int N, void* out, int64_t ld_out, void* ws, size_t ws_bytes, void* stream);
@@ -270,7 +273,8 @@ DELS_API int dels_correction_mid_bf16(const void* h, int64_t ld_h, const void* w
 /* The same layer for larger batches, where one warp per output row does not scale: s =
  * W_s . h[b] by the tensor-core split-K projection GEMM, then the same epilogue
  * (s_scaled[b] = bf16(alpha[0] * SiLU(z[b] + bf16(s))), keys[0..B) reset).  G % 8 == 0;
- * ws >= dels_linear_workspace_bytes(B, G, M). */
+ * ws >= dels_correction_mid_tc_workspace_bytes(B, G, M). */
+DELS_API size_t dels_correction_mid_tc_workspace_bytes(int B, int G, int M);
 DELS_API int dels_correction_mid_tc_bf16(const void* h, int64_t ld_h, const void* w_s, int64_t ld_ws, const void* z,
                                          int64_t ld_z, int B, int G, int M, const float* alpha, void* s_scaled,
                                          int64_t* keys, void* ws, size_t ws_bytes, void* stream);

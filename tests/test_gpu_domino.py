@@ -67,6 +67,34 @@ def test_linear_bf16_matches_oracle(cuda_device):
         np.testing.assert_allclose(out, ref, rtol=2 ** -7, atol=1e-3)
 
 
+def test_linear_bf16_single_split_epilogue(cuda_device):
+    """Vocabulary-sized N: the output tiles fill the device, K is not split and the GEMM's
+    epilogue writes bf16 itself (no partials, workspace = header).  16-byte stores (packed
+    rows) and element stores (a row stride that is not a multiple of 8) must give the
+    same bits, within one bf16 rounding of the exact sum."""
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(33)
+    # 14 rows: one 128-row tile (single-CTA kernel); 130 and 300 rows: CTA-pair tiles
+    for rows, K, N, bias in ((14, 512, 40000, True), (130, 256, 38000, False), (300, 256, 38000, True)):
+        assert ops.linear_workspace_bytes(rows, K, N) == ops.linear_workspace_bytes(0, K, N)
+        x = O.bf16_round(rng.standard_normal((rows, K)).astype(np.float32))
+        w = O.bf16_round((rng.standard_normal((N, K)) * 0.05).astype(np.float32))
+        b = O.bf16_round(rng.standard_normal(N).astype(np.float32)) if bias else None
+        xt, wt = _bf16(x, cuda_device), _bf16(w, cuda_device)
+        bt = _bf16(b, cuda_device) if bias else None
+        packed = ops.linear_bf16(xt, wt, bt)
+        wide = torch.full((rows, N + 3), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+        strided = ops.linear_bf16(xt, wt, bt, out=wide[:, :N])
+        assert torch.equal(packed.view(torch.int16), strided.view(torch.int16))
+        assert torch.isnan(wide[:, N:].float()).all()  # nothing written past N
+        out = packed.float().cpu().numpy()
+        acc = x.astype(np.float64) @ w.astype(np.float64).T + (0.0 if b is None else b.astype(np.float64))
+        ref = O.bf16_round(acc.astype(np.float32))
+        assert np.mean(out == ref) > 0.99
+        np.testing.assert_allclose(out, ref, rtol=2 ** -7, atol=1e-3)
+
+
 def test_correction_mid_matches_oracle(cuda_device):
     from dels_b200 import ops
 
@@ -102,7 +130,7 @@ def test_correction_mid_tc_matches_oracle(cuda_device):
     dev = cuda_device
     out = torch.empty(B, M, dtype=torch.bfloat16, device=dev)
     keys = torch.zeros(B, dtype=torch.int64, device=dev)
-    ws = ops.Workspace(ops.linear_workspace_bytes(B, G, M), dev)
+    ws = ops.Workspace(ops.correction_mid_tc_workspace_bytes(B, G, M), dev)
     ops.correction_mid_tc(_bf16(h, dev), _bf16(w_s, dev), _bf16(z, dev), torch.tensor([alpha], device=dev), out,
                           keys=keys, ws=ws)
     s = O.bf16_round((h.astype(np.float64) @ w_s.astype(np.float64).T).astype(np.float32)).astype(np.float64)

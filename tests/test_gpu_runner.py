@@ -181,10 +181,14 @@ def test_runner_batches(cuda_device, B):
     assert _compare(out, gaps, toks, 1e-2) >= B * steps // 2
 
 
-def test_fused_long_logit_runner_matches_oracle(cuda_device):
-    """DeLSFusedGraphRunner: long logits computed inside the scorer from the hidden states."""
+@pytest.mark.parametrize("schedule", ["fused", "materialised"])
+def test_fused_long_logit_runner_matches_oracle(cuda_device, monkeypatch, schedule):
+    """DeLSFusedGraphRunner from the hidden states: long logits computed inside each step's
+    scorer (never rounded to bf16), or by one GEMM per call into the runner's own bf16
+    buffer (the schedule for small batches)."""
     from kernel.dels import DeLSFusedGraphRunner
 
+    monkeypatch.setenv("DELS_FUSED_RUNNER_ROWS", "1" if schedule == "fused" else "1000000")
     rng = np.random.default_rng(31)
     V, E, G, r, H, B, steps = 3001, 32, 64, 32, 256, 3, 6
     w = {
@@ -206,7 +210,10 @@ def test_fused_long_logit_runner_matches_oracle(cuda_device):
     prefix = np.array([[5], [77], [2999]])
     out = runner(torch.from_numpy(prefix).to(cuda_device),
                  torch.from_numpy(hid).to(cuda_device).to(torch.bfloat16)).cpu().numpy()
-    base = np.einsum("bsh,vh->bsv", hid.astype(np.float64), W.astype(np.float64))  # exact, never rounded
+    assert runner._fused == (schedule == "fused")
+    base = np.einsum("bsh,vh->bsv", hid.astype(np.float64), W.astype(np.float64))  # exact
+    if schedule == "materialised":
+        base = O.bf16_round(base.astype(np.float32))  # the bf16 long logits, as the reference feeds them
     toks, gaps = O.dels_runner_rollout(prefix, base, embed=w["embed"], w_ih=w["w_ih"], w_hh=w["w_hh"],
                                        w_rank=w["w_rank"], Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta,
                                        activation="silu", bf16=True)
