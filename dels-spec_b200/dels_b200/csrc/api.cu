@@ -227,6 +227,7 @@ int init_device(int dev) {
     SET((tc_scorer_pair_kernel<true>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<false, true>), PairConfig::kSmemBytes);
     SET((tc_skinny_kernel<16>), SkinnyConfig<16>::kSmemBytes);
+    SET((tc_skinny_gh_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_staged_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_kernel<32>), SkinnyConfig<32>::kSmemBytes);
     SET((tc_skinny_staged_kernel<32>), SkinnyConfig<32>::kSmemBytes);
@@ -362,7 +363,7 @@ int launch_tc(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) 
 
 // The skinny scorer: weight maps (W, Vr) in 64 x 128 boxes as the MMA's A operand, row
 // maps (h, s) in 64 x NB boxes as its B operand; one persistent CTA per SM.
-template <int NB, bool SB>
+template <int NB, bool SB, bool GH = false>
 int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t st) {
   int rc = ensure_encode();
   if (rc != DELS_OK) return rc;
@@ -395,7 +396,10 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
   const int tiles = cdiv(op.n_extent, kSkinnyBM);
   const int grid = tiles < sm_count ? tiles : sm_count;
   if (grid <= 0) return DELS_OK;
-  if (SB) {
+  if constexpr (GH) {
+    DELS_CHECK_PDL("tc_skinny_gh_kernel launch", launch_pdl(tc_skinny_gh_kernel<NB>, dim3(grid),
+        dim3(kSkinnyGhThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
+  } else if constexpr (SB) {
     DELS_CHECK_PDL("tc_skinny_staged_kernel launch", launch_pdl(tc_skinny_staged_kernel<NB>, dim3(grid),
         dim3(kTcThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, mbase, mprior, args));
   } else {
@@ -544,7 +548,7 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
                         const float* prior, const float* beta, int n_pos, const int32_t* row_pos, int rows,
                         const int32_t* rows_dev, int H, int r, int V, long long v_begin, uint32_t flags,
                         int64_t* keys, int64_t* idx_out, float* score_out, void* ws, size_t ws_bytes,
-                        cudaStream_t st) {
+                        cudaStream_t st, const TcArgs* gh = nullptr) {
   const int have_keys = keys != nullptr;
   int rc = check_common_score_args(rows, V, v_begin, beta, prior, n_pos, &have_keys);
   if (rc != DELS_OK) return rc;
@@ -607,6 +611,20 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
   a.score_out = score_out;
   a.counter = hdr.counter;
   const bool vec_base = base != nullptr && aligned16(base) && (ld_base % 8) == 0;
+  if (gh != nullptr) {
+    // the next step's W_hh h on the plain skinny scorer's helper warps
+    if (!(rows <= kSkinnyStageRows && g_use_skinny))
+      return fail(DELS_ERR_UNSUPPORTED, "the fused gh projection needs at most %d rows and the skinny scorer",
+                  kSkinnyStageRows);
+    a.gh_w = gh->gh_w;
+    a.gh_bias = gh->gh_bias;
+    a.gh_x = gh->gh_x;
+    a.gh_out = gh->gh_out;
+    a.gh_rows = gh->gh_rows;
+    a.gh_k = gh->gh_k;
+    a.gh_b = rows;
+    return launch_skinny<16, false, true>(op, a, ds->sm_count, st);
+  }
   if (rows <= kSkinnyMaxRows && g_use_skinny) {
     // Decode-shaped call: the vocab tile is the MMA's M side, the rows its N side.  Above
     // kSkinnyStageRows rows the producer stages the epilogue operands (base logits when
@@ -715,6 +733,32 @@ int dels_fused_argmax_base_bf16(const void* base, int64_t ld_base, const void* s
   return fused_argmax_common(nullptr, 0, nullptr, 0, base, ld_base, s_scaled, ld_s, Vr, ld_vr, prior, beta, n_pos,
                              row_pos, rows, rows_dev, 0, r, V, v_begin, flags, keys, idx_out, score_out, ws,
                              ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dels_fused_argmax_base_gru_bf16(const void* base, int64_t ld_base, const void* s_scaled, int64_t ld_s,
+                                    const void* Vr, int64_t ld_vr, const float* prior, const float* beta, int n_pos,
+                                    int rows, int r, int V, uint32_t flags, int64_t* keys, int64_t* idx_out,
+                                    void* ws, size_t ws_bytes, const void* w_hh, const void* b_hh, const void* h,
+                                    int G, void* gh_out, void* stream) {
+  if (base == nullptr) return fail(DELS_ERR_INVALID_ARG, "base is NULL");
+  if (ld_base < V) return fail(DELS_ERR_INVALID_ARG, "ld_base %lld < V %d", (long long)ld_base, V);
+  if (r <= 0) return fail(DELS_ERR_INVALID_ARG, "r must be > 0");
+  if (w_hh == nullptr || h == nullptr || gh_out == nullptr) return fail(DELS_ERR_INVALID_ARG, "NULL GRU operand");
+  if (G <= 0 || (G % 8) != 0 || !aligned16(w_hh) || !aligned16(h))
+    return fail(DELS_ERR_ALIGNMENT, "GRU hidden size %d must be a multiple of 8, w_hh and h 16-byte aligned", G);
+  if (rows > kSkinnyStageRows)
+    return fail(DELS_ERR_UNSUPPORTED, "at most %d rows (got %d)", kSkinnyStageRows, rows);
+  TcArgs gh;
+  std::memset(&gh, 0, sizeof(gh));
+  gh.gh_w = reinterpret_cast<const __nv_bfloat16*>(w_hh);
+  gh.gh_bias = reinterpret_cast<const __nv_bfloat16*>(b_hh);
+  gh.gh_x = reinterpret_cast<const __nv_bfloat16*>(h);
+  gh.gh_out = reinterpret_cast<__nv_bfloat16*>(gh_out);
+  gh.gh_rows = 3 * G;
+  gh.gh_k = G;
+  return fused_argmax_common(nullptr, 0, nullptr, 0, base, ld_base, s_scaled, ld_s, Vr, ld_vr, prior, beta, n_pos,
+                             nullptr, rows, nullptr, 0, r, V, 0, flags, keys, idx_out, nullptr, ws, ws_bytes,
+                             reinterpret_cast<cudaStream_t>(stream), &gh);
 }
 
 size_t dels_score_workspace_bytes(int rows, int H, int r) {
@@ -1017,14 +1061,14 @@ int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, const void* g
 static int rank_gemv_common(const void* x, int64_t ld_x, const void* w, int64_t ld_w, const void* bias,
                             const void* addend, int64_t ld_add, int B, int K, int r, int activation,
                             const float* alpha, int n_pos, const int32_t* row_pos, void* s_out, void* s_scaled,
-                            int64_t* keys, void* ws, void* stream) {
+                            int64_t* keys, void* ws, void* stream, const GruGateSrc* gate = nullptr) {
   int rc;
   if (B < 0 || K <= 0 || r <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d K=%d r=%d", B, K, r);
   if ((K % 8) != 0) return fail(DELS_ERR_UNSUPPORTED, "K = %d must be a multiple of 8", K);
   if (activation != DELS_ACT_IDENTITY && activation != DELS_ACT_SILU)
     return fail(DELS_ERR_INVALID_ARG, "unsupported rank activation %d", activation);
   if (n_pos <= 0 || s_scaled == nullptr) return fail(DELS_ERR_INVALID_ARG, "n_pos <= 0 or s_scaled NULL");
-  if ((rc = check_bf16_matrix("x", x, ld_x, K)) != DELS_OK) return rc;
+  if (gate == nullptr && (rc = check_bf16_matrix("x", x, ld_x, K)) != DELS_OK) return rc;
   if ((rc = check_bf16_matrix("w_rank", w, ld_w, K)) != DELS_OK) return rc;
   if (addend != nullptr && ld_add < r) return fail(DELS_ERR_INVALID_ARG, "z leading dimension %lld < %d",
                                                    (long long)ld_add, r);
@@ -1039,7 +1083,8 @@ static int rank_gemv_common(const void* x, int64_t ld_x, const void* w, int64_t 
       reinterpret_cast<const __nv_bfloat16*>(x), ld_x, reinterpret_cast<const __nv_bfloat16*>(w), ld_w,
       reinterpret_cast<const __nv_bfloat16*>(bias), reinterpret_cast<const __nv_bfloat16*>(addend),
       (long long)ld_add, B, K, r, activation, alpha, n_pos, row_pos, reinterpret_cast<__nv_bfloat16*>(s_out),
-      reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys), counter));
+      reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys), counter,
+      gate != nullptr ? *gate : GruGateSrc{}));
   return DELS_OK;
 }
 
@@ -1048,6 +1093,32 @@ int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w
                         void* s_scaled, int64_t* keys, void* ws, void* stream) {
   return rank_gemv_common(x, ld_x, w, ld_w, bias, nullptr, 0, B, K, r, activation, alpha, n_pos, row_pos, s_out,
                           s_scaled, keys, ws, stream);
+}
+
+int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+                            const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V,
+                            const void* w_rank, int64_t ld_w, const void* bias, int r, int activation,
+                            const float* alpha, void* s_scaled, int64_t* keys, void* ws, void* stream) {
+  if (B < 0 || G <= 0 || V <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d V=%d", B, G, V);
+  if (tokens == nullptr || gi_table == nullptr || gh == nullptr || h_out == nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if ((G % 8) != 0 || (ld_table % 8) != 0 || (ld_gh % 8) != 0 || !aligned16(gi_table) || !aligned16(gh) ||
+      !aligned16(h_out) || (h_in != nullptr && !aligned16(h_in)))
+    return fail(DELS_ERR_ALIGNMENT, "gi table / gh / h rows must be 16-byte aligned (G, ld %% 8 == 0)");
+  if (ld_table < 3LL * G || ld_gh < 3LL * G) return fail(DELS_ERR_INVALID_ARG, "gi / gh leading dimension < 3G");
+  GruGateSrc gate;
+  gate.tokens = reinterpret_cast<const long long*>(tokens);
+  gate.tok_stride = tok_stride;
+  gate.table = reinterpret_cast<const __nv_bfloat16*>(gi_table);
+  gate.ld_table = ld_table;
+  gate.gh = reinterpret_cast<const __nv_bfloat16*>(gh);
+  gate.ld_gh = ld_gh;
+  gate.h_in = reinterpret_cast<const __nv_bfloat16*>(h_in);
+  gate.h_out = reinterpret_cast<__nv_bfloat16*>(h_out);
+  gate.V = V;
+  gate.status = ws != nullptr ? reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + 4) : nullptr;
+  return rank_gemv_common(nullptr, G, w_rank, ld_w, bias, nullptr, 0, B, G, r, activation, alpha, 1, nullptr,
+                          nullptr, s_scaled, keys, ws, stream, &gate);
 }
 
 int dels_correction_mid_bf16(const void* h, int64_t ld_h, const void* w_s, int64_t ld_ws, const void* z,

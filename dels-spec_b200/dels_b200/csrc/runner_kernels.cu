@@ -100,7 +100,6 @@ __device__ __forceinline__ void warp_row_dots(const RowPrefetch& pre, const __nv
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 }  // namespace
 
@@ -166,10 +165,7 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
       const float gh_z = gh_s[(1 * kGruCols + c) * kRunnerMaxB + b];
       const float gh_n = gh_s[(2 * kGruCols + c) * kRunnerMaxB + b];
       const float h = __bfloat162float(hs[(size_t)b * G + g]);
-      const float rg = sigmoidf_(gi_r + gh_r);
-      const float zg = sigmoidf_(gi_z + gh_z);
-      const float ng = tanhf(gi_n + rg * gh_n);
-      h_out[(long long)(b0 + b) * G + g] = __float2bfloat16_rn((1.0f - zg) * ng + zg * h);
+      h_out[(long long)(b0 + b) * G + g] = __float2bfloat16_rn(gru_unit(gi_r, gi_z, gi_n, gh_r, gh_z, gh_n, h));
     }
   }
   pdl_trigger();
@@ -182,7 +178,7 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
     const __nv_bfloat16* __restrict__ x, long long ld_x, const __nv_bfloat16* __restrict__ w, long long ld_w,
     const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ addend, long long ld_add, int B,
     int K, int r, int activation, const float* __restrict__ alpha, int n_pos, const int* __restrict__ row_pos,
-    __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter) {
+    __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter, const GruGateSrc gate) {
   extern __shared__ uint4 smem4[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);  // [kRunnerMaxB][K]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -194,10 +190,47 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
   for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
     const int nb = min(kRunnerMaxB, B - b0);
     __syncthreads();
-    for (int e = threadIdx.x; e < nb * K / 8; e += blockDim.x) {
-      const int b = e / (K / 8), k8 = e % (K / 8);
-      reinterpret_cast<uint4*>(xs + (size_t)b * K)[k8] =
-          *reinterpret_cast<const uint4*>(x + (long long)(b0 + b) * ld_x + k8 * 8);
+    if (gate.table != nullptr) {
+      // x = the GRU's new hidden state (K = G units), eight units per thread: every CTA
+      // evaluates all of them from L2-resident inputs instead of waiting for a GRU kernel
+      for (int e = threadIdx.x; e < nb * K / 8; e += blockDim.x) {
+        const int b = e / (K / 8), k8 = e % (K / 8);
+        const int row = b0 + b;
+        long long tok = gate.tokens[(long long)row * gate.tok_stride];
+        if (tok < 0 || tok >= gate.V) {
+          if (gate.status != nullptr) atomicCAS(gate.status, 0, DELS_ERR_INVALID_ARG);
+          tok = tok < 0 ? 0 : gate.V - 1;
+        }
+        const uint4* gi = reinterpret_cast<const uint4*>(gate.table + tok * gate.ld_table) + k8;
+        const uint4* gh = reinterpret_cast<const uint4*>(gate.gh + (long long)row * gate.ld_gh) + k8;
+        const int G8 = K / 8;  // uint4 per gate block
+        const uint4 ir = __ldg(gi), iz = __ldg(gi + G8), in = __ldg(gi + 2 * G8);
+        const uint4 hr = gh[0], hz = gh[G8], hn = gh[2 * G8];
+        const uint4 hp = gate.h_in != nullptr
+                             ? *(reinterpret_cast<const uint4*>(gate.h_in + (long long)row * K) + k8)
+                             : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t* a_r = &ir.x; const uint32_t* a_z = &iz.x; const uint32_t* a_n = &in.x;
+        const uint32_t* b_r = &hr.x; const uint32_t* b_z = &hz.x; const uint32_t* b_n = &hn.x;
+        const uint32_t* c_h = &hp.x;
+        uint4 o;
+        uint32_t* op = &o.x;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float lo = gru_unit(bf16_lo(a_r[q]), bf16_lo(a_z[q]), bf16_lo(a_n[q]), bf16_lo(b_r[q]),
+                                    bf16_lo(b_z[q]), bf16_lo(b_n[q]), bf16_lo(c_h[q]));
+          const float hi = gru_unit(bf16_hi(a_r[q]), bf16_hi(a_z[q]), bf16_hi(a_n[q]), bf16_hi(b_r[q]),
+                                    bf16_hi(b_z[q]), bf16_hi(b_n[q]), bf16_hi(c_h[q]));
+          op[q] = pack_bf16x2(lo, hi);
+        }
+        reinterpret_cast<uint4*>(xs + (size_t)b * K)[k8] = o;
+        if (blockIdx.x == 0) reinterpret_cast<uint4*>(gate.h_out + (long long)row * K)[k8] = o;
+      }
+    } else {
+      for (int e = threadIdx.x; e < nb * K / 8; e += blockDim.x) {
+        const int b = e / (K / 8), k8 = e % (K / 8);
+        reinterpret_cast<uint4*>(xs + (size_t)b * K)[k8] =
+            *reinterpret_cast<const uint4*>(x + (long long)(b0 + b) * ld_x + k8 * 8);
+      }
     }
     __syncthreads();
     for (int j = gwarp; j < r; j += nwarps) {
@@ -257,10 +290,9 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
     const __nv_bfloat16* gi = table + tok * ld_table;
     const __nv_bfloat16* ghb = gh + (long long)b * ld_gh;
     const float h = h_in != nullptr ? __bfloat162float(h_in[(long long)b * G + g]) : 0.0f;
-    const float rg = sigmoidf_(__bfloat162float(gi[g]) + __bfloat162float(ghb[g]));
-    const float zg = sigmoidf_(__bfloat162float(gi[G + g]) + __bfloat162float(ghb[G + g]));
-    const float ng = tanhf(__bfloat162float(gi[2 * G + g]) + rg * __bfloat162float(ghb[2 * G + g]));
-    h_out[(long long)b * G + g] = __float2bfloat16_rn((1.0f - zg) * ng + zg * h);
+    h_out[(long long)b * G + g] = __float2bfloat16_rn(
+        gru_unit(__bfloat162float(gi[g]), __bfloat162float(gi[G + g]), __bfloat162float(gi[2 * G + g]),
+                 __bfloat162float(ghb[g]), __bfloat162float(ghb[G + g]), __bfloat162float(ghb[2 * G + g]), h));
   }
   pdl_trigger();
 }

@@ -15,6 +15,34 @@ inline size_t gru_smem_bytes(int G) {
 }
 inline size_t rank_gemv_smem_bytes(int K) { return (size_t)kRunnerMaxB * K * 2; }
 
+// x of rank_gemv_kernel computed in place as the GRU's new hidden state (table == null:
+// x is read from memory): h_out[b] = GRU gates of (gi = table[tokens[b * tok_stride]],
+// gh[b], h_in[b]), staged in shared memory by every CTA and stored by CTA 0.
+struct GruGateSrc {
+  const long long* tokens;
+  long long tok_stride;
+  const __nv_bfloat16* table;  // [V, 3G] input projections, or null
+  long long ld_table;
+  const __nv_bfloat16* gh;     // [B, 3G] bf16(W_hh h + b_hh)
+  long long ld_gh;
+  const __nv_bfloat16* h_in;   // [B, G], null = zero state
+  __nv_bfloat16* h_out;        // [B, G]
+  int V;
+  int* status;
+};
+
+// One GRU unit (code/kernel/dels.py:368-373): r, z = sigmoid(gi + gh), n = tanh(gi_n + r gh_n),
+// h' = (1 - z) n + z h, in fp32 with the products pinned to explicit FMAs so that every
+// kernel that evaluates it rounds alike.
+__device__ __forceinline__ float sigmoid_unit(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float gru_unit(float gi_r, float gi_z, float gi_n, float gh_r, float gh_z, float gh_n,
+                                          float h) {
+  const float rg = sigmoid_unit(gi_r + gh_r);
+  const float zg = sigmoid_unit(gi_z + gh_z);
+  const float ng = tanhf(fmaf(rg, gh_n, gi_n));
+  return fmaf(zg, h, (1.0f - zg) * ng);
+}
+
 __global__ void gru_step_kernel(const long long* __restrict__ tokens, long long tok_stride,
                                 const __nv_bfloat16* __restrict__ table, long long ld_table,
                                 const __nv_bfloat16* __restrict__ w_hh, const __nv_bfloat16* __restrict__ b_hh,
@@ -25,7 +53,8 @@ __global__ void rank_gemv_kernel(const __nv_bfloat16* __restrict__ x, long long 
                                  const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ addend,
                                  long long ld_add, int B, int K, int r, int activation,
                                  const float* __restrict__ alpha, int n_pos, const int* __restrict__ row_pos,
-                                 __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter);
+                                 __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter,
+                                 const GruGateSrc gate);
 
 __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long tok_stride,
                                  const __nv_bfloat16* __restrict__ table, long long ld_table,

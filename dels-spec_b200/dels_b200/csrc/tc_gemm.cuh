@@ -71,6 +71,13 @@ struct TcArgs {
   __nv_bfloat16* out_bf16;         // non-null: bf16 result (k_splits == 1), row stride ld_out
   const __nv_bfloat16* bias_bf16;  // [n_cols] or null (out_bf16 only)
   int out_vec;                     // out_bf16 and ld_out allow 16-byte stores
+  // skinny scorer with helper warps (tc_skinny_gh_kernel): the next rollout step's
+  // gh_out[b] = bf16(gh_w . gh_x[b] + gh_bias), beside the scoring pipeline
+  const __nv_bfloat16* gh_w;     // [gh_rows, gh_k]
+  const __nv_bfloat16* gh_bias;  // [gh_rows] or null
+  const __nv_bfloat16* gh_x;     // [gh_b, gh_k]
+  __nv_bfloat16* gh_out;         // [gh_b, gh_rows]
+  int gh_rows, gh_k, gh_b;
 };
 
 // STAGED: the argmax epilogue with base logits prefetches each tile's base rows and

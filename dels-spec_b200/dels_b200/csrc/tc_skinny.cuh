@@ -21,7 +21,8 @@
 // atomicMax per row.
 //
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
-// warps 2..5 = epilogue (TMEM lane quadrant = warp % 4).
+// warps 2..5 = epilogue (TMEM lane quadrant = warp % 4); tc_skinny_gh_kernel adds warps
+// 6..7, which compute the next rollout step's W_hh h while the others score.
 // Reference: code/kernel/dels.py:49-79 + :443-456 (the per-step low-rank scorer and
 // argmax of the greedy rollout) and code/dflash.py:468 (the long-logit GEMM).
 #pragma once
@@ -31,6 +32,8 @@
 namespace dels {
 
 constexpr int kSkinnyBM = 128;  // vocab rows per tile (MMA M)
+constexpr int kSkinnyGhThreads = kTcThreads + 64;  // + two helper warps (tc_skinny_gh_kernel)
+constexpr int kSkinnyGhMaxB = 4;                   // rows of the helpers' GEMV
 
 template <int NB>
 struct SkinnyConfig {
@@ -56,7 +59,9 @@ struct SkinnyConfig {
 // the K blocks of the two segments (kb0 = 0 for the base-logit variant).  With STAGE:
 // `map_base` = base logits [rows, V slice] in 128 x NB boxes (when args.base is set) and
 // `map_prior` = the prior [V slice] fp32 in 128-element boxes (when args.prior is set).
-template <int NB, bool STAGE>
+// GH: warps 6 and 7 compute args.gh_out (the next rollout step's W_hh h), one output row
+// per warp at a time over a grid-wide stride, while warps 0-5 score.
+template <int NB, bool STAGE, bool GH = false>
 __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUtensorMap* map_b0,
                                             const CUtensorMap* map_a1, const CUtensorMap* map_b1,
                                             const CUtensorMap* map_base, const CUtensorMap* map_prior,
@@ -285,7 +290,7 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
         }
       }
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp can access
     const int nrows = m_rows < NB ? m_rows : NB;
@@ -379,6 +384,81 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
         __threadfence();
       }
     }
+  } else if constexpr (GH) {
+    // ---------------------------------------------------------------- helpers: gh_out
+    // gh_x was written by an earlier kernel (complete after pdl_wait above); lanes stride
+    // the row 16 bytes at a time, then a warp reduction per output row.
+    if (args.gh_out != nullptr) {
+      // A warp takes rows hw, hw + nhw, ... in groups of kRows; each lane loads its 16-byte
+      // pieces of all the group's rows (up to 4 x 32 pieces per row per pass) before any
+      // arithmetic, so a group costs one memory round trip instead of one per row.
+      constexpr int kRows = 4, kPieces = 4;
+      const int nb = args.gh_b < kSkinnyGhMaxB ? args.gh_b : kSkinnyGhMaxB;
+      const int k8n = args.gh_k / 8;
+      const int hw = (int)blockIdx.x * 2 + (warp - 6);
+      const int nhw = (int)gridDim.x * 2;
+      for (int j0 = hw; j0 < args.gh_rows; j0 += nhw * kRows) {
+        float acc[kRows][kSkinnyGhMaxB];
+#pragma unroll
+        for (int g = 0; g < kRows; ++g)
+#pragma unroll
+          for (int b = 0; b < kSkinnyGhMaxB; ++b) acc[g][b] = 0.0f;
+        for (int c0 = 0; c0 < k8n; c0 += 32 * kPieces) {
+          uint4 w[kRows][kPieces];
+#pragma unroll
+          for (int g = 0; g < kRows; ++g) {
+            const int j = j0 + g * nhw;
+#pragma unroll
+            for (int q = 0; q < kPieces; ++q) {
+              const int c = c0 + q * 32 + lane;
+              w[g][q] = (j < args.gh_rows && c < k8n)
+                            ? __ldg(reinterpret_cast<const uint4*>(args.gh_w + (long long)j * args.gh_k) + c)
+                            : make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < kSkinnyGhMaxB; ++b) {
+            if (b < nb) {
+#pragma unroll
+              for (int q = 0; q < kPieces; ++q) {
+                const int c = c0 + q * 32 + lane;
+                const uint4 x = c < k8n ? reinterpret_cast<const uint4*>(args.gh_x + (long long)b * args.gh_k)[c]
+                                        : make_uint4(0u, 0u, 0u, 0u);
+                const float x0 = bf16_lo(x.x), x1 = bf16_hi(x.x), x2 = bf16_lo(x.y), x3 = bf16_hi(x.y);
+                const float x4 = bf16_lo(x.z), x5 = bf16_hi(x.z), x6 = bf16_lo(x.w), x7 = bf16_hi(x.w);
+#pragma unroll
+                for (int g = 0; g < kRows; ++g) {
+                  float a = acc[g][b];
+                  a = fmaf(bf16_lo(w[g][q].x), x0, a);
+                  a = fmaf(bf16_hi(w[g][q].x), x1, a);
+                  a = fmaf(bf16_lo(w[g][q].y), x2, a);
+                  a = fmaf(bf16_hi(w[g][q].y), x3, a);
+                  a = fmaf(bf16_lo(w[g][q].z), x4, a);
+                  a = fmaf(bf16_hi(w[g][q].z), x5, a);
+                  a = fmaf(bf16_lo(w[g][q].w), x6, a);
+                  a = fmaf(bf16_hi(w[g][q].w), x7, a);
+                  acc[g][b] = a;
+                }
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < kRows; ++g) {
+          const int j = j0 + g * nhw;
+#pragma unroll
+          for (int b = 0; b < kSkinnyGhMaxB; ++b) {
+            float a = acc[g][b];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+            if (lane == 0 && b < nb && j < args.gh_rows) {
+              const float bj = args.gh_bias != nullptr ? __bfloat162float(args.gh_bias[j]) : 0.0f;
+              args.gh_out[(long long)b * args.gh_rows + j] = __float2bfloat16_rn(a + bj);
+            }
+          }
+        }
+      }
+    }
   }
 
   // ------------------------------------------------------------------ teardown
@@ -417,6 +497,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
                      const TcArgs args) {
   skinny_body<NB, false>(&map_a0, &map_b0, &map_a1, &map_b1, nullptr, nullptr, args);
+}
+
+// The plain scorer plus the helper warps that compute the next rollout step's gh.
+template <int NB>
+__global__ void __launch_bounds__(kSkinnyGhThreads, 1)
+    tc_skinny_gh_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                        const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                        const TcArgs args) {
+  skinny_body<NB, false, true>(&map_a0, &map_b0, &map_a1, &map_b1, nullptr, nullptr, args);
 }
 
 template <int NB>

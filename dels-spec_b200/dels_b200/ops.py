@@ -333,6 +333,44 @@ def fused_argmax_base_bf16(
     return out
 
 
+def fused_argmax_base_gru_bf16(
+    base: torch.Tensor,
+    s_scaled: torch.Tensor,
+    Vr: torch.Tensor,
+    prior: torch.Tensor | None,
+    beta: torch.Tensor,
+    w_hh: torch.Tensor,
+    b_hh: torch.Tensor | None,
+    h: torch.Tensor,
+    gh_out: torch.Tensor,
+    *,
+    keys_ready: bool = False,
+    out: ScoreOut,
+    ws: Workspace,
+) -> ScoreOut:
+    """fused_argmax_base_bf16 for a rollout step of at most 4 rows that also computes the
+    next step's gh_out = bf16(w_hh . h + b_hh) in the same launch."""
+    dev = base.device
+    for name, t in (("base", base), ("s_scaled", s_scaled), ("Vr", Vr), ("w_hh", w_hh), ("h", h), ("gh_out", gh_out)):
+        _require_cuda(name, t, torch.bfloat16, 2)
+    rows, V = base.shape
+    r = Vr.shape[1]
+    G = h.shape[1]
+    if Vr.shape[0] != V or s_scaled.shape != (rows, r):
+        raise ValueError("shape mismatch between base, s_scaled and Vr")
+    if w_hh.shape != (3 * G, G) or not w_hh.is_contiguous() or h.shape != (rows, G) or not h.is_contiguous() \
+            or gh_out.shape != (rows, 3 * G) or not gh_out.is_contiguous():
+        raise ValueError("GRU operands do not match")
+    _lib.call(
+        "dels_fused_argmax_base_gru_bf16",
+        _ptr(base), _row_major("base", base), _ptr(s_scaled), _row_major("s_scaled", s_scaled), _ptr(Vr),
+        _row_major("Vr", Vr), _ptr(_f32_vec("prior", prior, dev)), _ptr(_f32_vec("beta", beta, dev)),
+        _positions(None, None, beta), rows, r, V, _lib.DELS_FLAG_KEYS_READY if keys_ready else 0, _ptr(out.keys),
+        _ptr(out.tokens), ws.ptr, ws.nbytes, _ptr(w_hh), _ptr(b_hh), _ptr(h), G, _ptr(gh_out), _stream(dev),
+    )
+    return out
+
+
 def draft_score_f32(
     h: torch.Tensor,
     W: torch.Tensor,
@@ -551,6 +589,46 @@ def gru_gates(
               _ptr(gh), gh.stride(0), _ptr(h_in), _ptr(h_out), B, G, V, None if ws is None else ws.ptr,
               _stream(h_out.device))
     return h_out
+
+
+def gru_rank_gemv(
+    tokens: torch.Tensor,
+    gi_table: torch.Tensor,
+    gh: torch.Tensor,
+    h_in: torch.Tensor | None,
+    h_out: torch.Tensor,
+    w_rank: torch.Tensor,
+    alpha: torch.Tensor | None,
+    s_scaled: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    activation: str = "identity",
+    keys: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """One small-batch rollout step: h_out = GRU gates(gi_table[tokens], gh, h_in) (gh =
+    bf16(W_hh h_in + b_hh) from an earlier rank_gemv), then s_scaled = bf16(alpha[0] *
+    act(w_rank . h_out + bias)) in the same launch."""
+    _require_cuda("tokens", tokens, torch.int64)
+    _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
+    _require_cuda("gh", gh, torch.bfloat16, 2)
+    _require_cuda("h_out", h_out, torch.bfloat16, 2)
+    _require_cuda("w_rank", w_rank, torch.bfloat16, 2)
+    B, G = h_out.shape
+    V = gi_table.shape[0]
+    r = w_rank.shape[0]
+    if gh.shape != (B, 3 * G) or gh.stride(1) != 1 or gi_table.shape[1] != 3 * G or not h_out.is_contiguous():
+        raise ValueError("GRU gate operands do not match the hidden size")
+    if h_in is not None and (h_in.shape != (B, G) or not h_in.is_contiguous()):
+        raise ValueError("h_in must be a contiguous [B, G] tensor")
+    if w_rank.shape[1] != G or s_scaled.shape != (B, r) or not s_scaled.is_contiguous():
+        raise ValueError("rank projection shapes do not match")
+    tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
+    _lib.call("dels_gru_rank_gemv_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+              _ptr(gh), gh.stride(0), _ptr(h_in), _ptr(h_out), B, G, V, _ptr(w_rank), _row_major("w_rank", w_rank),
+              _ptr(bias), r, ACTIVATIONS[activation], _ptr(alpha), _ptr(s_scaled), _ptr(keys),
+              None if ws is None else ws.ptr, _stream(h_out.device))
+    return s_scaled
 
 
 def rank_gemv(

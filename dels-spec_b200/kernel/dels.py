@@ -4,14 +4,19 @@ Drop-in for ``kernel.dels.DeLSGraphRunner`` of the reference (code/kernel/dels.p
 same constructor keywords, same ``ValueError`` checks, same ``__call__(prefix_ids,
 base_logits) -> LongTensor[B, steps]`` returning a fresh tensor, same static buffers
 (``static_prefix_ids``, ``static_base_logits``, ``static_out``), warm-up on a side
-stream and capture into ``self.graph``.  Each captured step is three kernels of
-``libdels_b200.so``:
+stream and capture into ``self.graph``.  At small batches each captured step is, in
+``libdels_b200.so`` kernels:
 
-  1. GRU step: token -> input-table row, W_hh h, gates (``dels_gru_step_bf16``);
-  2. rank projection + activation + alpha_step scaling, keys reset (``dels_rank_gemv_bf16``);
-  3. fused scorer on tcgen05 tensor cores: base logits + low-rank logits - beta * prior,
-     argmax with the lowest index on ties, written straight into the step's token slot
-     (``dels_fused_argmax_base_bf16``).
+  1. the GRU gates of the previous token (input-table row, gh, h) fused into the rank
+     projection + activation + alpha_step scaling, keys reset (``dels_gru_rank_gemv_bf16``);
+  2. the fused scorer on tcgen05 tensor cores: base logits + low-rank logits - beta *
+     prior, argmax with the lowest index on ties, written straight into the step's token
+     slot (``dels_fused_argmax_base_bf16``);
+  3. beside 2, on a side stream of the graph: the next step's gh = bf16(W_hh h + b_hh)
+     (``dels_rank_gemv_bf16``), which needs h but not the token.
+
+From ``DELS_RUNNER_TC_ROWS`` rows up W_hh h and the rank projection run as tensor-core
+GEMMs instead (``dels_linear_bf16`` + ``dels_gru_gates_bf16``, ``dels_rank_project_bf16``).
 
 alpha / beta live in device arrays indexed by step, so one graph serves a schedule;
 the reference instead bakes them into the Triton kernels as constexprs (:404-409).
@@ -144,9 +149,17 @@ class DeLSGraphRunner:
         # finalisation); below it one warp per weight row does each in a single launch.
         tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
         self._tc = B >= tc_rows and self.rank_bias is None
+        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 4, at most 4; 0 turns it off) a step is
+        # two kernels: the GRU gates fused into the rank projection (dels_gru_rank_gemv_bf16),
+        # then the scorer, whose two helper warps per CTA compute the next step's W_hh h
+        # (which needs h but not the token) while the others score
+        # (dels_fused_argmax_base_gru_bf16).
+        self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "4"))) and not self._tc
+                         and self._scorer_computes_next_gh())
         if self._tc:
             need = max(ops.linear_workspace_bytes(B, G, 3 * G), ops.rank_workspace_bytes(B, G, r))
             self._tc_ws = ops.Workspace(need, device)
+        if self._tc or self._overlap:
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
             # the first step's h is zero, so its gh is the bias alone
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
@@ -184,7 +197,24 @@ class DeLSGraphRunner:
                                   activation=self._activation, s_scaled=self._s_scaled, keys=self._keys,
                                   want_state=False, ws=self._tc_ws)
 
+    def _forward_overlapped(self):
+        tokens, h_prev, gh, cur = self.static_prefix_ids[:, 0], None, self._gh0, 0
+        for step in range(self.steps):
+            h_new = self._h[cur]
+            ops.gru_rank_gemv(tokens, self._gru_input_proj_table, gh, h_prev, h_new, self.rank_weight,
+                              self._alpha[step : step + 1], self._s_scaled, bias=self.rank_bias,
+                              activation=self._activation, keys=self._keys, ws=self._ws)
+            if step + 1 < self.steps:
+                # the scorer's helper warps compute the next step's gh = bf16(W_hh h_new + b_hh)
+                self._score(step, next_gh=(h_new, self._gh))
+            else:
+                self._score(step)
+            tokens, h_prev, gh, cur = self._tokens[step], h_new, self._gh, cur ^ 1
+        self.static_out.copy_(self._tokens.t())
+
     def _forward_impl(self):
+        if self._overlap:
+            return self._forward_overlapped()
         prefix = self.static_prefix_ids[:, 0]
         h_cur = self._gru(prefix, None, self._h[0])
         nxt = 1
@@ -201,7 +231,18 @@ class DeLSGraphRunner:
         self.static_base_logits = torch.zeros(self.batch_size, self.steps, self.vocab_size, dtype=dtype,
                                               device=device)
 
-    def _score(self, step: int):
+    def _scorer_computes_next_gh(self) -> bool:
+        return True
+
+    def _score(self, step: int, next_gh=None):
+        if next_gh is not None:
+            h, gh_out = next_gh
+            ops.fused_argmax_base_gru_bf16(
+                self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight, self._prior_f32,
+                self._beta[step : step + 1], self.gru_w_hh, self.gru_b_hh, h, gh_out, keys_ready=True,
+                out=self._outs[step], ws=self._ws,
+            )
+            return
         ops.fused_argmax_base_bf16(
             self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight,
             self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],
@@ -269,9 +310,14 @@ class DeLSFusedGraphRunner(DeLSGraphRunner):
                             out=self.static_base_logits.view(B * S, self.vocab_size), ws=self._lm_ws)
         super()._forward_impl()
 
-    def _score(self, step: int):
+    def _scorer_computes_next_gh(self) -> bool:
+        return not self._fused  # the hidden-state scorer has no helper warps
+
+    def _score(self, step: int, next_gh=None):
         if not self._fused:
-            return super()._score(step)
+            return super()._score(step, next_gh)
+        if next_gh is not None:
+            raise RuntimeError("the per-step fused scorer does not compute the GRU projection")
         ops.fused_argmax_bf16(
             self.static_parallel_hiddens[:, step, :], self._lm_weight, self._s_scaled, self.lm_head_weight,
             self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],

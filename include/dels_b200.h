@@ -233,6 +233,36 @@ DELS_API int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int
                                  const int32_t* row_pos, void* s_out, void* s_scaled, int64_t* keys, void* ws,
                                  void* stream);
 
+/* The base-logit scorer of one rollout step (dels_fused_argmax_base_bf16, row positions
+ * 0..rows-1, v_begin 0, no score output) with the NEXT step's GRU hidden projection in the
+ * same launch: gh_out[b] = bf16(w_hh . h[b] + b_hh), w_hh [3G, G], h [rows, G] (the
+ * state after this step's GRU update), gh_out [rows, 3G] (code/kernel/dels.py:366,
+ * F.linear(h_state, W_hh, b_hh)).  It needs h but not this step's token, so two extra
+ * warps per CTA compute it while the others score, and the next step's
+ * dels_gru_rank_gemv_bf16 starts from it.  At most 4 rows; G % 8 == 0. */
+DELS_API int dels_fused_argmax_base_gru_bf16(const void* base, int64_t ld_base, const void* s_scaled, int64_t ld_s,
+                                             const void* Vr, int64_t ld_vr, const float* prior, const float* beta,
+                                             int n_pos, int rows, int r, int V, uint32_t flags, int64_t* keys,
+                                             int64_t* idx_out, void* ws, size_t ws_bytes, const void* w_hh,
+                                             const void* b_hh, const void* h, int G, void* gh_out, void* stream);
+
+/* One small-batch rollout step's GRU gates fused into its rank projection
+ * (code/kernel/dels.py:368-373 then :437-443):
+ *   h_out[b] = GRU gates of (gi = gi_table[tokens[b * tok_stride]], gh[b], h_in[b]) as in
+ *   dels_gru_gates_bf16, then s = bf16(act(bf16(w_rank . h_out[b] + bias))),
+ *   s_scaled[b] = bf16(alpha[0] * s), keys[0..B) reset, as in dels_rank_gemv_bf16.
+ * gh = bf16(W_hh h_in + b_hh) comes from an earlier call (dels_rank_gemv_bf16 with
+ * w = W_hh, bias = b_hh, identity activation and alpha NULL), which can run beside the
+ * previous step's scorer since it does not need that step's token.  Every CTA evaluates
+ * the gates for all B rows itself; G, ld_table, ld_gh % 8 == 0, 16-byte aligned rows.
+ * ws (optional) supplies the counter that the following scorer call expects at zero and
+ * the status word for out-of-range token ids (clamped). */
+DELS_API int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table,
+                                     int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in, void* h_out,
+                                     int B, int G, int V, const void* w_rank, int64_t ld_w, const void* bias, int r,
+                                     int activation, const float* alpha, void* s_scaled, int64_t* keys, void* ws,
+                                     void* stream);
+
 /* Markov rank state (code/kernel/markov_dels.py:288):
  *   s_scaled[b] = bf16(alpha_p * emb[tokens[b * tok_stride]]),  emb [V, r] bf16,
  * keys[0..B) reset.  Out-of-range ids are clamped and flagged as above. */

@@ -45,9 +45,13 @@ def _compare(ours, gaps, ref, thresh):
     return n
 
 
-def test_dels_runner_matches_reference_fixture(cuda_device, golden_dir):
+@pytest.mark.parametrize("overlap", ["1", "0"])
+def test_dels_runner_matches_reference_fixture(cuda_device, golden_dir, monkeypatch, overlap):
+    """Both small-batch schedules: the GRU gates fused into the rank projection with W_hh h
+    beside the scorer (default), and the GRU step kernel before the rank GEMV."""
     from kernel.dels import DeLSGraphRunner
 
+    monkeypatch.setenv("DELS_RUNNER_OVERLAP_ROWS", "64" if overlap == "1" else "0")
     g = np.load(golden_dir / "runners.npz")
     total = 0
     for c in json.loads(str(g["meta"])):
@@ -146,6 +150,39 @@ def test_runner_full_vocab_b1(cuda_device):
     toks, gaps = O.dels_runner_rollout(prefix, base, embed=None, w_ih=None, w_hh=w["w_hh"], w_rank=w["w_rank"],
                                        Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta, bf16=True, table=table)
     assert _compare(out.cpu().numpy(), gaps, toks, 1e-2) >= 3
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_scorer_with_next_gru_projection(cuda_device, B):
+    """dels_fused_argmax_base_gru_bf16: the same tokens as the plain base-logit scorer, and
+    gh_out within one bf16 rounding of bf16(W_hh h + b_hh) (helper warps' fp32 sums)."""
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(90 + B)
+    V, r, G = 5003, 64, 256
+    base = torch.from_numpy(O.bf16_round(rng.standard_normal((B, V)).astype(np.float32))).to(cuda_device)
+    s = torch.from_numpy(O.bf16_round((rng.standard_normal((B, r)) * 0.3).astype(np.float32))).to(cuda_device)
+    Vr = torch.from_numpy(O.bf16_round((rng.standard_normal((V, r)) * 0.3).astype(np.float32))).to(cuda_device)
+    prior = torch.from_numpy(O.bf16_round(O.zipf_log_prior(V).astype(np.float32))).to(cuda_device)
+    beta = torch.tensor([0.2], device=cuda_device)
+    w_hh = O.bf16_round((rng.standard_normal((3 * G, G)) * 0.1).astype(np.float32))
+    b_hh = O.bf16_round(rng.standard_normal(3 * G).astype(np.float32))
+    h = O.bf16_round(rng.standard_normal((B, G)).astype(np.float32))
+    bf = lambda a: torch.from_numpy(a).to(cuda_device).to(torch.bfloat16)  # noqa: E731
+    base, s, Vr = base.to(torch.bfloat16), s.to(torch.bfloat16), Vr.to(torch.bfloat16)
+    ws = ops.Workspace(1 << 12, cuda_device)
+    ref = ops.fused_argmax_base_bf16(base, s, Vr, prior, beta, n_pos=1, ws=ws)
+    out = ops.ScoreOut(tokens=torch.empty(B, dtype=torch.int64, device=cuda_device), scores=None,
+                       keys=torch.empty(B, dtype=torch.int64, device=cuda_device))
+    gh = torch.full((B, 3 * G), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    ops.fused_argmax_base_gru_bf16(base, s, Vr, prior, beta, bf(w_hh), bf(b_hh), bf(h), gh, out=out, ws=ws)
+    ws.check()
+    assert torch.equal(out.tokens, ref.tokens)
+    exact = h.astype(np.float64) @ w_hh.astype(np.float64).T + b_hh.astype(np.float64)
+    got = gh.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.mean(got == O.bf16_round(exact.astype(np.float32))) > 0.99
+    np.testing.assert_allclose(got, exact, rtol=2 ** -7, atol=1e-3)
 
 
 @pytest.mark.parametrize("B", [5, 20, 48, 64])
