@@ -678,6 +678,16 @@ def run_rnn(args, rank, world, dev):
     }
 
 
+def runner_launches(runner, steps: int) -> int:
+    """Kernels of libdels_b200.so one DeLSGraphRunner call launches (its graph replay)."""
+    lm = 1 if hasattr(runner, "_lm_ws") else 0  # the long-logit GEMM of the materialising runner
+    if runner._overlap:  # gates + rank GEMV, scorer (with the next step's W_hh h)
+        return lm + 2 * steps
+    if runner._tc:  # gates; per step rank GEMM + finalisation, scorer; W_hh GEMM (+ finalisation)
+        return lm + 1 + 3 * steps + 3 * (steps - 1)
+    return lm + 3 * steps  # GRU step, rank GEMV, scorer
+
+
 def run_runner(args, rank, world, dev):
     """The drop-in DeLSGraphRunner (kernel/dels.py) at the released local-head shapes
     (V = 151936, E = 256, G = 1024, r = 256), batch B, 14 suffix steps: one call =
@@ -762,7 +772,7 @@ def run_runner(args, rank, world, dev):
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
                 "d2h_bytes_per_step": B * steps * 8},
-        "gpu_launches": (1 + 3 * steps - 1 + (1 if args.runner_hidden and not runner._fused else 0)) * args.steps,
+        "gpu_launches": runner_launches(runner, steps) * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
                      "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call,
                      "note": "Vr (77.8 MB) can stay L2-resident across the 14 steps, so this bound can be beaten"},
