@@ -861,7 +861,9 @@ def run_domino(args, rank, world, dev):
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
                 "d2h_bytes_per_step": B * steps * 8},
-        "gpu_launches": (2 + P + 3 * steps - 1) * args.steps,
+        # z GEMM + finalisation, the prefix GRU steps, per step the correction layer and the
+        # scorer, and a GRU update between steps unless the scorer's helper warps feed it
+        "gpu_launches": (2 + P + 2 * steps + (0 if runner._overlap else steps - 1)) * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
                      "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call},
         "clocks": clk,

@@ -631,6 +631,43 @@ def gru_rank_gemv(
     return s_scaled
 
 
+def gru_correction_mid(
+    tokens: torch.Tensor,
+    gi_table: torch.Tensor,
+    gh: torch.Tensor,
+    h_in: torch.Tensor | None,
+    h_out: torch.Tensor,
+    w_s: torch.Tensor,
+    z: torch.Tensor,
+    alpha: torch.Tensor,
+    s_scaled: torch.Tensor,
+    *,
+    keys: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """One small-batch Domino step: h_out = GRU gates(gi_table[tokens], gh, h_in), then
+    s_scaled = bf16(alpha[0] * SiLU(z + bf16(w_s . h_out))) in the same launch."""
+    _require_cuda("tokens", tokens, torch.int64)
+    for name, t in (("gi_table", gi_table), ("gh", gh), ("h_out", h_out), ("w_s", w_s), ("z", z)):
+        _require_cuda(name, t, torch.bfloat16, 2)
+    B, G = h_out.shape
+    V = gi_table.shape[0]
+    M = w_s.shape[0]
+    if gh.shape != (B, 3 * G) or gh.stride(1) != 1 or gi_table.shape[1] != 3 * G or not h_out.is_contiguous():
+        raise ValueError("GRU gate operands do not match the hidden size")
+    if h_in is not None and (h_in.shape != (B, G) or not h_in.is_contiguous()):
+        raise ValueError("h_in must be a contiguous [B, G] tensor")
+    if w_s.shape[1] != G or z.shape != (B, M) or z.stride(1) != 1 or s_scaled.shape != (B, M) \
+            or not s_scaled.is_contiguous():
+        raise ValueError("correction MLP shapes do not match")
+    tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
+    _lib.call("dels_gru_correction_mid_bf16", _ptr(tokens), tok_stride, _ptr(gi_table),
+              _row_major("gi_table", gi_table), _ptr(gh), gh.stride(0), _ptr(h_in), _ptr(h_out), B, G, V, _ptr(w_s),
+              _row_major("w_s", w_s), _ptr(z), _row_major("z", z), M, _ptr(_f32_vec("alpha", alpha, h_out.device)),
+              _ptr(s_scaled), _ptr(keys), None if ws is None else ws.ptr, _stream(h_out.device))
+    return s_scaled
+
+
 def rank_gemv(
     x: torch.Tensor,
     w: torch.Tensor,

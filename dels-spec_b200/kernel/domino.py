@@ -164,10 +164,16 @@ class DraftCorrectionGraphRunner:
         if self._tc:
             self._tc_ws = ops.Workspace(max(ops.linear_workspace_bytes(B, G, 3 * G),
                                             ops.correction_mid_tc_workspace_bytes(B, G, M)), device)
-            self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
             if self.gru_b_hh is not None:
                 self._gh0.copy_(self.gru_b_hh[None, :].expand(B, -1))
+        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 4, at most 4; 0 turns it off) a step
+        # after the first is two kernels: the previous token's GRU gates fused into the
+        # correction layer (dels_gru_correction_mid_bf16), then the scorer, whose helper
+        # warps compute the next update's W_hh h (dels_fused_argmax_base_gru_bf16).
+        self._overlap = B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "4"))) and not self._tc
+        if self._tc or self._overlap:
+            self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
 
         ops.init(device)
         stream = torch.cuda.Stream(device=device)
@@ -201,17 +207,30 @@ class DraftCorrectionGraphRunner:
             h = self._gru(self.static_prefix_ids[:, p], h, self._h[cur])
             cur ^= 1
         for t in range(S):
-            if self._tc:
+            last = t + 1 == S
+            if self._overlap and t > 0:
+                # the previous token's GRU gates fused into this step's correction layer
+                h_prev, h = h, self._h[cur]
+                cur ^= 1
+                ops.gru_correction_mid(self._tokens[t - 1], self._gru_input_proj_table, self._gh, h_prev, h,
+                                       self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
+                                       ws=self._ws)
+            elif self._tc:
                 ops.correction_mid_tc(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
                                       ws=self._tc_ws)
             else:
                 ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
                                    ws=self._ws)
-            ops.fused_argmax_base_bf16(
-                self.static_base_logits[:, t, :], self._s_scaled, self.fc2_weight, self._prior_f32, self._beta,
-                n_pos=1, keys_ready=True, out=self._outs[t], ws=self._ws,
-            )
-            if t + 1 < S:
+            base_t = self.static_base_logits[:, t, :]
+            if self._overlap and not last:
+                # the scorer's helper warps compute the next update's gh = bf16(W_hh h + b_hh)
+                ops.fused_argmax_base_gru_bf16(base_t, self._s_scaled, self.fc2_weight, self._prior_f32,
+                                               self._beta, self.gru_w_hh, self.gru_b_hh, h, self._gh,
+                                               keys_ready=True, out=self._outs[t], ws=self._ws)
+            else:
+                ops.fused_argmax_base_bf16(base_t, self._s_scaled, self.fc2_weight, self._prior_f32, self._beta,
+                                           n_pos=1, keys_ready=True, out=self._outs[t], ws=self._ws)
+            if not last and not self._overlap:
                 h = self._gru(self._tokens[t], h, self._h[cur])
                 cur ^= 1
         if S > 0:

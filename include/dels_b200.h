@@ -263,6 +263,17 @@ DELS_API int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, 
                                      int activation, const float* alpha, void* s_scaled, int64_t* keys, void* ws,
                                      void* stream);
 
+/* The same fusion for the Domino correction runner: the GRU gates of the previous token
+ * (code/kernel/domino.py:423-435) into the correction MLP's hidden layer of the next step
+ * (:402, :92-97),
+ * h_out as in dels_gru_rank_gemv_bf16, then s_scaled[b] = bf16(alpha[0] * SiLU(z[b] +
+ * bf16(w_s . h_out[b]))) and keys[0..B) reset as in dels_correction_mid_bf16. */
+DELS_API int dels_gru_correction_mid_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table,
+                                          int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in,
+                                          void* h_out, int B, int G, int V, const void* w_s, int64_t ld_ws,
+                                          const void* z, int64_t ld_z, int M, const float* alpha, void* s_scaled,
+                                          int64_t* keys, void* ws, void* stream);
+
 /* Markov rank state (code/kernel/markov_dels.py:288):
  *   s_scaled[b] = bf16(alpha_p * emb[tokens[b * tok_stride]]),  emb [V, r] bf16,
  * keys[0..B) reset.  Out-of-range ids are clamped and flagged as above. */
