@@ -57,6 +57,11 @@ def test_pure_host_entry_points(lib):
     assert _lib.query("dels_score_workspace_bytes", 512, 4096, 256) > 512 * 256 * 2
     assert _lib.query("dels_rank_workspace_bytes", 0, 1, 1) == _lib.DELS_WS_HEADER_BYTES
     assert _lib.query("dels_rnn_workspace_bytes", 512, 16, 4096, 256) >= 8192 * 256 * 4
+    # vocabulary-sized F.linear: the GEMM writes bf16 itself, no split-K partials
+    assert _lib.query("dels_linear_workspace_bytes", 14, 4096, 151936) == _lib.DELS_WS_HEADER_BYTES
+    # the correction layer always finalises from partials, even when K is a single block
+    assert _lib.query("dels_correction_mid_tc_workspace_bytes", 40, 64, 48) >= \
+        _lib.DELS_WS_HEADER_BYTES + 40 * 48 * 4
 
 
 def test_argument_errors_are_reported_before_device_work(lib):
@@ -82,6 +87,23 @@ def test_argument_errors_are_reported_before_device_work(lib):
     # commit_extra outside {0, 1}
     with pytest.raises(_lib.DelsArgumentError):
         _lib.call("dels_accept_offsets", None, 0, None, 0, 1, 1, 2, None, None, None)
+    # the fused GRU-gate entry points check their operands before any device work
+    with pytest.raises(_lib.DelsArgumentError) as ei:
+        _lib.call("dels_gru_rank_gemv_bf16", None, 1, None, 3072, None, 3072, None, None, 1, 1024, 100, None, 1024,
+                  None, 256, 0, None, None, None, None, None)
+    assert ei.value.status == _lib.DELS_ERR_INVALID_ARG
+    with pytest.raises(_lib.DelsArgumentError) as ei:
+        _lib.call("dels_gru_correction_mid_bf16", ctypes.c_void_p(addr), 1, ctypes.c_void_p(addr), 3072,
+                  ctypes.c_void_p(addr), 3072, None, ctypes.c_void_p(addr), 1, 1024, 100, None, 1024,
+                  ctypes.c_void_p(addr), 1024, 1024, None, None, None, None, None)
+    assert ei.value.status == _lib.DELS_ERR_ALIGNMENT
+    # the scorer with the next GRU projection takes at most 4 rows
+    ok = (ctypes.c_char * 256)()
+    p = ctypes.c_void_p((ctypes.addressof(ok) + 15) & ~15)
+    with pytest.raises(_lib.DelsError) as ei:
+        _lib.call("dels_fused_argmax_base_gru_bf16", p, 1000, p, 64, p, 64, None, None, 1, 5, 64, 1000, 0, None,
+                  None, p, 256, p, None, p, 1024, p, None)
+    assert ei.value.status == _lib.DELS_ERR_UNSUPPORTED
     # fp32 scorer needs H % 4 == 0
     with pytest.raises(_lib.DelsError):
         _lib.call("dels_draft_score_f32", None, 0, None, 0, None, 0, None, 0, None, None, None, 1, None, 1, 6, 4, 10,
