@@ -64,6 +64,33 @@ def test_pure_host_entry_points(lib):
         _lib.DELS_WS_HEADER_BYTES + 40 * 48 * 4
 
 
+def test_plain_c_host_links_and_calls(lib, tmp_path):
+    """The header is C99 and a C program links against the library directly (no Python,
+    no torch): the boundary a cgo / JNI / N-API binding would wrap."""
+    import shutil
+
+    from dels_b200 import _lib
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "host.c"
+    src.write_text(
+        "#include <stdio.h>\n#include \"dels_b200.h\"\n"
+        "int main(void) {\n"
+        "  if (dels_version() != 1) return 2;\n"
+        "  if (dels_linear_workspace_bytes(14, 4096, 151936) != DELS_WS_HEADER_BYTES) return 3;\n"
+        "  if (dels_rank_workspace_bytes(0, 1, 1) != DELS_WS_HEADER_BYTES) return 4;\n"
+        "  puts(dels_status_string(DELS_ERR_WORKSPACE));\n"
+        "  return 0;\n}\n")
+    libdir = _lib.LIB_PATH.parent
+    exe = tmp_path / "host"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", str(HEADER.parent), str(src), "-L", str(libdir),
+                    "-ldels_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    assert out.strip() == "workspace missing or too small"
+
+
 def test_argument_errors_are_reported_before_device_work(lib):
     from dels_b200 import _lib
 
