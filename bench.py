@@ -889,16 +889,20 @@ def run_domino(args, rank, world, dev):
 
 
 # ----------------------------------------------------------------------------- reference arm
-def run_reference(args, dev):
-    """The reference's CPU formula on the host cores, same workload / metric / unit."""
+def run_reference(args, dev, world: int = 1):
+    """The reference's CPU formula on the host cores, same workload / metric / unit / config
+    as our arm at the same N (rank 0 alone runs it)."""
     from dels_b200 import workloads
 
-    wname = args.workload if args.workload != "auto" else "cfg2"
+    wname = args.workload if args.workload != "auto" else ("cfg2" if world == 1 else "cfg5")
     gen = {"cfg1": workloads.cfg1, "cfg2": workloads.cfg2, "cfg5": workloads.cfg5}.get(wname, workloads.cfg2)
     gdev = dev if torch.cuda.is_available() else "cpu"
     wl = gen(device=gdev)
     nrows = 16 if wl.dtype == torch.float32 else 24
     h, W, w_rank, Vr, prior, a, b = cpu_sample(wl, nrows)
+    config = {"workload": wl.name, "rows": wl.rows, "H": wl.H, "r": wl.r, "V": wl.V,
+              "parallelism": "host cores of rank 0", "rows_per_step_sample": nrows}
+    dtype = "f32" if wl.dtype == torch.float32 else "bf16"
     del wl
     torch.cuda.empty_cache() if torch.cuda.is_available() else None
     rates = []
@@ -909,10 +913,11 @@ def run_reference(args, dev):
             rates.append(rps)
     rps = len(rates) / sum(1.0 / x for x in rates)
     return {
-        "metric": METRIC, "value": rps, "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": nrows / rps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": str(h.dtype).replace("torch.", ""), "data": "synthetic (seeded)",
-        "config": {"workload": wname, "rows_per_step_sample": nrows},
+        "metric": METRIC, "value": rps, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": nrows / rps * 1e3, "higher_is_better": True,
+        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic (seeded)",
+        "config": config,
         "impl": "reference",
         "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
                          "sample": f"{nrows} rows x full vocabulary per step, torch on the host"},
@@ -939,7 +944,7 @@ def main():
         if rank != 0:
             return
         dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
-        print(json.dumps(run_reference(args, dev)), flush=True)
+        print(json.dumps(run_reference(args, dev, world)), flush=True)
         return
 
     dev = torch.device("cuda", local)
