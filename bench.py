@@ -345,18 +345,55 @@ def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None
 
 
 # ----------------------------------------------------------------------------- CPU reference
-def reference_rows_per_s(h, W, w_rank, Vr, prior, alpha_rows, beta_rows, reps: int) -> tuple[float, int]:
-    """Time the reference formula (torch on the host) on the given rows; returns rows/s."""
-    from oracle.reference_torch import score_rows
+def reference_rows_per_s(h, W, w_rank, Vr, prior, alpha_rows, beta_rows, reps: int, rnn=None) -> tuple[float, int]:
+    """Time the reference formula (torch on the host) on the given rows; returns rows/s.
+    rnn = (w_in, w_s, bias, T): the rank states come from the RNN head's recurrence."""
+    from oracle.reference_torch import rnn_rank_states, score_rows
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    score_rows(h[:1], W, w_rank, Vr, prior, alpha_rows[:1], beta_rows[:1])  # warm caches
+
+    def once(n):
+        state = None if rnn is None else rnn_rank_states(h[:n], *rnn)
+        score_rows(h[:n], W, w_rank, Vr, prior, alpha_rows[:n], beta_rows[:n], rank_state=state)
+
+    once(rnn[3] if rnn is not None else 1)  # warm caches
     t0 = time.perf_counter()
     for _ in range(reps):
-        score_rows(h, W, w_rank, Vr, prior, alpha_rows, beta_rows)
+        once(h.shape[0])
     dt = time.perf_counter() - t0
     return h.shape[0] * reps / dt, torch.get_num_threads()
+
+
+def ragged_sample(wl, rows: int):
+    """cfg3 on the host: acceptance as code/dflash.py:645-651 computes it, then the first
+    `rows` accepted rows (draft position j of sequence b for j < accept[b]) with their
+    positions' schedules."""
+    t = wl.tensors
+    draft, target = t["draft"].cpu(), t["target"].cpu()
+    P = draft.shape[1]
+    accept = (draft == target[:, :P]).to(torch.int64).cumprod(1).sum(1)
+    seqs, pos = [], []
+    for b in range(draft.shape[0]):
+        for j in range(int(accept[b])):
+            if len(pos) < rows:
+                seqs.append(b)
+                pos.append(j)
+    h = t["hidden"][torch.tensor(seqs, device=t["hidden"].device), torch.tensor(pos, device=t["hidden"].device)]
+    a = torch.tensor(wl.alpha, dtype=torch.float64)[pos]
+    b = torch.tensor(wl.beta, dtype=torch.float64)[pos]
+    return h.cpu(), t["W"].cpu(), t["w_rank"].cpu(), t["Vr"].cpu(), t["prior"].cpu(), a, b
+
+
+def rnn_sample(wl, n_seq: int):
+    """cfg4 on the host: the rows of the first n_seq sequences and the RNN head's weights."""
+    t = wl.tensors
+    T = wl.n_pos
+    pos = torch.arange(n_seq * T) % T
+    a = torch.tensor(wl.alpha, dtype=torch.float64)[pos]
+    b = torch.tensor(wl.beta, dtype=torch.float64)[pos]
+    rnn = (t["w_in"].cpu(), t["w_s"].cpu(), t["bias"].cpu(), T)
+    return (t["x"][: n_seq * T].cpu(), t["W"].cpu(), None, t["Vr"].cpu(), t["prior"].cpu(), a, b), rnn
 
 
 def cpu_sample(wl, rows: int):
@@ -688,19 +725,18 @@ def runner_launches(runner, steps: int) -> int:
     return lm + 3 * steps  # GRU step, rank GEMV, scorer
 
 
-def run_runner(args, rank, world, dev):
-    """The drop-in DeLSGraphRunner (kernel/dels.py) at the released local-head shapes
-    (V = 151936, E = 256, G = 1024, r = 256), batch B, 14 suffix steps: one call =
-    copy-in of prefix ids and base logits, CUDA-graph replay, clone of the tokens —
-    exactly the reference runner's __call__ (code/kernel/dels.py:469-478)."""
+def runner_inputs(args, dev):
+    """The runner workload's seeded local head (released shapes V = 151936, E = 256,
+    G = 1024, r = 256), schedules and call inputs, built with torch alone (shared by both
+    arms): base logits [B, 14, V], or with --runner-hidden the target LM head W [V, 4096]
+    and the draft hidden states [B, 14, 4096]."""
+    import types
+
     import torch.nn as nn
 
     import dels as D
-    from kernel.dels import DeLSGraphRunner
     from dels_b200 import workloads
 
-    if world > 1:
-        raise SystemExit("the runner workload is single-GPU")
     V, E, G, r, steps, B = workloads.VOCAB, 256, 1024, 256, 14, args.runner_batch
     g = torch.Generator(device=dev)
     g.manual_seed(5)
@@ -714,25 +750,67 @@ def run_runner(args, rank, world, dev):
                        (head.prefix_gru.weight_hh_l0, 0.03), (head.rank_proj.weight, 0.05),
                        (head.low_rank_lm_head.weight, 0.05)):
             p.copy_(torch.randn(p.shape, generator=g, device=dev) * std)
-    prior = workloads.zipf_log_prior(V, device=dev).to(torch.bfloat16)
-    alpha = workloads.linspace(0.9, 0.3, steps)
-    beta = workloads.linspace(0.3, 0.1, steps)
+    inp = types.SimpleNamespace(V=V, E=E, G=G, r=r, steps=steps, B=B, H=4096, head=head, W=None, x=None, base=None)
+    inp.prior = workloads.zipf_log_prior(V, device=dev).to(torch.bfloat16)
+    inp.alpha = workloads.linspace(0.9, 0.3, steps)
+    inp.beta = workloads.linspace(0.3, 0.1, steps)
+    inp.prefix = torch.randint(0, V, (B, 1), generator=g, device=dev)
+    if args.runner_hidden:
+        inp.W = (torch.randn(V, inp.H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        inp.x = torch.randn(B, steps, inp.H, generator=g, device=dev).to(torch.bfloat16)
+        inp.name = f"runner_hidden_b{B}_steps{steps}"
+    else:
+        inp.base = (torch.randn(B, steps, V, generator=g, device=dev)).to(torch.bfloat16)
+        inp.name = f"runner_b{B}_steps{steps}"
+    return inp
+
+
+def runner_cpu_rate(inp, reps: int = 2) -> tuple[float, int, str]:
+    """The reference's torch rollout (oracle/reference_torch.runner_rollout) of the first
+    sequence on the host cores; returns (rows/s, threads, sample)."""
+    from oracle.reference_torch import runner_rollout
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    head = inp.head
+    table = torch.nn.functional.linear(head.embed_tokens.weight, head.prefix_gru.weight_ih_l0).cpu()
+    base1 = (torch.nn.functional.linear(inp.x[:1], inp.W) if inp.x is not None else inp.base[:1]).cpu()
+    cpu_args = (inp.prefix[:1].cpu(), base1, table, head.prefix_gru.weight_hh_l0.detach().cpu(),
+                head.rank_proj.weight.detach().cpu(), head.low_rank_lm_head.weight.detach().cpu(), inp.prior.cpu(),
+                inp.alpha, inp.beta)
+    runner_rollout(*cpu_args)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        runner_rollout(*cpu_args)
+    dt = (time.perf_counter() - t0) / reps
+    return inp.steps / dt, torch.get_num_threads(), \
+        f"one batch-1 rollout of {inp.steps} steps x {reps} repetitions, bf16 torch on the host"
+
+
+def run_runner(args, rank, world, dev):
+    """The drop-in DeLSGraphRunner (kernel/dels.py) at the released local-head shapes
+    (V = 151936, E = 256, G = 1024, r = 256), batch B, 14 suffix steps: one call =
+    copy-in of prefix ids and base logits, CUDA-graph replay, clone of the tokens —
+    exactly the reference runner's __call__ (code/kernel/dels.py:469-478)."""
+    from kernel.dels import DeLSGraphRunner
+
+    if world > 1:
+        raise SystemExit("the runner workload is single-GPU")
+    inp = runner_inputs(args, dev)
+    V, E, G, r, steps, B = inp.V, inp.E, inp.G, inp.r, inp.steps, inp.B
+    head, prior, alpha, beta, prefix = inp.head, inp.prior, inp.alpha, inp.beta, inp.prefix
     kw = dict(local_head=head, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha, beta_values=beta,
               baseline_logits=prior, device=dev)
-    prefix = torch.randint(0, V, (B, 1), generator=g, device=dev)
     stream = torch.cuda.current_stream(dev)
     per_step = (r * V + 3 * G * G + r * G + B * V + B * 3 * G) * 2  # Vr, W_hh, W_rank, base row, table rows
     extra = {}
+    name = inp.name
     if args.runner_hidden:
         # DeLSFusedGraphRunner: the call takes the draft hidden states [B, steps, H] and the
         # runner owns the target LM head (Qwen3-8B shape, H = 4096)
         from kernel.dels import DeLSFusedGraphRunner
 
-        H = 4096
-        W = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        H, W, x = inp.H, inp.W, inp.x
         runner = DeLSFusedGraphRunner(target_lm_head_weight=W, **kw)
-        x = torch.randn(B, steps, H, generator=g, device=dev).to(torch.bfloat16)
-        name = f"runner_hidden_b{B}_steps{steps}"
         if runner._fused:  # W streamed by every step's scorer
             bytes_call = steps * (per_step - B * V * 2 + V * H * 2 + B * H * 2)
         else:  # one GEMM over all rows writes the logits, the steps read them back
@@ -748,10 +826,8 @@ def run_runner(args, rank, world, dev):
         inputs = [prefix, x]
     else:
         runner = DeLSGraphRunner(**kw)
-        base = (torch.randn(B, steps, V, generator=g, device=dev)).to(torch.bfloat16)
-        name = f"runner_b{B}_steps{steps}"
         bytes_call = steps * per_step + B * steps * V * 2 * 2  # + copy-in of the base logits (read + write)
-        inputs = [prefix, base]
+        inputs = [prefix, inp.base]
     call = lambda: runner(*inputs)  # noqa: E731
     clocks = ClockSampler(dev)
     ms = timed(call, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
@@ -779,39 +855,21 @@ def run_runner(args, rank, world, dev):
         "clocks": clk,
     }
     if not args.no_cpu_baseline:
-        from oracle.reference_torch import runner_rollout
-
-        torch.set_num_threads(os.cpu_count() or 1)
-        table = torch.nn.functional.linear(head.embed_tokens.weight, head.prefix_gru.weight_ih_l0).cpu()
-        base1 = (torch.nn.functional.linear(x[:1], W) if args.runner_hidden else base[:1]).cpu()
-        cpu_args = (prefix[:1].cpu(), base1, table, head.prefix_gru.weight_hh_l0.detach().cpu(),
-                    head.rank_proj.weight.detach().cpu(), head.low_rank_lm_head.weight.detach().cpu(), prior.cpu(),
-                    alpha, beta)
-        runner_rollout(*cpu_args)
-        t0 = time.perf_counter()
-        reps = 2
-        for _ in range(reps):
-            runner_rollout(*cpu_args)
-        dt = (time.perf_counter() - t0) / reps
-        res["cpu_baseline"] = {"value": steps / dt, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
-                               "sample": "one batch-1 rollout of 14 steps x 2 repetitions, bf16 torch on the host"}
+        rps, cores, sample = runner_cpu_rate(inp)
+        res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample}
     return res
 
 
-def run_domino(args, rank, world, dev):
-    """The drop-in Domino DraftCorrectionGraphRunner (kernel/domino.py) at Qwen3-8B target
-    shapes (V = 151936, H = 4096) with GRU and correction-MLP widths G = M = 1024 (the
-    reference fixes no released width), batch B, 14 suffix steps, 2 prefix tokens: one call
-    = copy-in of prefix ids, draft hiddens and base logits, graph replay, clone of the tokens
-    (code/kernel/domino.py:499-520)."""
+def domino_inputs(args, dev):
+    """The Domino workload's seeded draft model (GRU and correction MLP, G = M = 1024),
+    target embedding and call inputs, built with torch alone (shared by both arms)."""
+    import types
+
     import torch.nn as nn
 
-    from kernel.domino import DraftCorrectionGraphRunner
     from dels_b200 import workloads
 
-    if world > 1:
-        raise SystemExit("the domino workload is single-GPU")
-    V, H, G, M, steps, P, B, alpha = workloads.VOCAB, 4096, 1024, 1024, 14, 2, args.runner_batch, 1.0
+    V, H, G, M, steps, P, B = workloads.VOCAB, 4096, 1024, 1024, 14, 2, args.runner_batch
     g = torch.Generator(device=dev)
     g.manual_seed(6)
 
@@ -830,12 +888,52 @@ def run_domino(args, rank, world, dev):
     stub.model.embed_tokens = nn.Embedding(V, H).to(device=dev, dtype=torch.bfloat16)
     with torch.no_grad():
         stub.model.embed_tokens.weight.copy_(torch.randn(V, H, generator=g, device=dev) * 0.02)
+    inp = types.SimpleNamespace(V=V, H=H, G=G, M=M, steps=steps, P=P, B=B, alpha=1.0, draft=draft, target=stub,
+                                name=f"domino_b{B}_steps{steps}")
+    inp.hiddens = torch.randn(B, steps, H, generator=g, device=dev).to(torch.bfloat16)
+    inp.base = torch.randn(B, steps, V, generator=g, device=dev).to(torch.bfloat16)
+    inp.prefix = torch.randint(0, V, (B, P), generator=g, device=dev)
+    return inp
+
+
+def domino_cpu_rate(inp, reps: int = 2) -> tuple[float, int, str]:
+    """The reference runner's torch path (oracle/reference_torch.domino_rollout) for the
+    first sequence on the host cores; returns (rows/s, threads, sample)."""
+    from oracle.reference_torch import domino_rollout
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu = lambda t: t.detach().cpu()  # noqa: E731
+    draft, H = inp.draft, inp.H
+    w1 = cpu(draft.embed_proj[0].weight)
+    table = torch.nn.functional.linear(inp.target.model.embed_tokens.weight, draft.prefix_gru.weight_ih_l0).cpu()
+    cpu_args = (inp.prefix[:1].cpu(), inp.hiddens[:1].cpu(), inp.base[:1].cpu(), table,
+                cpu(draft.prefix_gru.weight_hh_l0), w1[:, :H].contiguous(), w1[:, H:].contiguous(),
+                cpu(draft.embed_proj[2].weight), inp.alpha)
+    domino_rollout(*cpu_args)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        domino_rollout(*cpu_args)
+    dt = (time.perf_counter() - t0) / reps
+    return inp.steps / dt, torch.get_num_threads(), \
+        f"one batch-1 rollout of {inp.steps} steps x {reps} repetitions, bf16 torch on the host"
+
+
+def run_domino(args, rank, world, dev):
+    """The drop-in Domino DraftCorrectionGraphRunner (kernel/domino.py) at Qwen3-8B target
+    shapes (V = 151936, H = 4096) with GRU and correction-MLP widths G = M = 1024 (the
+    reference fixes no released width), batch B, 14 suffix steps, 2 prefix tokens: one call
+    = copy-in of prefix ids, draft hiddens and base logits, graph replay, clone of the tokens
+    (code/kernel/domino.py:499-520)."""
+    from kernel.domino import DraftCorrectionGraphRunner
+
+    if world > 1:
+        raise SystemExit("the domino workload is single-GPU")
+    inp = domino_inputs(args, dev)
+    V, H, G, M, steps, P, B, alpha = inp.V, inp.H, inp.G, inp.M, inp.steps, inp.P, inp.B, inp.alpha
+    draft, stub, hiddens, base, prefix = inp.draft, inp.target, inp.hiddens, inp.base, inp.prefix
     runner = DraftCorrectionGraphRunner(draft_model=draft, target_model=stub, batch_size=B, steps=steps,
                                         hidden_dim=H, gru_hidden_dim=G, vocab_size=V, prefix_token_count=P,
                                         device=dev, guidance_alpha=alpha)
-    hiddens = torch.randn(B, steps, H, generator=g, device=dev).to(torch.bfloat16)
-    base = torch.randn(B, steps, V, generator=g, device=dev).to(torch.bfloat16)
-    prefix = torch.randint(0, V, (B, P), generator=g, device=dev)
     stream = torch.cuda.current_stream(dev)
     call = lambda: runner(prefix, hiddens, base)  # noqa: E731
     clocks = ClockSampler(dev)
@@ -869,48 +967,58 @@ def run_domino(args, rank, world, dev):
         "clocks": clk,
     }
     if not args.no_cpu_baseline:
-        from oracle.reference_torch import domino_rollout
-
-        torch.set_num_threads(os.cpu_count() or 1)
-        cpu = lambda t: t.detach().cpu()  # noqa: E731
-        w1 = cpu(draft.embed_proj[0].weight)
-        table = torch.nn.functional.linear(stub.model.embed_tokens.weight, draft.prefix_gru.weight_ih_l0).cpu()
-        cpu_args = (prefix[:1].cpu(), hiddens[:1].cpu(), base[:1].cpu(), table, cpu(draft.prefix_gru.weight_hh_l0),
-                    w1[:, :H].contiguous(), w1[:, H:].contiguous(), cpu(draft.embed_proj[2].weight), alpha)
-        domino_rollout(*cpu_args)
-        t0 = time.perf_counter()
-        reps = 2
-        for _ in range(reps):
-            domino_rollout(*cpu_args)
-        dt = (time.perf_counter() - t0) / reps
-        res["cpu_baseline"] = {"value": steps / dt, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
-                               "sample": "one batch-1 rollout of 14 steps x 2 repetitions, bf16 torch on the host"}
+        rps, cores, sample = domino_cpu_rate(inp)
+        res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample}
     return res
 
 
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, dev, world: int = 1):
     """The reference's CPU formula on the host cores, same workload / metric / unit / config
-    as our arm at the same N (rank 0 alone runs it)."""
+    as our arm at the same N (rank 0 alone runs it).  Each step is a bounded sample: a few
+    dozen rows of the dense workloads (cfg3: accepted rows after the acceptance step; cfg4:
+    whole sequences through the RNN head), or one batch-1 rollout for the runners."""
     from dels_b200 import workloads
 
     wname = args.workload if args.workload != "auto" else ("cfg2" if world == 1 else "cfg5")
-    gen = {"cfg1": workloads.cfg1, "cfg2": workloads.cfg2, "cfg5": workloads.cfg5}.get(wname, workloads.cfg2)
-    gdev = dev if torch.cuda.is_available() else "cpu"
-    wl = gen(device=gdev)
-    nrows = 16 if wl.dtype == torch.float32 else 24
-    h, W, w_rank, Vr, prior, a, b = cpu_sample(wl, nrows)
-    config = {"workload": wl.name, "rows": wl.rows, "H": wl.H, "r": wl.r, "V": wl.V,
-              "parallelism": "host cores of rank 0", "rows_per_step_sample": nrows}
-    dtype = "f32" if wl.dtype == torch.float32 else "bf16"
-    del wl
-    torch.cuda.empty_cache() if torch.cuda.is_available() else None
-    rates = []
-    cores = 0
-    for i in range(args.warmup + args.steps):
-        rps, cores = reference_rows_per_s(h, W, w_rank, Vr, prior, a, b, reps=1)
-        if i >= args.warmup:
-            rates.append(rps)
+    gdev = dev if torch.cuda.is_available() else torch.device("cpu")
+    if wname in ("runner", "domino"):
+        inp = (runner_inputs if wname == "runner" else domino_inputs)(args, gdev)
+        rate = runner_cpu_rate if wname == "runner" else domino_cpu_rate
+        config = {"workload": inp.name, "V": inp.V, "G": inp.G, "parallelism": "host cores of rank 0",
+                  "rows_per_step_sample": inp.steps}
+        rates, cores, sample = [], 0, ""
+        for i in range(args.warmup + args.steps):
+            rps, cores, sample = rate(inp, reps=1)
+            if i >= args.warmup:
+                rates.append(rps)
+        nrows, dtype = inp.steps, "bf16"
+    else:
+        gen = {"cfg1": workloads.cfg1, "cfg2": workloads.cfg2, "cfg3": workloads.cfg3, "cfg4": workloads.cfg4,
+               "cfg5": workloads.cfg5}[wname]
+        wl = gen(device=gdev)
+        nrows = 16 if wl.dtype == torch.float32 else 24
+        rnn = None
+        if wname == "cfg3":
+            sample_t = ragged_sample(wl, nrows)
+            sample = f"the first {nrows} accepted rows x full vocabulary per step, torch on the host"
+        elif wname == "cfg4":
+            sample_t, rnn = rnn_sample(wl, 2)
+            nrows = sample_t[0].shape[0]
+            sample = "2 sequences x 16 positions through the RNN head x full vocabulary per step, torch on the host"
+        else:
+            sample_t = cpu_sample(wl, nrows)
+            sample = f"{nrows} rows x full vocabulary per step, torch on the host"
+        config = {"workload": wl.name, "rows": wl.rows, "H": wl.H, "r": wl.r, "V": wl.V,
+                  "parallelism": "host cores of rank 0", "rows_per_step_sample": nrows}
+        dtype = "f32" if wl.dtype == torch.float32 else "bf16"
+        del wl
+        torch.cuda.empty_cache() if torch.cuda.is_available() else None
+        rates, cores = [], 0
+        for i in range(args.warmup + args.steps):
+            rps, cores = reference_rows_per_s(*sample_t, reps=1, rnn=rnn)
+            if i >= args.warmup:
+                rates.append(rps)
     rps = len(rates) / sum(1.0 / x for x in rates)
     return {
         "metric": METRIC, "value": rps, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
@@ -919,8 +1027,7 @@ def run_reference(args, dev, world: int = 1):
         "dtype": dtype, "data": "synthetic (seeded)",
         "config": config,
         "impl": "reference",
-        "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
-                         "sample": f"{nrows} rows x full vocabulary per step, torch on the host"},
+        "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": rps, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

@@ -16,10 +16,12 @@ import torch.nn.functional as F
 
 
 @torch.inference_mode()
-def score_rows(h, W, w_rank, Vr, prior, alpha_rows, beta_rows) -> torch.Tensor:
-    """Token ids [rows] for rows whose draft positions carry alpha_rows / beta_rows."""
+def score_rows(h, W, w_rank, Vr, prior, alpha_rows, beta_rows, rank_state=None) -> torch.Tensor:
+    """Token ids [rows] for rows whose draft positions carry alpha_rows / beta_rows
+    (rank_state given: it replaces F.linear(h, w_rank))."""
     long_logits = F.linear(h, W)
-    rank_state = F.linear(h, w_rank)
+    if rank_state is None:
+        rank_state = F.linear(h, w_rank)
     short_logits = F.linear(rank_state, Vr)
     prior = None if prior is None else prior.to(long_logits.dtype).view(1, -1)
     out = torch.empty(h.shape[0], dtype=torch.long)
@@ -94,3 +96,19 @@ def domino_rollout(prefix_ids, hiddens, base_logits, table, w_hh, w_z, w_s, fc2,
         if t + 1 < steps:
             h = cell(table[tok], h)
     return out
+
+
+@torch.inference_mode()
+def rnn_rank_states(x, w_in, w_s, bias, T: int) -> torch.Tensor:
+    """Rank states of the input-projected RNN head for rows x [n_seq * T, H] in [seq, t]
+    order: s_t = tanh(W_in x_t + W_s s_(t-1) + b), s_0 = 0, in fp32, returned in x's dtype.
+    The reference has no such head (only the GRU form); this restates the workload's own
+    formula for the CPU baseline."""
+    n_seq = x.shape[0] // T
+    u = F.linear(x.float(), w_in.float()).view(n_seq, T, -1) + bias.float()
+    s = torch.zeros(n_seq, w_s.shape[0], dtype=torch.float32)
+    out = torch.empty_like(u)
+    for t in range(T):
+        s = torch.tanh(u[:, t] + F.linear(s, w_s.float()))
+        out[:, t] = s
+    return out.view(n_seq * T, -1).to(x.dtype)
