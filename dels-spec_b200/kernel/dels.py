@@ -156,10 +156,17 @@ class DeLSGraphRunner:
         # (dels_fused_argmax_base_gru_bf16).
         self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "3"))) and not self._tc
                          and self._scorer_computes_next_gh())
+        # The other batches of at most 4 rows (DELS_RUNNER_SPLIT_GRU=0 turns it off): the
+        # scorer's helper warps still compute the next W_hh h, and the step's GRU update
+        # shrinks to the gates (dels_gru_gates_bf16) before the rank GEMV, three kernels.
+        # Above 4 rows the helpers' work, which grows with the rows, outlasts the scorer.
+        self._split_gru = (not self._tc and not self._overlap and B <= 4
+                           and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0"
+                           and self._scorer_computes_next_gh())
         if self._tc:
             need = max(ops.linear_workspace_bytes(B, G, 3 * G), ops.rank_workspace_bytes(B, G, r))
             self._tc_ws = ops.Workspace(need, device)
-        if self._tc or self._overlap:
+        if self._tc or self._overlap or self._split_gru:
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
             # the first step's h is zero, so its gh is the bias alone
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
@@ -201,9 +208,13 @@ class DeLSGraphRunner:
         tokens, h_prev, gh, cur = self.static_prefix_ids[:, 0], None, self._gh0, 0
         for step in range(self.steps):
             h_new = self._h[cur]
-            ops.gru_rank_gemv(tokens, self._gru_input_proj_table, gh, h_prev, h_new, self.rank_weight,
-                              self._alpha[step : step + 1], self._s_scaled, bias=self.rank_bias,
-                              activation=self._activation, keys=self._keys, ws=self._ws)
+            if self._overlap:
+                ops.gru_rank_gemv(tokens, self._gru_input_proj_table, gh, h_prev, h_new, self.rank_weight,
+                                  self._alpha[step : step + 1], self._s_scaled, bias=self.rank_bias,
+                                  activation=self._activation, keys=self._keys, ws=self._ws)
+            else:
+                ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_prev, h_new, ws=self._ws)
+                self._rank(h_new, step)
             if step + 1 < self.steps:
                 # the scorer's helper warps compute the next step's gh = bf16(W_hh h_new + b_hh)
                 self._score(step, next_gh=(h_new, self._gh))
@@ -213,7 +224,7 @@ class DeLSGraphRunner:
         self.static_out.copy_(self._tokens.t())
 
     def _forward_impl(self):
-        if self._overlap:
+        if self._overlap or self._split_gru:
             return self._forward_overlapped()
         prefix = self.static_prefix_ids[:, 0]
         h_cur = self._gru(prefix, None, self._h[0])

@@ -172,7 +172,11 @@ class DraftCorrectionGraphRunner:
         # correction layer (dels_gru_correction_mid_bf16), then the scorer, whose helper
         # warps compute the next update's W_hh h (dels_fused_argmax_base_gru_bf16).
         self._overlap = B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "3"))) and not self._tc
-        if self._tc or self._overlap:
+        # The other batches of at most 4 rows (DELS_RUNNER_SPLIT_GRU=0 turns it off): the same
+        # helper warps, with the GRU update reduced to its gates (dels_gru_gates_bf16).
+        self._split_gru = (not self._tc and not self._overlap and B <= 4
+                           and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0")
+        if self._tc or self._overlap or self._split_gru:
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
 
         ops.init(device)
@@ -206,6 +210,7 @@ class DraftCorrectionGraphRunner:
         for p in range(self.prefix_token_count):
             h = self._gru(self.static_prefix_ids[:, p], h, self._h[cur])
             cur ^= 1
+        gh_on_scorer = self._overlap or self._split_gru
         for t in range(S):
             last = t + 1 == S
             if self._overlap and t > 0:
@@ -215,6 +220,12 @@ class DraftCorrectionGraphRunner:
                 ops.gru_correction_mid(self._tokens[t - 1], self._gru_input_proj_table, self._gh, h_prev, h,
                                        self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
                                        ws=self._ws)
+            elif self._split_gru and t > 0:
+                h_prev, h = h, self._h[cur]
+                cur ^= 1
+                ops.gru_gates(self._tokens[t - 1], self._gru_input_proj_table, self._gh, h_prev, h, ws=self._ws)
+                ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
+                                   ws=self._ws)
             elif self._tc:
                 ops.correction_mid_tc(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
                                       ws=self._tc_ws)
@@ -222,7 +233,7 @@ class DraftCorrectionGraphRunner:
                 ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
                                    ws=self._ws)
             base_t = self.static_base_logits[:, t, :]
-            if self._overlap and not last:
+            if gh_on_scorer and not last:
                 # the scorer's helper warps compute the next update's gh = bf16(W_hh h + b_hh)
                 ops.fused_argmax_base_gru_bf16(base_t, self._s_scaled, self.fc2_weight, self._prior_f32,
                                                self._beta, self.gru_w_hh, self.gru_b_hh, h, self._gh,
@@ -230,7 +241,7 @@ class DraftCorrectionGraphRunner:
             else:
                 ops.fused_argmax_base_bf16(base_t, self._s_scaled, self.fc2_weight, self._prior_f32, self._beta,
                                            n_pos=1, keys_ready=True, out=self._outs[t], ws=self._ws)
-            if not last and not self._overlap:
+            if not last and not gh_on_scorer:
                 h = self._gru(self._tokens[t], h, self._h[cur])
                 cur ^= 1
         if S > 0:

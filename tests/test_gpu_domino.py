@@ -140,13 +140,15 @@ def test_correction_mid_tc_matches_oracle(cuda_device):
     assert (keys.cpu().numpy() == np.iinfo(np.int64).min).all()
 
 
-@pytest.mark.parametrize("overlap", ["1", "0"])
+@pytest.mark.parametrize("overlap", ["1", "split", "0"])
 def test_domino_runner_matches_reference_fixture(cuda_device, golden_dir, monkeypatch, overlap):
-    """Both small-batch schedules: the GRU gates fused into the correction layer with the
-    next W_hh h on the scorer's helper warps (default), and the GRU step kernel first."""
+    """The three small-batch schedules: the GRU gates fused into the correction layer or a
+    gates kernel before it, both with the next W_hh h on the scorer's helper warps, and the
+    GRU step kernel first."""
     from kernel.domino import DraftCorrectionGraphRunner
 
     monkeypatch.setenv("DELS_RUNNER_OVERLAP_ROWS", "4" if overlap == "1" else "0")
+    monkeypatch.setenv("DELS_RUNNER_SPLIT_GRU", "0" if overlap == "0" else "1")
     g = np.load(golden_dir / "domino.npz")
     total = 0
     for c in json.loads(str(g["meta"])):

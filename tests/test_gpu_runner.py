@@ -45,13 +45,15 @@ def _compare(ours, gaps, ref, thresh):
     return n
 
 
-@pytest.mark.parametrize("overlap", ["1", "0"])
+@pytest.mark.parametrize("overlap", ["1", "split", "0"])
 def test_dels_runner_matches_reference_fixture(cuda_device, golden_dir, monkeypatch, overlap):
-    """Both small-batch schedules: the GRU gates fused into the rank projection with W_hh h
-    beside the scorer (default), and the GRU step kernel before the rank GEMV."""
+    """The three small-batch schedules: the GRU gates fused into the rank projection or a
+    gates kernel before the rank GEMV, both with the next step's W_hh h on the scorer's
+    helper warps, and the GRU step kernel first."""
     from kernel.dels import DeLSGraphRunner
 
     monkeypatch.setenv("DELS_RUNNER_OVERLAP_ROWS", "64" if overlap == "1" else "0")
+    monkeypatch.setenv("DELS_RUNNER_SPLIT_GRU", "0" if overlap == "0" else "1")
     g = np.load(golden_dir / "runners.npz")
     total = 0
     for c in json.loads(str(g["meta"])):
@@ -152,7 +154,7 @@ def test_runner_full_vocab_b1(cuda_device):
     assert _compare(out.cpu().numpy(), gaps, toks, 1e-2) >= 3
 
 
-@pytest.mark.parametrize("B", [1, 3])
+@pytest.mark.parametrize("B", [1, 3, 4])
 def test_scorer_with_next_gru_projection(cuda_device, B):
     """dels_fused_argmax_base_gru_bf16: the same tokens as the plain base-logit scorer, and
     gh_out within one bf16 rounding of bf16(W_hh h + b_hh) (helper warps' fp32 sums)."""
@@ -185,7 +187,7 @@ def test_scorer_with_next_gru_projection(cuda_device, B):
     np.testing.assert_allclose(got, exact, rtol=2 ** -7, atol=1e-3)
 
 
-@pytest.mark.parametrize("B", [5, 20, 48, 64])
+@pytest.mark.parametrize("B", [4, 5, 20, 48, 64])
 def test_runner_batches(cuda_device, B):
     """Batch sizes past the fixtures': the plain (<= 4 rows) and staged skinny scorers (16- and
     32-column row tiles), the 128-row tile scorer (33..128 rows) and the GRU step's loop over
