@@ -4,19 +4,21 @@ Drop-in for ``kernel.dels.DeLSGraphRunner`` of the reference (code/kernel/dels.p
 same constructor keywords, same ``ValueError`` checks, same ``__call__(prefix_ids,
 base_logits) -> LongTensor[B, steps]`` returning a fresh tensor, same static buffers
 (``static_prefix_ids``, ``static_base_logits``, ``static_out``), warm-up on a side
-stream and capture into ``self.graph``.  At small batches each captured step is, in
+stream and capture into ``self.graph``.  At 1-3 rows each captured step is two
 ``libdels_b200.so`` kernels:
 
   1. the GRU gates of the previous token (input-table row, gh, h) fused into the rank
      projection + activation + alpha_step scaling, keys reset (``dels_gru_rank_gemv_bf16``);
   2. the fused scorer on tcgen05 tensor cores: base logits + low-rank logits - beta *
      prior, argmax with the lowest index on ties, written straight into the step's token
-     slot (``dels_fused_argmax_base_bf16``);
-  3. beside 2, on a side stream of the graph: the next step's gh = bf16(W_hh h + b_hh)
-     (``dels_rank_gemv_bf16``), which needs h but not the token.
+     slot, while two helper warps per CTA compute the next step's gh = bf16(W_hh h +
+     b_hh), which needs h but not the token (``dels_fused_argmax_base_gru_bf16``).
 
-From ``DELS_RUNNER_TC_ROWS`` rows up W_hh h and the rank projection run as tensor-core
-GEMMs instead (``dels_linear_bf16`` + ``dels_gru_gates_bf16``, ``dels_rank_project_bf16``).
+At 4 rows the gates run as their own kernel before the rank GEMV (``dels_gru_gates_bf16``,
+``dels_rank_gemv_bf16``), with the same scorer.  At 5-15 rows a step is the GRU step
+kernel (``dels_gru_step_bf16``), the rank GEMV and the scorer; from ``DELS_RUNNER_TC_ROWS``
+rows up W_hh h and the rank projection run as tensor-core GEMMs (``dels_linear_bf16`` +
+``dels_gru_gates_bf16``, ``dels_rank_project_bf16``).
 
 alpha / beta live in device arrays indexed by step, so one graph serves a schedule;
 the reference instead bakes them into the Triton kernels as constexprs (:404-409).
@@ -204,7 +206,7 @@ class DeLSGraphRunner:
                                   activation=self._activation, s_scaled=self._s_scaled, keys=self._keys,
                                   want_state=False, ws=self._tc_ws)
 
-    def _forward_overlapped(self):
+    def _forward_gh_on_scorer(self):
         tokens, h_prev, gh, cur = self.static_prefix_ids[:, 0], None, self._gh0, 0
         for step in range(self.steps):
             h_new = self._h[cur]
@@ -225,7 +227,7 @@ class DeLSGraphRunner:
 
     def _forward_impl(self):
         if self._overlap or self._split_gru:
-            return self._forward_overlapped()
+            return self._forward_gh_on_scorer()
         prefix = self.static_prefix_ids[:, 0]
         h_cur = self._gru(prefix, None, self._h[0])
         nxt = 1
