@@ -15,7 +15,7 @@ stream and capture into ``self.graph``.  At 1-3 rows each captured step is two
      b_hh), which needs h but not the token (``dels_fused_argmax_base_gru_bf16``).
 
 At 4 rows the gates run as their own kernel before the rank GEMV (``dels_gru_gates_bf16``,
-``dels_rank_gemv_bf16``), with the same scorer.  At 5-15 rows a step is the GRU step
+``dels_rank_gemv_bf16``), with the same scorer.  At 5-11 rows a step is the GRU step
 kernel (``dels_gru_step_bf16``), the rank GEMV and the scorer; from ``DELS_RUNNER_TC_ROWS``
 rows up W_hh h and the rank projection run as tensor-core GEMMs (``dels_linear_bf16`` +
 ``dels_gru_gates_bf16``, ``dels_rank_project_bf16``).
@@ -146,10 +146,10 @@ class DeLSGraphRunner:
         self._keys = torch.empty(B, dtype=torch.int64, device=device)
         self._ws = ops.Workspace(1 << 12, device)
         self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
-        # From DELS_RUNNER_TC_ROWS rows up (default 16) the GRU's W_hh product and the rank
+        # From DELS_RUNNER_TC_ROWS rows up (default 12) the GRU's W_hh product and the rank
         # projection run as tensor-core split-K GEMMs (then the gates / the rank
         # finalisation); below it one warp per weight row does each in a single launch.
-        tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
+        tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "12"))
         self._tc = B >= tc_rows and self.rank_bias is None
         # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 3, at most 4; 0 turns it off) a step is
         # two kernels: the GRU gates fused into the rank projection (dels_gru_rank_gemv_bf16),

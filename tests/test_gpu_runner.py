@@ -187,7 +187,7 @@ def test_scorer_with_next_gru_projection(cuda_device, B):
     np.testing.assert_allclose(got, exact, rtol=2 ** -7, atol=1e-3)
 
 
-@pytest.mark.parametrize("B", [4, 5, 20, 48, 64])
+@pytest.mark.parametrize("B", [4, 5, 12, 20, 48, 64])
 def test_runner_batches(cuda_device, B):
     """Batch sizes past the fixtures': the plain (<= 4 rows) and staged skinny scorers (16- and
     32-column row tiles), the 128-row tile scorer (33..128 rows) and the GRU step's loop over
