@@ -31,3 +31,23 @@ def test_reference_arm_line_on_the_host():
     assert d["e2e"] == {"value": d["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     if "metric" in BASELINE:
         assert d["metric"] == BASELINE["metric"]
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """Launched like the driver's N > 1 runs: rank 0 alone times the reference formula on
+    the sharded workload's config and prints one line; every rank exits 0."""
+    import socket
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    proc = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                           "--master-addr", "127.0.0.1", "--master-port", str(port), str(ROOT / "bench.py"),
+                           "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "3"],
+                          capture_output=True, text=True, timeout=900, cwd=ROOT)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [line for line in proc.stdout.splitlines() if line.startswith("{")]
+    assert len(lines) == 1, proc.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["scaling"] == "strong"
+    assert d["config"]["workload"] == "cfg5_vocab_sharded_16384" and d["value"] > 0
