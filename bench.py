@@ -141,6 +141,57 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
+def default_workload(world: int) -> str:
+    """cfg2 (512 rows, the headline) for a plain single-process run; the vocabulary-sharded
+    cfg5 (16384 rows) whenever the process was started by torch.distributed.run, N = 1
+    included, so that every point of a 1/2/4/8-GPU scaling run times the same workload."""
+    under_torchrun = "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+    return "cfg5" if (world > 1 or under_torchrun) else "cfg2"
+
+
+def dense_workload_for(wname: str, dev, v_slice=None):
+    """The seeded dense workload (cfg1 / cfg2 / cfg5), optionally one vocabulary slice."""
+    from dels_b200 import workloads
+
+    if v_slice is None:
+        return {"cfg1": workloads.cfg1, "cfg2": workloads.cfg2, "cfg5": workloads.cfg5}[wname](device=dev)
+    base = {"cfg2": dict(rows=512, alpha=workloads.linspace(0.5, 0.1, 16), beta=workloads.linspace(0.3, 0.0, 16),
+                         seed=1),
+            "cfg5": dict(rows=16384, alpha=[0.3], beta=[0.3], seed=4)}[wname]
+    name = {"cfg2": "cfg2_qwen3_8b_bf16_b32x16", "cfg5": "cfg5_vocab_sharded_16384"}[wname]
+    return workloads.dense_workload(name, H=4096, r=256, dtype=torch.bfloat16, device=dev, v_slice=v_slice, **base)
+
+
+# The config dict of each workload, built by one function that both arms call, so the
+# reference arm's line carries exactly our arm's config.
+def dense_config(name: str, rows: int, H: int, r: int, V: int, world: int, sharded: bool) -> dict:
+    from dels_b200 import workloads
+
+    v0, v1 = workloads.shard_range(V, world, 0) if sharded else (0, V)
+    return {"workload": name, "rows": rows, "H": H, "r": r, "V": V, "vocab_per_rank": v1 - v0,
+            "parallelism": f"vocab-shard x{world}" if sharded else "single",
+            "l2": "W alone is larger than L2 (streamed from HBM every step)"}
+
+
+def ragged_config(name: str, n_seq: int, P: int, accepted: int, H: int, r: int, V: int) -> dict:
+    return {"workload": name, "sequences": n_seq, "draft": P, "accepted_rows": accepted, "H": H, "r": r, "V": V,
+            "l2": "W alone is larger than L2"}
+
+
+def rnn_config(name: str, rows: int, H: int, r: int, V: int) -> dict:
+    return {"workload": name, "rows": rows, "H": H, "r": r, "V": V, "l2": "W alone is larger than L2"}
+
+
+def runner_config(inp) -> dict:
+    return {"workload": inp.name, "V": inp.V, "E": inp.E, "G": inp.G, "r": inp.r,
+            "note": "one step = one runner call (14 scored positions per sequence)"}
+
+
+def domino_config(inp) -> dict:
+    return {"workload": inp.name, "V": inp.V, "H": inp.H, "G": inp.G, "M": inp.M, "prefix_tokens": inp.P,
+            "note": "one step = one DraftCorrectionGraphRunner call (14 scored positions per sequence)"}
+
+
 class PipelinedE2E:
     """Serving-style end-to-end loop through the public API.
 
@@ -412,39 +463,43 @@ def run_ours(args, rank, world, dev):
 
     pk_tflops, pk_gbs, pk_src = peaks()
     stream = torch.cuda.current_stream(dev)
-    wname = args.workload if args.workload != "auto" else ("cfg2" if world == 1 else "cfg5")
-    sharded = world > 1
+    wname = args.workload if args.workload != "auto" else default_workload(world)
+    # cfg5 is the vocabulary-sharded configuration at every N (N = 1 included, so the
+    # points of a 1 -> 8 curve run one code path); other dense workloads shard when N > 1
+    sharded = world > 1 or wname == "cfg5"
     if wname in ("cfg1", "cfg2", "cfg5"):
+        from dels_b200.sharded import VocabShardedScorer
+
         V = workloads.VOCAB
         v0, v1 = workloads.shard_range(V, world, rank) if sharded else (0, V)
-        gen = {"cfg1": workloads.cfg1, "cfg2": workloads.cfg2, "cfg5": workloads.cfg5}[wname]
-        wl = None if sharded else gen(device=dev)
-        if sharded:
-            base = {"cfg2": dict(rows=512, alpha=workloads.linspace(0.5, 0.1, 16), beta=workloads.linspace(0.3, 0.0, 16), seed=1),
-                    "cfg5": dict(rows=16384, alpha=[0.3], beta=[0.3], seed=4),
-                    "cfg1": None}[wname]
-            if base is None:
-                raise SystemExit("cfg1 (fp32, 16 rows) is single-GPU only")
-            wl = workloads.dense_workload(wname, H=4096, r=256, dtype=torch.bfloat16, device=dev, v_slice=(v0, v1),
-                                          **base)
+        if sharded and wname == "cfg1":
+            raise SystemExit("cfg1 (fp32, 16 rows) is single-GPU only")
+        wl = dense_workload_for(wname, dev, (v0, v1) if world > 1 else None)
         t = wl.tensors
         rows, H, r = wl.rows, wl.H, wl.r
         Vloc = t["W"].shape[0]
         fp32 = wl.dtype == torch.float32
-        out = ops.ScoreOut(tokens=torch.empty(rows, dtype=torch.int64, device=dev), scores=None,
-                           keys=torch.empty(rows, dtype=torch.int64, device=dev))
         need = ops._lib.query("dels_score_f32_workspace_bytes" if fp32 else "dels_score_workspace_bytes",
                               rows, H, r)
         ws = ops.Workspace(need, dev)
-        score = ops.draft_score_f32 if fp32 else ops.draft_score_bf16
+        if sharded:
+            scorer = VocabShardedScorer(t["W"], t["Vr"], t["prior"], t["w_rank"], t["alpha"], t["beta"], v_begin=v0,
+                                        n_pos=wl.n_pos, rows=rows, with_scores=False)
+            out = scorer.out
+            ws = scorer.ws
 
-        def step(h=t["h"]):
-            score(h, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
-                  v_begin=v0, keys_only=sharded, out=out, ws=ws)
-            if sharded:
-                torch.distributed.all_reduce(out.keys, op=torch.distributed.ReduceOp.MAX)
-                ops.keys_decode(out.keys, tokens=out.tokens, with_scores=False)
+            def step(h=t["h"]):
+                scorer(h)
+        else:
+            out = ops.ScoreOut(tokens=torch.empty(rows, dtype=torch.int64, device=dev), scores=None,
+                               keys=torch.empty(rows, dtype=torch.int64, device=dev))
+            score = ops.draft_score_f32 if fp32 else ops.draft_score_bf16
 
+            def step(h=t["h"]):
+                score(h, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
+                      out=out, ws=ws)
+
+        # projection + finalisation + scorer (fp32: transpose passes); sharded adds the decode
         launches_per_step = (3 if not fp32 else 2 + (rows + 15) // 16 + 1) + (1 if sharded else 0)
         flops_main = 2.0 * rows * Vloc * (H + r)
         bytes_main = (t["W"].numel() * t["W"].element_size() + t["Vr"].numel() * t["Vr"].element_size()
@@ -452,29 +507,27 @@ def run_ours(args, rank, world, dev):
         # With vocab sharding every rank needs all rows: each rank copies only its 1/N
         # slice from the host and an NCCL all-gather over NVLink rebuilds the batch, so
         # the box moves each input byte over PCIe once instead of N times.
-        gather = sharded and rows % world == 0
+        gather = world > 1 and rows % world == 0
         rows_in = rows // world if gather else rows
         h_host = t["h"][rank * rows_in:(rank + 1) * rows_in].cpu().pin_memory() if gather else t["h"].cpu().pin_memory()
         h_full = torch.empty_like(t["h"]) if gather else None
         bi, bo = h_host.numel() * h_host.element_size(), rows * 8
-        e2e_outs = [ops.ScoreOut(tokens=None, scores=None, keys=torch.empty(rows, dtype=torch.int64, device=dev))
-                    for _ in range(2)]
-        e2e_ws = [ops.Workspace(need, dev) for _ in range(2)]
 
-        def e2e_score(h_in, tokens, _slot=[0]):
-            o, w = e2e_outs[_slot[0]], e2e_ws[_slot[0]]
-            _slot[0] ^= 1
-            o.tokens = tokens
-            if gather:
-                torch.distributed.all_gather_into_tensor(h_full, h_in)
-                h_in = h_full
-            score(h_in, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
-                  v_begin=v0, keys_only=sharded, out=o, ws=w)
-            if sharded:
-                torch.distributed.all_reduce(o.keys, op=torch.distributed.ReduceOp.MAX)
-                ops.keys_decode(o.keys, tokens=tokens, with_scores=False)
+        if sharded:
+            e2e_outs = [scorer.new_out() for _ in range(2)]
+            e2e_ws = [scorer.new_workspace() for _ in range(2)]
 
-        if not sharded and not fp32:
+            def e2e_score(h_in, tokens, _slot=[0]):
+                o, w = e2e_outs[_slot[0]], e2e_ws[_slot[0]]
+                _slot[0] ^= 1
+                o.tokens = tokens
+                if gather:
+                    torch.distributed.all_gather_into_tensor(h_full, h_in)
+                    h_in = h_full
+                scorer(h_in, out=o, ws=w)
+
+            pipe = PipelinedE2E(h_host, e2e_score, rows, dev, stream)
+        elif not fp32:
             # projection and scorer as two public calls, so the cross-stream waits sit
             # between them (PipelinedE2ESplit)
             n_sl = PipelinedE2ESplit.SLOTS
@@ -495,6 +548,17 @@ def run_ours(args, rank, world, dev):
 
             pipe = PipelinedE2ESplit(h_host, e2e_project, e2e_scorer, rows, dev, stream)
         else:
+            e2e_outs = [ops.ScoreOut(tokens=None, scores=None, keys=torch.empty(rows, dtype=torch.int64, device=dev))
+                        for _ in range(2)]
+            e2e_ws = [ops.Workspace(need, dev) for _ in range(2)]
+
+            def e2e_score(h_in, tokens, _slot=[0]):
+                o, w = e2e_outs[_slot[0]], e2e_ws[_slot[0]]
+                _slot[0] ^= 1
+                o.tokens = tokens
+                score(h_in, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
+                      out=o, ws=w)
+
             pipe = PipelinedE2E(h_host, e2e_score, rows, dev, stream)
         e2e_note = ("per rank: this rank's 1/N row slice (all-gathered over NVLink)" if gather else
                     "per rank: all rows")
@@ -564,11 +628,7 @@ def run_ours(args, rank, world, dev):
         "vs_baseline": None,
         "dtype": "f32" if fp32 else "bf16",
         "data": "synthetic (seeded, shapes and distributions of the workload)",
-        "config": {
-            "workload": wl.name, "rows": rows, "H": H, "r": r, "V": workloads.VOCAB,
-            "vocab_per_rank": Vloc, "parallelism": f"vocab-shard x{world}" if sharded else "single",
-            "l2": "W alone is larger than L2 (streamed from HBM every step)",
-        },
+        "config": dense_config(wl.name, rows, H, r, workloads.VOCAB, world, sharded),
         "e2e": {"value": total_rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "note": e2e_note},
         "gpu_launches": launches_per_step * args.steps,
@@ -645,8 +705,7 @@ def run_ragged(args, rank, world, dev):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, shapes and distributions of the workload)",
-        "config": {"workload": wl.name, "sequences": n_seq, "draft": P, "accepted_rows": total, "H": wl.H, "r": wl.r,
-                   "V": wl.V, "l2": "W alone is larger than L2"},
+        "config": ragged_config(wl.name, n_seq, P, total, wl.H, wl.r, wl.V),
         "e2e": {"value": total * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in hh.values()),
                 "d2h_bytes_per_step": n_seq * P * 8 + n_seq * 4},
@@ -703,8 +762,7 @@ def run_rnn(args, rank, world, dev):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, shapes and distributions of the workload)",
-        "config": {"workload": wl.name, "rows": rows, "H": wl.H, "r": wl.r, "V": wl.V,
-                   "l2": "W alone is larger than L2"},
+        "config": rnn_config(wl.name, rows, wl.H, wl.r, wl.V),
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": rows * 8},
         "gpu_launches": 3 * args.steps,
@@ -805,7 +863,6 @@ def run_runner(args, rank, world, dev):
     stream = torch.cuda.current_stream(dev)
     per_step = (r * V + 3 * G * G + r * G + B * V + B * 3 * G) * 2  # Vr, W_hh, W_rank, base row, table rows
     extra = {}
-    name = inp.name
     if args.runner_hidden:
         # DeLSFusedGraphRunner: the call takes the draft hidden states [B, steps, H] and the
         # runner owns the target LM head (Qwen3-8B shape, H = 4096)
@@ -845,8 +902,7 @@ def run_runner(args, rank, world, dev):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, random-init local head at the released shapes)",
-        "config": {"workload": name, "V": V, "E": E, "G": G, "r": r,
-                   "note": "one step = one runner call (14 scored positions per sequence)", **extra},
+        "config": runner_config(inp),
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
                 "d2h_bytes_per_step": B * steps * 8},
@@ -856,6 +912,8 @@ def run_runner(args, rank, world, dev):
                      "note": "Vr (77.8 MB) can stay L2-resident across the 14 steps, so this bound can be beaten"},
         "clocks": clk,
     }
+    if extra:
+        res["runner_schedule"] = extra
     if not args.no_cpu_baseline:
         rps, cores, sample = runner_cpu_rate(inp)
         res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample}
@@ -956,8 +1014,7 @@ def run_domino(args, rank, world, dev):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, random-init Domino head; G = M = 1024 assumed)",
-        "config": {"workload": f"domino_b{B}_steps{steps}", "V": V, "H": H, "G": G, "M": M, "prefix_tokens": P,
-                   "note": "one step = one DraftCorrectionGraphRunner call (14 scored positions per sequence)"},
+        "config": domino_config(inp),
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
                 "d2h_bytes_per_step": B * steps * 8},
@@ -982,13 +1039,12 @@ def run_reference(args, dev, world: int = 1):
     whole sequences through the RNN head), or one batch-1 rollout for the runners."""
     from dels_b200 import workloads
 
-    wname = args.workload if args.workload != "auto" else ("cfg2" if world == 1 else "cfg5")
+    wname = args.workload if args.workload != "auto" else default_workload(world)
     gdev = dev if torch.cuda.is_available() else torch.device("cpu")
     if wname in ("runner", "domino"):
         inp = (runner_inputs if wname == "runner" else domino_inputs)(args, gdev)
         rate = runner_cpu_rate if wname == "runner" else domino_cpu_rate
-        config = {"workload": inp.name, "V": inp.V, "G": inp.G, "parallelism": "host cores of rank 0",
-                  "rows_per_step_sample": inp.steps}
+        config = (runner_config if wname == "runner" else domino_config)(inp)
         rates, cores, sample = [], 0, ""
         for i in range(args.warmup + args.steps):
             rps, cores, sample = rate(inp, reps=1)
@@ -1004,15 +1060,20 @@ def run_reference(args, dev, world: int = 1):
         if wname == "cfg3":
             sample_t = ragged_sample(wl, nrows)
             sample = f"the first {nrows} accepted rows x full vocabulary per step, torch on the host"
+            draft, target = wl.tensors["draft"].cpu(), wl.tensors["target"].cpu()
+            n_seq, P = draft.shape
+            accepted = int((draft == target[:, :P]).to(torch.int64).cumprod(1).sum())
+            config = ragged_config(wl.name, n_seq, P, accepted, wl.H, wl.r, wl.V)
         elif wname == "cfg4":
             sample_t, rnn = rnn_sample(wl, 2)
             nrows = sample_t[0].shape[0]
             sample = "2 sequences x 16 positions through the RNN head x full vocabulary per step, torch on the host"
+            config = rnn_config(wl.name, wl.rows, wl.H, wl.r, wl.V)
         else:
             sample_t = cpu_sample(wl, nrows)
             sample = f"{nrows} rows x full vocabulary per step, torch on the host"
-        config = {"workload": wl.name, "rows": wl.rows, "H": wl.H, "r": wl.r, "V": wl.V,
-                  "parallelism": "host cores of rank 0", "rows_per_step_sample": nrows}
+            config = dense_config(wl.name, wl.rows, wl.H, wl.r, wl.V, world, world > 1 or wname == "cfg5")
+        sample += f" (rank 0's host cores, {world} rank(s) launched)"
         dtype = "f32" if wl.dtype == torch.float32 else "bf16"
         del wl
         torch.cuda.empty_cache() if torch.cuda.is_available() else None
@@ -1025,7 +1086,7 @@ def run_reference(args, dev, world: int = 1):
     return {
         "metric": METRIC, "value": rps, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": nrows / rps * 1e3, "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
+        "scaling": "strong" if (world > 1 or wname == "cfg5") else "weak", "vs_baseline": None,
         "dtype": dtype, "data": "synthetic (seeded)",
         "config": config,
         "impl": "reference",

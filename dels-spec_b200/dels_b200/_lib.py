@@ -95,6 +95,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I,
         [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _I64, _I, _P, _P, _P, _P],
     ),
+    "dels_noalloc_status": (_I, [_P, _I, _P]),
+    "dels_selftest_bounded_wait_noalloc": (_I, [_P, ctypes.c_double, _P]),
 }
 
 

@@ -1281,43 +1281,42 @@ int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, cons
 // synchronisation at the worst moment.  dels_draft_score_bf16_noalloc serves those
 // callers: it runs exactly the dels_draft_score_bf16 kernels, with the scratch they
 // need (packed keys, the scaled rank state, the split-K partial sums, the completion
-// counter and the status word) placed in the fixed array below, which the module
-// reserves on every device that loads the library and keeps until the process exits.
+// counter and the status word) placed in the fixed array below.  The array is part of
+// the module image: it is reserved on every device on which the library's module is
+// loaded, whether or not the entry point is ever called, and kept until the process
+// exits.
 //
 // The array holds only the state of the call in flight: every call rewrites the keys,
 // the rank state and the partials, and its rank-projection finalisation zeroes the
-// completion counter before the scorer runs, so nothing carries over between calls.
-// Calls that can overlap on the device (different streams, or different host threads
-// without ordering) share the one array and race; serialise them.
+// completion counter before the scorer runs, so nothing carries over between calls
+// except the status word (bytes [4, 8)), which a kernel that gives up on a bounded wait
+// sets and which stays set until dels_noalloc_status clears it.  Calls that can overlap
+// on the device (different streams, or different host threads without ordering) share
+// the one array and race; serialise them.
 namespace {
 
 constexpr size_t kStaticScratchBytes = (size_t)DELS_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-struct StaticScratch {
-  void* ptr = nullptr;
-};
-StaticScratch g_static_scratch_dev[kMaxDevices];
-std::mutex g_static_scratch_mu;
-
-// Device address of g_static_scratch on the current device, looked up once per device
-// (the symbol's host-side name is not a device pointer and must never reach a kernel).
+// Device address of g_static_scratch in the current device's context.  The symbol's
+// host-side name is a stand-in, not a device pointer, and must never reach a kernel.
+// Looked up on every call (a host-side query, no stream work), so a context that was
+// torn down and created again never sees a stale address.
 int static_scratch_for_current_device(void** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(DELS_ERR_INVALID_ARG, "device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
-  if (g_static_scratch_dev[dev].ptr == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
-    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255u) != 0)
-      return fail(DELS_ERR_CUDA, "static scratch address is NULL or not 256-byte aligned");
-    g_static_scratch_dev[dev].ptr = p;
-  }
-  *out = g_static_scratch_dev[dev].ptr;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+  if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255u) != 0)
+    return fail(DELS_ERR_CUDA, "static scratch address is NULL or not 256-byte aligned");
+  *out = p;
   return DELS_OK;
+}
+
+// One thread: copy the status word out, and clear it when asked.
+__global__ void noalloc_status_kernel(int* word, int* out, int clear) {
+  const int v = *reinterpret_cast<volatile int*>(word);
+  if (out != nullptr) *out = v;
+  if (clear) atomicExch(word, 0);
 }
 
 }  // namespace
@@ -1342,6 +1341,25 @@ int dels_draft_score_bf16_noalloc(const void* h, int64_t ld_h, const void* W, in
   return dels_draft_score_bf16(h, ld_h, W, ld_w, w_rank, ld_wr, Vr, ld_vr, prior, alpha, beta, n_pos, row_pos, rows,
                                rows_dev, H, r, V, v_begin, activation, keys, idx_out, score_out, scratch,
                                kStaticScratchBytes, stream);
+}
+
+int dels_noalloc_status(int* status_out, int clear, void* stream) {
+  if (status_out == nullptr && !clear) return fail(DELS_ERR_INVALID_ARG, "nothing to do: status_out NULL, clear 0");
+  void* scratch = nullptr;
+  int rc = static_scratch_for_current_device(&scratch);
+  if (rc != DELS_OK) return rc;
+  int* word = reinterpret_cast<int*>(reinterpret_cast<char*>(scratch) + 4);
+  noalloc_status_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(word, status_out, clear ? 1 : 0);
+  DELS_CHECK_LAUNCH("noalloc_status_kernel launch");
+  return DELS_OK;
+}
+
+int dels_selftest_bounded_wait_noalloc(uint64_t* waited_ns, double limit_ms, void* stream) {
+  void* scratch = nullptr;
+  int rc = static_scratch_for_current_device(&scratch);
+  if (rc != DELS_OK) return rc;
+  return dels_selftest_bounded_wait(reinterpret_cast<int*>(reinterpret_cast<char*>(scratch) + 4), waited_ns,
+                                    limit_ms, stream);
 }
 
 }  // extern "C"

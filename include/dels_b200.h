@@ -324,14 +324,16 @@ DELS_API int dels_correction_mid_tc_bf16(const void* h, int64_t ld_h, const void
  * Allocation-free variant of dels_draft_score_bf16 (no counterpart in the reference).
  * For callers that cannot hand the library device memory — an FFI host without a
  * device allocator, or a serving engine whose memory pool already owns the device —
- * the scratch lives in a fixed array of DELS_NOALLOC_SCRATCH_BYTES that the library
- * reserves on each device it is loaded on, for the life of the process.  Same
+ * the scratch lives in a fixed array of DELS_NOALLOC_SCRATCH_BYTES that is part of the
+ * library's device module: it is reserved on every device on which that module is
+ * loaded, whether or not this entry point is called, until the process exits.  Same
  * arguments and results as dels_draft_score_bf16 without ws / ws_bytes; shapes whose
  * dels_score_workspace_bytes(rows, H, r) exceeds the array are rejected with
- * DELS_ERR_WORKSPACE (the Qwen3-8B block batch, 512 x 4096 x 256, fits).  The first
- * call on a device looks up the array's device address; make that first call before
- * any stream capture.  All calls share the one array: calls that may overlap on the
- * device race, so serialise them.  Never calls cudaMalloc / cudaFree.
+ * DELS_ERR_WORKSPACE (the Qwen3-8B block batch, 512 x 4096 x 256, fits).  Each call
+ * looks up the array's device address in the current context; the first call on a
+ * device may load the module, so make it before any stream capture.  All calls share
+ * the one array: calls that may overlap on the device race, so serialise them.  Never
+ * calls cudaMalloc / cudaFree.
  * --------------------------------------------------------------------------------- */
 #define DELS_NOALLOC_SCRATCH_BYTES (12u * 1024u * 1024u)
 DELS_API int dels_draft_score_bf16_noalloc(const void* h, int64_t ld_h, const void* W, int64_t ld_w,
@@ -340,6 +342,21 @@ DELS_API int dels_draft_score_bf16_noalloc(const void* h, int64_t ld_h, const vo
                                            const int32_t* row_pos, int rows, const int32_t* rows_dev, int H, int r,
                                            int V, int64_t v_begin, int activation, int64_t* keys, int64_t* idx_out,
                                            float* score_out, void* stream);
+
+/* Device status word of the allocation-free entry point (no counterpart in the
+ * reference): the counterpart of the workspace status word at bytes [4, 8) of a caller
+ * workspace.  A kernel of dels_draft_score_bf16_noalloc that gives up on a bounded wait
+ * stores DELS_ERR_DEVICE_TIMEOUT there, and the word stays set across calls until it
+ * is cleared.  Enqueues on `stream` one single-thread kernel that writes the word to
+ * *status_out (an int the GPU can write: device memory or mapped pinned host memory;
+ * NULL to only clear) and, when `clear` != 0, resets it to 0.  Read *status_out after
+ * the stream has reached this point. */
+DELS_API int dels_noalloc_status(int* status_out, int clear, void* stream);
+
+/* dels_selftest_bounded_wait with the allocation-free status word as its status: lets a
+ * caller (and the test suite) check that a device timeout there is seen and cleared by
+ * dels_noalloc_status.  No fault, trap or hang. */
+DELS_API int dels_selftest_bounded_wait_noalloc(uint64_t* waited_ns, double limit_ms, void* stream);
 
 #ifdef __cplusplus
 }

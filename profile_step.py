@@ -1,6 +1,9 @@
-"""Run a few launches of one kernel of the scoring path, for external profilers.
+"""Profiling entry: a few launches of one kernel of the scoring path, for ncu.
 
-    python dels-spec_b200/dels_b200/profile_step.py --workload cfg2 --kernel scorer --launches 4
+    python profile_step.py --workload cfg2 --kernel scorer --launches 4
+
+The ncu summaries under ``profiles/`` were captured with this script (their commands
+name it); ``bench.py`` is the timing entry, this one only launches.
 
 ``--kernel scorer`` launches the fused tcgen05 scorer, each call after a small
 keys-reset kernel (the scorer's epilogue skips chunks below the row's best key so far,
@@ -17,9 +20,10 @@ import argparse
 import sys
 from pathlib import Path
 
-PKG = Path(__file__).resolve().parent.parent
-if str(PKG) not in sys.path:
-    sys.path.insert(0, str(PKG))
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "dels-spec_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
 
 import torch  # noqa: E402
 

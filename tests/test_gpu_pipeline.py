@@ -223,3 +223,35 @@ def test_cfg3_full_size(cuda_device):
                                         want_state=False)
     ref = _torch_scores(packed[:total], t["W"], s_scaled, t["Vr"], t["prior"], t["beta"][row_pos[:total].long()])
     _check_full(out.tokens[:total], out.scores[:total], ref)
+
+
+def test_cfg5_full_size(cuda_device):
+    """The vocabulary-sharded configuration at full size on one GPU: 16384 rows over the
+    whole 151936-token vocabulary against the fp32 torch reference, then the 8 contiguous
+    vocabulary slices an 8-GPU run would own, each scored with global-index keys
+    (keys_only), whose element-wise maximum must decode to exactly the unsharded tokens
+    and scores (the NCCL all-reduce(MAX) computes that maximum across ranks)."""
+    from dels_b200 import ops, workloads
+
+    dev = cuda_device
+    wl = workloads.cfg5(device=dev)
+    t = wl.tensors
+    V = t["W"].shape[0]
+    out = ops.draft_score_bf16(t["h"], t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=1,
+                               with_scores=True)
+    _, s_scaled = ops.rank_project_bf16(t["h"], t["w_rank"], t["alpha"], n_pos=1, want_state=False)
+    ref = _torch_scores(t["h"], t["W"], s_scaled, t["Vr"], t["prior"], torch.full((wl.rows,), 0.3, device=dev))
+    frac = _check_full(out.tokens, out.scores, ref)
+    assert frac > 0.9
+    del ref
+    torch.cuda.empty_cache()
+    keys = None
+    for rank in range(8):
+        v0, v1 = workloads.shard_range(V, 8, rank)
+        part = ops.draft_score_bf16(t["h"], t["W"][v0:v1], t["w_rank"], t["Vr"][v0:v1], t["prior"][v0:v1],
+                                    t["alpha"], t["beta"], n_pos=1, v_begin=v0, keys_only=True)
+        keys = part.keys.clone() if keys is None else torch.maximum(keys, part.keys)
+    tok, sc = ops.keys_decode(keys)
+    assert torch.equal(keys, out.keys)
+    assert torch.equal(tok, out.tokens)
+    assert torch.equal(sc, out.scores)
