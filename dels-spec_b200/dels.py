@@ -12,8 +12,9 @@ runners in ``kernel/`` hand to the B200 kernels; the modules' own forward helper
 
 from __future__ import annotations
 
+from dataclasses import dataclass
 from pathlib import Path
-from typing import Iterable, Literal, Optional
+from typing import Callable, Iterable, Literal, Optional
 
 import torch
 import torch.nn as nn
@@ -28,35 +29,44 @@ def _activation_check(rank_activation: str) -> None:
         raise ValueError(f"rank_activation={rank_activation!r}; must be one of {_VALID_RANK_ACTIVATIONS}")
 
 
+def _counts_from_pt(p: Path) -> torch.Tensor:
+    payload = torch.load(p, map_location="cpu", weights_only=False)
+    if torch.is_tensor(payload):
+        return payload
+    if isinstance(payload, dict) and "counts" in payload:
+        return payload["counts"]
+    raise ValueError(
+        f"Unsupported unigram baseline .pt payload in {p}: expected a tensor or a dict with key 'counts'."
+    )
+
+
+def _counts_from_npz(p: Path) -> torch.Tensor:
+    import numpy as np
+
+    archive = np.load(p)
+    if "counts" not in archive.files:
+        raise ValueError(f"Unigram baseline npz {p} has no 'counts'.")
+    return torch.from_numpy(archive["counts"])
+
+
+# file suffix -> reader of the raw counts; a directory is resolved to the first of
+# _PRIOR_FILES it holds
+_COUNT_READERS = {".pt": _counts_from_pt, ".npz": _counts_from_npz}
+
+
 def _read_counts(path: str) -> torch.Tensor:
     """Unigram counts (float64, flat) from a .pt / .npz file or a directory holding one."""
     p = Path(path)
     if p.is_dir():
-        found = [p / name for name in _PRIOR_FILES if (p / name).exists()]
-        if not found:
+        p = next((p / name for name in _PRIOR_FILES if (p / name).exists()), None)
+        if p is None:
             raise ValueError(
                 f"Unigram baseline directory {path!r} must contain loss_mask_unigram.pt or loss_mask_unigram.npz."
             )
-        p = found[0]
-    if p.suffix == ".pt":
-        payload = torch.load(p, map_location="cpu", weights_only=False)
-        if isinstance(payload, dict) and "counts" in payload:
-            counts = payload["counts"]
-        elif torch.is_tensor(payload):
-            counts = payload
-        else:
-            raise ValueError(
-                f"Unsupported unigram baseline .pt payload in {p}: expected a tensor or a dict with key 'counts'."
-            )
-        return counts.to(torch.float64).reshape(-1)
-    if p.suffix == ".npz":
-        import numpy as np
-
-        archive = np.load(p)
-        if "counts" not in archive.files:
-            raise ValueError(f"Unigram baseline npz {p} has no 'counts'.")
-        return torch.from_numpy(archive["counts"]).to(torch.float64).reshape(-1)
-    raise ValueError(f"Unsupported unigram baseline path {p}; expected .pt, .npz, or a directory.")
+    reader = _COUNT_READERS.get(p.suffix)
+    if reader is None:
+        raise ValueError(f"Unsupported unigram baseline path {p}; expected .pt, .npz, or a directory.")
+    return reader(p).to(torch.float64).reshape(-1)
 
 
 def load_unigram_log_prior(
@@ -109,24 +119,176 @@ def parse_scalar_schedule(values: str | float | Iterable[float], steps: int, *, 
     return items
 
 
+def _state(ckpt) -> dict | None:
+    st = ckpt.get("model_state_dict")
+    return st if isinstance(st, dict) else None
+
+
+# Ordered probes: the first that matches names the runtime for a checkpoint.
+_KIND_PROBES: tuple[tuple[Callable[[dict], bool], str], ...] = (
+    (lambda ck: _state(ck) is not None and "down_proj" in _state(ck) and "up_proj" in _state(ck), "markov"),
+    (lambda ck: _state(ck) is not None and any(k.startswith("prefix_gru.") for k in _state(ck)), "dels"),
+    (lambda ck: isinstance(ck.get("model_config"), dict) and "gru_hidden_dim" in ck["model_config"], "dels"),
+    (lambda ck: "embedding_weight" in ck and "lm_head_weight" in ck, "markov"),
+)
+
+
 def detect_local_head_checkpoint_kind(checkpoint_path: str) -> Literal["dels", "markov"]:
     """Return the local-head runtime kind for a SpecForge checkpoint."""
     ckpt = torch.load(checkpoint_path, map_location="cpu", weights_only=False)
-    state = ckpt.get("model_state_dict")
-    if isinstance(state, dict):
-        if "down_proj" in state and "up_proj" in state:
-            return "markov"
-        if any(key.startswith("prefix_gru.") for key in state):
-            return "dels"
-    config = ckpt.get("model_config")
-    if isinstance(config, dict) and "gru_hidden_dim" in config:
-        return "dels"
-    if "embedding_weight" in ckpt and "lm_head_weight" in ckpt:
-        return "markov"
+    for matches, kind in _KIND_PROBES:
+        if matches(ckpt):
+            return kind  # type: ignore[return-value]
     raise ValueError(
         "Cannot identify local-head checkpoint type. Expected a SpecForge local_head.pt, "
         "merged_rnn_local_head.pt, markov_local_head.pt, or merged_markov_local_head.pt."
     )
+
+
+# ----------------------------------------------------------------------------- state-dict schemas
+# A checkpoint kind is described by a _Schema: how checkpoint keys map to module keys, an
+# ordered list of rules (the first rule whose predicate accepts an entry decides what
+# happens to it), which missing module keys are tolerated, and the error texts.  One
+# routine, _apply_schema, walks any state dict with any schema.
+
+def _open_checkpoint(path: str, what: str, checks) -> tuple[dict, dict]:
+    """(model_config, model_state_dict) of a training checkpoint, after the kind's
+    ordered (rejects(config, state), message) checks."""
+    ckpt = torch.load(path, map_location="cpu", weights_only=False)
+    config, state = ckpt.get("model_config"), ckpt.get("model_state_dict")
+    if config is None or state is None:
+        raise ValueError(f"{what} checkpoint must contain model_config and model_state_dict.")
+    for rejects, message in checks:
+        if rejects(config, state):
+            raise ValueError(message)
+    return config, state
+
+
+_JOINT_CONFIG_CHECKS = (
+    (lambda cfg, st: cfg.get("method") != "block_prefix_position_mix_joint",
+     "Only block_prefix_position_mix_joint checkpoints are supported."),
+    (lambda cfg, st: cfg.get("rnn_input", "block_prefix") != "block_prefix",
+     "Only block_prefix position-joint checkpoints are supported."),
+    (lambda cfg, st: cfg.get("local_head_config") is None, "Checkpoint is missing local_head_config."),
+    (lambda cfg, st: "baseline_logits" not in st, "Block-prefix position checkpoint is missing baseline_logits."),
+)
+
+_FROZEN_PREFIXES = ("embed_tokens.", "target_lm_head.")  # tensors that belong to the target model
+
+
+@dataclass
+class _Entry:
+    key: str  # key in the checkpoint
+    name: Optional[str]  # module key it maps to (None: not one of the module's tensors)
+    tensor: torch.Tensor
+
+
+@dataclass(frozen=True)
+class _Rule:
+    """``applies(entry, own_state, ctx)``; ``action`` one of load / load_reshaped /
+    frozen / fold_rank_to_hidden / reject (``message(entry, ctx)`` gives the text)."""
+
+    applies: Callable[[_Entry, dict, dict], bool]
+    action: str
+    message: Optional[Callable[[_Entry, dict], str]] = None
+
+
+@dataclass(frozen=True)
+class _Schema:
+    rename: Callable[[str], Optional[str]]
+    rules: tuple[_Rule, ...]
+    tolerated_missing: Callable[[str, nn.Module], bool]
+    mismatch: Callable[[list, list, list], str]
+
+
+def _shape_match(e: _Entry, own: dict, ctx: dict) -> bool:
+    return e.name in own and own[e.name].shape == e.tensor.shape
+
+
+def _apply_schema(model: nn.Module, state: dict, schema: _Schema, ctx: dict,
+                  extra: Optional[dict] = None) -> None:
+    """Load ``state`` into ``model`` as ``schema`` prescribes; ``extra`` entries (module
+    key -> tensor) override the checkpoint's.  Raises ValueError with the schema's texts."""
+    own = model.state_dict()
+    plan: dict[str, torch.Tensor] = {}
+    frozen: list[str] = []
+    for key, tensor in state.items():
+        e = _Entry(key, schema.rename(key), tensor)
+        rule = next((r for r in schema.rules if r.applies(e, own, ctx)), None)
+        if rule is None or rule.action == "reject":
+            raise ValueError(rule.message(e, ctx) if rule is not None and rule.message else f"cannot load {key}")
+        if rule.action == "load":
+            plan[e.name] = tensor.to(dtype=own[e.name].dtype)
+        elif rule.action == "load_reshaped":
+            plan[e.name] = tensor.reshape_as(own[e.name]).to(dtype=own[e.name].dtype)
+        elif rule.action == "fold_rank_to_hidden":
+            w = own["low_rank_lm_head.weight"]
+            plan["low_rank_lm_head.weight"] = (ctx["target_lm_head"].float() @ tensor.float()).to(dtype=w.dtype)
+        else:  # frozen: owned by the target model, recorded for the error text
+            frozen.append(key)
+    for name, tensor in (extra or {}).items():
+        plan[name] = tensor.to(dtype=own[name].dtype)
+    missing, unexpected = model.load_state_dict(plan, strict=False)
+    missing = [k for k in missing if not schema.tolerated_missing(k, model)]
+    if missing or unexpected:
+        raise ValueError(schema.mismatch(missing, unexpected, frozen))
+
+
+def _dels_tolerated(key: str, model: nn.Module) -> bool:
+    if key.startswith(_FROZEN_PREFIXES):
+        return True
+    unused = {"low_rank": "rank_to_hidden.", "target_lm_head": "low_rank_lm_head."}.get(model.lm_head_mode)
+    return unused is not None and key.startswith(unused)
+
+
+# DeLSLocalHead (local_head.pt, merged_rnn_local_head.pt): keys are module keys; a tensor
+# of the module's shape loads; target-model tensors are skipped, except the embedding of
+# a direct-vocab head, which is the head's own.
+_DELS_SCHEMA = _Schema(
+    rename=lambda key: key,
+    rules=(
+        _Rule(_shape_match, "load"),
+        _Rule(lambda e, own, ctx: e.key.startswith(_FROZEN_PREFIXES)
+              and not (ctx["direct_vocab"] and e.key.startswith("embed_tokens.")), "frozen"),
+        _Rule(lambda e, own, ctx: True, "reject",
+              lambda e, ctx: f"Unexpected local-head tensor {e.key} with shape {tuple(e.tensor.shape)}."),
+    ),
+    tolerated_missing=_dels_tolerated,
+    mismatch=lambda m, u, f: f"Local-head checkpoint mismatch: missing={m}, unexpected={u}, skipped_frozen={f}",
+)
+
+_JOINT_PREFIX = "local_head_model."
+_JOINT_TOP_LEVEL = ("position_gates", "baseline_logits")
+
+
+def _joint_rename(key: str) -> Optional[str]:
+    if key.startswith(_JOINT_PREFIX):
+        return key[len(_JOINT_PREFIX):]
+    return key if key in _JOINT_TOP_LEVEL else None
+
+
+# PositionMixJointHead: the local head's tensors sit under "local_head_model.", the gates
+# and the baseline at the top level; other keys (optimizer, target copies) are skipped; a
+# rank_to_hidden projection is folded into the low-rank head when the local head used
+# the target's LM head.
+_JOINT_SCHEMA = _Schema(
+    rename=_joint_rename,
+    rules=(
+        _Rule(lambda e, own, ctx: e.name is None or e.name.startswith(_FROZEN_PREFIXES), "frozen"),
+        _Rule(lambda e, own, ctx: e.name == "baseline_logits", "load_reshaped"),
+        _Rule(_shape_match, "load"),
+        _Rule(lambda e, own, ctx: e.name == "rank_to_hidden.weight" and ctx["lm_head_mode"] != "target_lm_head",
+              "reject",
+              lambda e, ctx: "Unexpected rank_to_hidden.weight for block-prefix joint local "
+                             f"lm_head_mode={ctx['lm_head_mode']!r}."),
+        _Rule(lambda e, own, ctx: e.name == "rank_to_hidden.weight", "fold_rank_to_hidden"),
+        _Rule(lambda e, own, ctx: True, "reject",
+              lambda e, ctx: f"Unexpected block-prefix joint tensor {e.key} mapped to {e.name} with shape "
+                             f"{tuple(e.tensor.shape)}."),
+    ),
+    tolerated_missing=lambda key, model: key.startswith(_FROZEN_PREFIXES),
+    mismatch=lambda m, u, f: f"Block-prefix position checkpoint mismatch: missing={m}, unexpected={u}, skipped={f}",
+)
 
 
 def _rank_logits(module, hidden: torch.Tensor) -> torch.Tensor:
@@ -201,10 +363,7 @@ class DeLSLocalHead(nn.Module):
         device: torch.device,
         merged_lm_head_path: Optional[str] = None,
     ) -> "DeLSLocalHead":
-        ckpt = torch.load(checkpoint_path, map_location="cpu", weights_only=False)
-        config, state = ckpt.get("model_config"), ckpt.get("model_state_dict")
-        if config is None or state is None:
-            raise ValueError("Local-head checkpoint must contain model_config and model_state_dict.")
+        config, state = _open_checkpoint(checkpoint_path, "Local-head", ())
         param = config.get("rnn_parameterization", config.get("local_head_parameterization"))
         direct_vocab = param == "direct_vocab" or config.get("architecture") == "direct_vocab_rnn"
         embedding_weight = None
@@ -232,37 +391,12 @@ class DeLSLocalHead(nn.Module):
         )
         model.pure_draft_prefix_len = int(config.get("pure_draft_prefix_len", 0 if direct_vocab else 1))
         model.shift_label = bool(config.get("shift_label", False))
-
-        own = model.state_dict()
-        keep, frozen = {}, []
-        for key, tensor in state.items():
-            if key in own and own[key].shape == tensor.shape:
-                keep[key] = tensor.to(dtype=own[key].dtype)
-                continue
-            frozen_copy = key.startswith(("embed_tokens.", "target_lm_head."))
-            if frozen_copy and not (direct_vocab and key.startswith("embed_tokens.")):
-                frozen.append(key)
-                continue
-            raise ValueError(f"Unexpected local-head tensor {key} with shape {tuple(tensor.shape)}.")
+        extra = None
         if merged_lm_head_path is not None:
             merged = torch.load(merged_lm_head_path, map_location="cpu", weights_only=False)
-            weight = merged["weight"] if isinstance(merged, dict) else merged
-            keep["low_rank_lm_head.weight"] = weight.to(dtype=own["low_rank_lm_head.weight"].dtype)
+            extra = {"low_rank_lm_head.weight": merged["weight"] if isinstance(merged, dict) else merged}
             model.lm_head_mode = "low_rank"
-        missing, unexpected = model.load_state_dict(keep, strict=False)
-
-        def tolerated(key: str) -> bool:
-            if key.startswith(("embed_tokens.", "target_lm_head.")):
-                return True
-            if model.lm_head_mode == "low_rank" and key.startswith("rank_to_hidden."):
-                return True
-            return model.lm_head_mode == "target_lm_head" and key.startswith("low_rank_lm_head.")
-
-        missing = [key for key in missing if not tolerated(key)]
-        if missing or unexpected:
-            raise ValueError(
-                f"Local-head checkpoint mismatch: missing={missing}, unexpected={unexpected}, skipped_frozen={frozen}"
-            )
+        _apply_schema(model, state, _DELS_SCHEMA, {"direct_vocab": direct_vocab}, extra)
         if model.lm_head_mode == "target_lm_head":
             model.fuse_target_lm_head_()
         return model
@@ -294,6 +428,37 @@ class DeLSLocalHead(nn.Module):
         return hidden
 
 
+def _markov_merged(ckpt: dict, target_model) -> tuple[torch.Tensor, torch.Tensor]:
+    return ckpt["embedding_weight"], ckpt["lm_head_weight"]
+
+
+def _markov_factorized(ckpt: dict, target_model) -> tuple[torch.Tensor, torch.Tensor]:
+    """embedding = E_target . down, lm_head = W_target . up^T (fp32 products)."""
+    config, state = ckpt.get("model_config"), ckpt.get("model_state_dict")
+    if config is None or state is None:
+        raise ValueError(
+            "Markov DeLS checkpoint must be either merged_markov_local_head.pt or markov_local_head.pt "
+            "from SpecForge scripts/train_markov_local_head.py."
+        )
+    if "down_proj" not in state or "up_proj" not in state:
+        raise ValueError("Markov local-head checkpoint must contain down_proj and up_proj.")
+    down, up = state["down_proj"].to(torch.float32), state["up_proj"].to(torch.float32)
+    emb = target_model.model.embed_tokens.weight.detach().cpu().to(torch.float32) @ down
+    head = target_model.lm_head.weight.detach().cpu().to(torch.float32) @ up.t()
+    want_rank = int(config.get("rank", down.shape[1]))
+    if emb.shape[1] != want_rank:
+        raise ValueError(f"Unexpected Markov rank: merged={emb.shape[1]}, config={want_rank}")
+    return emb, head
+
+
+# Ordered (accepts, factors) pairs: merged_markov_local_head.pt carries both merged
+# factors; anything else is read as the factorised training checkpoint.
+_MARKOV_FORMATS: tuple[tuple[Callable[[dict], bool], Callable], ...] = (
+    (lambda ck: "embedding_weight" in ck and "lm_head_weight" in ck, _markov_merged),
+    (lambda ck: True, _markov_factorized),
+)
+
+
 class MarkovDeLSLocalHead(nn.Module):
     """Inference module for dense Markov local-head checkpoints: logits of the next token
     are embedding[prev] . lm_head^T with both factors merged to the vocabulary."""
@@ -318,25 +483,11 @@ class MarkovDeLSLocalHead(nn.Module):
     def from_checkpoint(cls, *, checkpoint_path: str, target_model: nn.Module, dtype: torch.dtype,
                         device: torch.device) -> "MarkovDeLSLocalHead":
         ckpt = torch.load(checkpoint_path, map_location="cpu", weights_only=False)
-        if "embedding_weight" in ckpt and "lm_head_weight" in ckpt:
-            emb, head = ckpt["embedding_weight"], ckpt["lm_head_weight"]
-        else:
-            config, state = ckpt.get("model_config"), ckpt.get("model_state_dict")
-            if config is None or state is None:
-                raise ValueError(
-                    "Markov DeLS checkpoint must be either merged_markov_local_head.pt or markov_local_head.pt "
-                    "from SpecForge scripts/train_markov_local_head.py."
-                )
-            if "down_proj" not in state or "up_proj" not in state:
-                raise ValueError("Markov local-head checkpoint must contain down_proj and up_proj.")
-            down = state["down_proj"].to(torch.float32)
-            up = state["up_proj"].to(torch.float32)
-            emb = target_model.model.embed_tokens.weight.detach().cpu().to(torch.float32) @ down
-            head = target_model.lm_head.weight.detach().cpu().to(torch.float32) @ up.t()
-            want_rank = int(config.get("rank", down.shape[1]))
-            if emb.shape[1] != want_rank:
-                raise ValueError(f"Unexpected Markov rank: merged={emb.shape[1]}, config={want_rank}")
-        return cls(embedding_weight=emb, lm_head_weight=head, dtype=dtype, device=device)
+        for matches, factors in _MARKOV_FORMATS:
+            if matches(ckpt):
+                emb, head = factors(ckpt, target_model)
+                return cls(embedding_weight=emb, lm_head_weight=head, dtype=dtype, device=device)
+        raise AssertionError("unreachable: the last Markov format accepts every checkpoint")
 
     @torch.inference_mode()
     def logits_from_token(self, token_ids: torch.Tensor) -> torch.Tensor:
@@ -386,19 +537,8 @@ class PositionMixJointHead(nn.Module):
     @classmethod
     def from_checkpoint(cls, *, checkpoint_path: str, target_model: nn.Module, block_size: int,
                         dtype: torch.dtype, device: torch.device) -> "PositionMixJointHead":
-        ckpt = torch.load(checkpoint_path, map_location="cpu", weights_only=False)
-        config, state = ckpt.get("model_config"), ckpt.get("model_state_dict")
-        if config is None or state is None:
-            raise ValueError("Block-prefix position checkpoint must contain model_config and model_state_dict.")
-        if config.get("method") != "block_prefix_position_mix_joint":
-            raise ValueError("Only block_prefix_position_mix_joint checkpoints are supported.")
-        if config.get("rnn_input", "block_prefix") != "block_prefix":
-            raise ValueError("Only block_prefix position-joint checkpoints are supported.")
-        local = config.get("local_head_config")
-        if local is None:
-            raise ValueError("Checkpoint is missing local_head_config.")
-        if "baseline_logits" not in state:
-            raise ValueError("Block-prefix position checkpoint is missing baseline_logits.")
+        config, state = _open_checkpoint(checkpoint_path, "Block-prefix position", _JOINT_CONFIG_CHECKS)
+        local = config["local_head_config"]
         shift_label = bool(config.get("dflash_shift_label", False))
         suffix_len = int(block_size) - (1 if shift_label else 2)
         if suffix_len <= 0:
@@ -419,42 +559,9 @@ class PositionMixJointHead(nn.Module):
             dtype=dtype,
             device=device,
         )
-        own = model.state_dict()
-        keep, skipped = {}, []
-        prefix = "local_head_model."
-        for key, tensor in state.items():
-            if key.startswith(prefix):
-                name = key[len(prefix):]
-            elif key in ("position_gates", "baseline_logits"):
-                name = key
-            else:
-                skipped.append(key)
-                continue
-            if name.startswith(("embed_tokens.", "target_lm_head.")):
-                skipped.append(key)
-            elif name == "baseline_logits":
-                keep[name] = tensor.reshape_as(own[name]).to(dtype=own[name].dtype)
-            elif name in own and own[name].shape == tensor.shape:
-                keep[name] = tensor.to(dtype=own[name].dtype)
-            elif name == "rank_to_hidden.weight":
-                mode = local.get("lm_head_mode", "low_rank")
-                if mode != "target_lm_head":
-                    raise ValueError(
-                        f"Unexpected rank_to_hidden.weight for block-prefix joint local lm_head_mode={mode!r}."
-                    )
-                fused = target_model.lm_head.weight.detach().float() @ tensor.float()
-                keep["low_rank_lm_head.weight"] = fused.to(dtype=own["low_rank_lm_head.weight"].dtype)
-            else:
-                raise ValueError(
-                    f"Unexpected block-prefix joint tensor {key} mapped to {name} with shape {tuple(tensor.shape)}."
-                )
-        missing, unexpected = model.load_state_dict(keep, strict=False)
-        missing = [k for k in missing if not k.startswith(("embed_tokens.", "target_lm_head."))]
-        if missing or unexpected:
-            raise ValueError(
-                f"Block-prefix position checkpoint mismatch: missing={missing}, unexpected={unexpected}, "
-                f"skipped={skipped}"
-            )
+        ctx = {"lm_head_mode": local.get("lm_head_mode", "low_rank"),
+               "target_lm_head": target_model.lm_head.weight.detach()}
+        _apply_schema(model, state, _JOINT_SCHEMA, ctx)
         return model
 
     @torch.inference_mode()
