@@ -846,6 +846,32 @@ def runner_cpu_rate(inp, reps: int = 2) -> tuple[float, int, str]:
         f"one batch-1 rollout of {inp.steps} steps x {reps} repetitions, bf16 torch on the host"
 
 
+def reference_gpu_runner(args, kw, ours, prefix, base, stream, dev) -> dict:
+    """The reference's own DeLSGraphRunner (Triton kernels, code/kernel/dels.py:214-478) on
+    this GPU, beside ours: same local head, schedules, prior and call inputs.  The
+    reference tree is not part of this repository; ``--reference-runner`` names a copy of
+    its ``code/`` directory, whose ``kernel/dels.py`` is loaded under a module name of its
+    own.  Returns its ms per call (same timing as ours) and how many tokens agree (a
+    greedy rollout may part ways after a near-tie of the scores)."""
+    import importlib.util
+
+    path = Path(args.reference_runner) / "kernel" / "dels.py"
+    spec = importlib.util.spec_from_file_location("dels_reference_kernel_dels", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    ref = mod.DeLSGraphRunner(**kw)
+    ms = timed(lambda: ref(prefix, base), args.steps, args.warmup, 1, stream, dev, hold_ms=300.0) / args.steps
+    ms_ours = timed(lambda: ours(prefix, base), args.steps, args.warmup, 1, stream, dev, hold_ms=300.0) / args.steps
+    t_ref, t_ours = ref(prefix, base), ours(prefix, base)
+    torch.cuda.synchronize()
+    same = (t_ref == t_ours)
+    first_diff = [int(torch.nonzero(~row).min()) if not bool(row.all()) else None for row in same]
+    return {"ms_per_call": ms, "ms_per_call_ours_same_run": ms_ours, "speedup": ms / ms_ours,
+            "uses_triton": bool(getattr(ref, "_can_triton_fuse", False)),
+            "tokens_identical_frac": float(same.float().mean()), "first_differing_step_per_row": first_diff[:8],
+            "source": "the reference's code/kernel/dels.py, loaded from --reference-runner at run time"}
+
+
 def run_runner(args, rank, world, dev):
     """The drop-in DeLSGraphRunner (kernel/dels.py) at the released local-head shapes
     (V = 151936, E = 256, G = 1024, r = 256), batch B, 14 suffix steps: one call =
@@ -914,6 +940,8 @@ def run_runner(args, rank, world, dev):
     }
     if extra:
         res["runner_schedule"] = extra
+    if args.reference_runner and not args.runner_hidden:
+        res["reference_gpu_runner"] = reference_gpu_runner(args, kw, runner, prefix, inp.base, stream, dev)
     if not args.no_cpu_baseline:
         rps, cores, sample = runner_cpu_rate(inp)
         res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample}
@@ -1106,6 +1134,9 @@ def main():
     ap.add_argument("--runner-hidden", action="store_true",
                     help="runner workload: DeLSFusedGraphRunner fed the draft hidden states")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reference-runner", default="",
+                    help="runner workload: path to a copy of the reference's code/ directory; its Triton "
+                         "DeLSGraphRunner is timed beside ours on the same GPU and inputs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()

@@ -78,10 +78,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dels_gru_step_bf16": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "dels_fused_argmax_base_gru_bf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _I, _U32, _P, _P,
                                              _P, _SZ, _P, _P, _P, _I, _P, _P]),
-    "dels_gru_correction_mid_bf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _I64, _P, _I64, _I,
-                                          _P, _P, _P, _P, _P]),
-    "dels_gru_rank_gemv_bf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _I64, _P, _I, _I, _P, _P,
-                                     _P, _P, _P]),
+    "dels_gru_correction_mid_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _I64, _P, _I64,
+                                          _I, _P, _P, _P, _P, _P]),
+    "dels_gru_rank_gemv_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _I64, _P, _I, _I, _P,
+                                     _P, _P, _P, _P]),
     "dels_gru_gates_bf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _P]),
     "dels_rank_gemv_bf16": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "dels_gather_scaled_rows_bf16": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),

@@ -1096,9 +1096,9 @@ int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w
 }
 
 // The GRU gates of (tokens, gi_table, gh, h_in) as the x source of rank_gemv_common.
-static int gru_gate_source(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
-                           const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V,
-                           void* ws, GruGateSrc* gate) {
+static int gru_gate_source(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
+                           int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B,
+                           int G, int V, void* ws, GruGateSrc* gate) {
   if (B < 0 || G <= 0 || V <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d V=%d", B, G, V);
   if (tokens == nullptr || gi_table == nullptr || gh == nullptr || h_out == nullptr)
     return fail(DELS_ERR_INVALID_ARG, "NULL argument");
@@ -1108,6 +1108,7 @@ static int gru_gate_source(const int64_t* tokens, int64_t tok_stride, const void
   if (ld_table < 3LL * G || ld_gh < 3LL * G) return fail(DELS_ERR_INVALID_ARG, "gi / gh leading dimension < 3G");
   gate->tokens = reinterpret_cast<const long long*>(tokens);
   gate->tok_stride = tok_stride;
+  gate->token_keys = token_keys != 0 ? 1 : 0;
   gate->table = reinterpret_cast<const __nv_bfloat16*>(gi_table);
   gate->ld_table = ld_table;
   gate->gh = reinterpret_cast<const __nv_bfloat16*>(gh);
@@ -1119,24 +1120,26 @@ static int gru_gate_source(const int64_t* tokens, int64_t tok_stride, const void
   return DELS_OK;
 }
 
-int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
-                            const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V,
-                            const void* w_rank, int64_t ld_w, const void* bias, int r, int activation,
+int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
+                            int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B,
+                            int G, int V, const void* w_rank, int64_t ld_w, const void* bias, int r, int activation,
                             const float* alpha, void* s_scaled, int64_t* keys, void* ws, void* stream) {
   GruGateSrc gate;
-  int rc = gru_gate_source(tokens, tok_stride, gi_table, ld_table, gh, ld_gh, h_in, h_out, B, G, V, ws, &gate);
+  int rc = gru_gate_source(tokens, tok_stride, token_keys, gi_table, ld_table, gh, ld_gh, h_in, h_out, B, G, V, ws,
+                           &gate);
   if (rc != DELS_OK) return rc;
   return rank_gemv_common(nullptr, G, w_rank, ld_w, bias, nullptr, 0, B, G, r, activation, alpha, 1, nullptr,
                           nullptr, s_scaled, keys, ws, stream, &gate);
 }
 
-int dels_gru_correction_mid_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table,
+int dels_gru_correction_mid_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
                                  int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in, void* h_out,
                                  int B, int G, int V, const void* w_s, int64_t ld_ws, const void* z, int64_t ld_z,
                                  int M, const float* alpha, void* s_scaled, int64_t* keys, void* ws, void* stream) {
   if (z == nullptr) return fail(DELS_ERR_INVALID_ARG, "z is NULL");
   GruGateSrc gate;
-  int rc = gru_gate_source(tokens, tok_stride, gi_table, ld_table, gh, ld_gh, h_in, h_out, B, G, V, ws, &gate);
+  int rc = gru_gate_source(tokens, tok_stride, token_keys, gi_table, ld_table, gh, ld_gh, h_in, h_out, B, G, V, ws,
+                           &gate);
   if (rc != DELS_OK) return rc;
   return rank_gemv_common(nullptr, G, w_s, ld_ws, nullptr, z, ld_z, B, G, M, DELS_ACT_IDENTITY, alpha, 1, nullptr,
                           nullptr, s_scaled, keys, ws, stream, &gate);

@@ -197,6 +197,7 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
         const int b = e / (K / 8), k8 = e % (K / 8);
         const int row = b0 + b;
         long long tok = gate.tokens[(long long)row * gate.tok_stride];
+        if (gate.token_keys) tok = (long long)key_index(tok);  // the scorer's packed (score, index) key
         if (tok < 0 || tok >= gate.V) {
           if (gate.status != nullptr) atomicCAS(gate.status, 0, DELS_ERR_INVALID_ARG);
           tok = tok < 0 ? 0 : gate.V - 1;

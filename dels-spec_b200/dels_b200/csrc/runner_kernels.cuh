@@ -19,8 +19,9 @@ inline size_t rank_gemv_smem_bytes(int K) { return (size_t)kRunnerMaxB * K * 2; 
 // x is read from memory): h_out[b] = GRU gates of (gi = table[tokens[b * tok_stride]],
 // gh[b], h_in[b]), staged in shared memory by every CTA and stored by CTA 0.
 struct GruGateSrc {
-  const long long* tokens;
+  const long long* tokens;     // token ids, or (token_keys) the previous step's packed argmax keys
   long long tok_stride;
+  int token_keys;
   const __nv_bfloat16* table;  // [V, 3G] input projections, or null
   long long ld_table;
   const __nv_bfloat16* gh;     // [B, 3G] bf16(W_hh h + b_hh)

@@ -381,7 +381,9 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
       for (int q = 1; q < 4; ++q) k = red[q * NB + et] > k ? red[q * NB + et] : k;
       if (k != kKeyEmpty) {
         atomicMax(&args.keys[et], k);
-        __threadfence();
+        // ordered before this CTA's completion count only when the last CTA decodes;
+        // keys-only calls leave their visibility to the end of the grid
+        if (args.idx_out != nullptr) __threadfence();
       }
     }
   } else if constexpr (GH) {

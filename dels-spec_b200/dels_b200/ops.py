@@ -605,10 +605,12 @@ def gru_rank_gemv(
     activation: str = "identity",
     keys: torch.Tensor | None = None,
     ws: Workspace | None = None,
+    tokens_are_keys: bool = False,
 ) -> torch.Tensor:
     """One small-batch rollout step: h_out = GRU gates(gi_table[tokens], gh, h_in) (gh =
     bf16(W_hh h_in + b_hh) from an earlier rank_gemv), then s_scaled = bf16(alpha[0] *
-    act(w_rank . h_out + bias)) in the same launch."""
+    act(w_rank . h_out + bias)) in the same launch.  ``tokens_are_keys``: ``tokens`` holds
+    the previous step's packed argmax keys (a keys-only scorer call), decoded here."""
     _require_cuda("tokens", tokens, torch.int64)
     _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
     _require_cuda("gh", gh, torch.bfloat16, 2)
@@ -624,7 +626,8 @@ def gru_rank_gemv(
     if w_rank.shape[1] != G or s_scaled.shape != (B, r) or not s_scaled.is_contiguous():
         raise ValueError("rank projection shapes do not match")
     tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
-    _lib.call("dels_gru_rank_gemv_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+    _lib.call("dels_gru_rank_gemv_bf16", _ptr(tokens), tok_stride, int(tokens_are_keys), _ptr(gi_table),
+              _row_major("gi_table", gi_table),
               _ptr(gh), gh.stride(0), _ptr(h_in), _ptr(h_out), B, G, V, _ptr(w_rank), _row_major("w_rank", w_rank),
               _ptr(bias), r, ACTIVATIONS[activation], _ptr(alpha), _ptr(s_scaled), _ptr(keys),
               None if ws is None else ws.ptr, _stream(h_out.device))
@@ -644,9 +647,11 @@ def gru_correction_mid(
     *,
     keys: torch.Tensor | None = None,
     ws: Workspace | None = None,
+    tokens_are_keys: bool = False,
 ) -> torch.Tensor:
     """One small-batch Domino step: h_out = GRU gates(gi_table[tokens], gh, h_in), then
-    s_scaled = bf16(alpha[0] * SiLU(z + bf16(w_s . h_out))) in the same launch."""
+    s_scaled = bf16(alpha[0] * SiLU(z + bf16(w_s . h_out))) in the same launch
+    (``tokens_are_keys`` as in :func:`gru_rank_gemv`)."""
     _require_cuda("tokens", tokens, torch.int64)
     for name, t in (("gi_table", gi_table), ("gh", gh), ("h_out", h_out), ("w_s", w_s), ("z", z)):
         _require_cuda(name, t, torch.bfloat16, 2)
@@ -661,7 +666,7 @@ def gru_correction_mid(
             or not s_scaled.is_contiguous():
         raise ValueError("correction MLP shapes do not match")
     tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
-    _lib.call("dels_gru_correction_mid_bf16", _ptr(tokens), tok_stride, _ptr(gi_table),
+    _lib.call("dels_gru_correction_mid_bf16", _ptr(tokens), tok_stride, int(tokens_are_keys), _ptr(gi_table),
               _row_major("gi_table", gi_table), _ptr(gh), gh.stride(0), _ptr(h_in), _ptr(h_out), B, G, V, _ptr(w_s),
               _row_major("w_s", w_s), _ptr(z), _row_major("z", z), M, _ptr(_f32_vec("alpha", alpha, h_out.device)),
               _ptr(s_scaled), _ptr(keys), None if ws is None else ws.ptr, _stream(h_out.device))

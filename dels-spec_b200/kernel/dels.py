@@ -168,6 +168,13 @@ class DeLSGraphRunner:
         if self._tc:
             need = max(ops.linear_workspace_bytes(B, G, 3 * G), ops.rank_workspace_bytes(B, G, r))
             self._tc_ws = ops.Workspace(need, device)
+        if self._overlap:
+            # Per-step packed argmax keys: each step's scorer only writes keys (no in-kernel
+            # decode: no last-CTA count, fence or decode at the end of every step), the next
+            # step's fused GRU-gates + rank GEMV decodes the token it needs, and one decode
+            # per call fills the token slots.
+            self._step_keys = torch.empty(S, B, dtype=torch.int64, device=device)
+            self._key_outs = [ops.ScoreOut(tokens=None, scores=None, keys=self._step_keys[i]) for i in range(S)]
         if self._tc or self._overlap or self._split_gru:
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
             # the first step's h is zero, so its gh is the bias alone
@@ -213,7 +220,8 @@ class DeLSGraphRunner:
             if self._overlap:
                 ops.gru_rank_gemv(tokens, self._gru_input_proj_table, gh, h_prev, h_new, self.rank_weight,
                                   self._alpha[step : step + 1], self._s_scaled, bias=self.rank_bias,
-                                  activation=self._activation, keys=self._keys, ws=self._ws)
+                                  activation=self._activation, keys=self._step_keys[step], ws=self._ws,
+                                  tokens_are_keys=step > 0)
             else:
                 ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_prev, h_new, ws=self._ws)
                 self._rank(h_new, step)
@@ -222,7 +230,13 @@ class DeLSGraphRunner:
                 self._score(step, next_gh=(h_new, self._gh))
             else:
                 self._score(step)
-            tokens, h_prev, gh, cur = self._tokens[step], h_new, self._gh, cur ^ 1
+            if self._overlap:
+                tokens = self._step_keys[step]
+            else:
+                tokens = self._tokens[step]
+            h_prev, gh, cur = h_new, self._gh, cur ^ 1
+        if self._overlap:
+            ops.keys_decode(self._step_keys.view(-1), tokens=self._tokens.view(-1), with_scores=False)
         self.static_out.copy_(self._tokens.t())
 
     def _forward_impl(self):
@@ -248,18 +262,18 @@ class DeLSGraphRunner:
         return True
 
     def _score(self, step: int, next_gh=None):
+        out = self._key_outs[step] if self._overlap else self._outs[step]
         if next_gh is not None:
             h, gh_out = next_gh
             ops.fused_argmax_base_gru_bf16(
                 self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight, self._prior_f32,
                 self._beta[step : step + 1], self.gru_w_hh, self.gru_b_hh, h, gh_out, keys_ready=True,
-                out=self._outs[step], ws=self._ws,
+                out=out, ws=self._ws,
             )
             return
         ops.fused_argmax_base_bf16(
             self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight,
-            self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],
-            ws=self._ws,
+            self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=out, ws=self._ws,
         )
 
     @torch.inference_mode()

@@ -185,6 +185,11 @@ class DraftCorrectionGraphRunner:
                            and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0")
         if self._tc or self._overlap or self._split_gru:
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
+        if self._overlap:
+            # per-step packed argmax keys: keys-only scorer calls, the next step's fused gates
+            # decode the token they need, one decode per call fills the token slots
+            self._step_keys = torch.empty(max(S, 1), B, dtype=torch.int64, device=device)
+            self._key_outs = [ops.ScoreOut(tokens=None, scores=None, keys=self._step_keys[i]) for i in range(S)]
 
         ops.init(device)
         stream = torch.cuda.Stream(device=device)
@@ -220,13 +225,16 @@ class DraftCorrectionGraphRunner:
         gh_on_scorer = self._overlap or self._split_gru
         for t in range(S):
             last = t + 1 == S
+            keys = self._step_keys[t] if self._overlap else self._keys
+            out = self._key_outs[t] if self._overlap else self._outs[t]
             if self._overlap and t > 0:
-                # the previous token's GRU gates fused into this step's correction layer
+                # the previous token's GRU gates fused into this step's correction layer; the
+                # token comes from the previous step's packed key
                 h_prev, h = h, self._h[cur]
                 cur ^= 1
-                ops.gru_correction_mid(self._tokens[t - 1], self._gru_input_proj_table, self._gh, h_prev, h,
-                                       self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
-                                       ws=self._ws)
+                ops.gru_correction_mid(self._step_keys[t - 1], self._gru_input_proj_table, self._gh, h_prev, h,
+                                       self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=keys, ws=self._ws,
+                                       tokens_are_keys=True)
             elif self._split_gru and t > 0:
                 h_prev, h = h, self._h[cur]
                 cur ^= 1
@@ -237,21 +245,22 @@ class DraftCorrectionGraphRunner:
                 ops.correction_mid_tc(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
                                       ws=self._tc_ws)
             else:
-                ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
-                                   ws=self._ws)
+                ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=keys, ws=self._ws)
             base_t = self.static_base_logits[:, t, :]
             if gh_on_scorer and not last:
                 # the scorer's helper warps compute the next update's gh = bf16(W_hh h + b_hh)
                 ops.fused_argmax_base_gru_bf16(base_t, self._s_scaled, self.fc2_weight, self._prior_f32,
                                                self._beta, self.gru_w_hh, self.gru_b_hh, h, self._gh,
-                                               keys_ready=True, out=self._outs[t], ws=self._ws)
+                                               keys_ready=True, out=out, ws=self._ws)
             else:
                 ops.fused_argmax_base_bf16(base_t, self._s_scaled, self.fc2_weight, self._prior_f32, self._beta,
-                                           n_pos=1, keys_ready=True, out=self._outs[t], ws=self._ws)
+                                           n_pos=1, keys_ready=True, out=out, ws=self._ws)
             if not last and not gh_on_scorer:
                 h = self._gru(self._tokens[t], h, self._h[cur])
                 cur ^= 1
         if S > 0:
+            if self._overlap:
+                ops.keys_decode(self._step_keys[:S].reshape(-1), tokens=self._tokens[:S].view(-1), with_scores=False)
             self.static_out.copy_(self._tokens[:S].t())
 
     @torch.inference_mode()

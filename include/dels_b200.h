@@ -256,8 +256,11 @@ DELS_API int dels_fused_argmax_base_gru_bf16(const void* base, int64_t ld_base, 
  * previous step's scorer since it does not need that step's token.  Every CTA evaluates
  * the gates for all B rows itself; G, ld_table, ld_gh % 8 == 0, 16-byte aligned rows.
  * ws (optional) supplies the counter that the following scorer call expects at zero and
- * the status word for out-of-range token ids (clamped). */
-DELS_API int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table,
+ * the status word for out-of-range token ids (clamped).  token_keys != 0: tokens[] holds
+ * the previous step's packed argmax keys (a keys-only scorer call, idx_out NULL), decoded
+ * here, so the rollout's scorer needs no in-kernel decode (its last-CTA count and fences)
+ * and one dels_keys_decode per call yields all the tokens. */
+DELS_API int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
                                      int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in, void* h_out,
                                      int B, int G, int V, const void* w_rank, int64_t ld_w, const void* bias, int r,
                                      int activation, const float* alpha, void* s_scaled, int64_t* keys, void* ws,
@@ -267,8 +270,9 @@ DELS_API int dels_gru_rank_gemv_bf16(const int64_t* tokens, int64_t tok_stride, 
  * (code/kernel/domino.py:423-435) into the correction MLP's hidden layer of the next step
  * (:402, :92-97),
  * h_out as in dels_gru_rank_gemv_bf16, then s_scaled[b] = bf16(alpha[0] * SiLU(z[b] +
- * bf16(w_s . h_out[b]))) and keys[0..B) reset as in dels_correction_mid_bf16. */
-DELS_API int dels_gru_correction_mid_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table,
+ * bf16(w_s . h_out[b]))) and keys[0..B) reset as in dels_correction_mid_bf16; token_keys
+ * as above. */
+DELS_API int dels_gru_correction_mid_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
                                           int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in,
                                           void* h_out, int B, int G, int V, const void* w_s, int64_t ld_ws,
                                           const void* z, int64_t ld_z, int M, const float* alpha, void* s_scaled,

@@ -116,11 +116,11 @@ def test_argument_errors_are_reported_before_device_work(lib):
         _lib.call("dels_accept_offsets", None, 0, None, 0, 1, 1, 2, None, None, None)
     # the fused GRU-gate entry points check their operands before any device work
     with pytest.raises(_lib.DelsArgumentError) as ei:
-        _lib.call("dels_gru_rank_gemv_bf16", None, 1, None, 3072, None, 3072, None, None, 1, 1024, 100, None, 1024,
+        _lib.call("dels_gru_rank_gemv_bf16", None, 1, 0, None, 3072, None, 3072, None, None, 1, 1024, 100, None, 1024,
                   None, 256, 0, None, None, None, None, None)
     assert ei.value.status == _lib.DELS_ERR_INVALID_ARG
     with pytest.raises(_lib.DelsArgumentError) as ei:
-        _lib.call("dels_gru_correction_mid_bf16", ctypes.c_void_p(addr), 1, ctypes.c_void_p(addr), 3072,
+        _lib.call("dels_gru_correction_mid_bf16", ctypes.c_void_p(addr), 1, 0, ctypes.c_void_p(addr), 3072,
                   ctypes.c_void_p(addr), 3072, None, ctypes.c_void_p(addr), 1, 1024, 100, None, 1024,
                   ctypes.c_void_p(addr), 1024, 1024, None, None, None, None, None)
     assert ei.value.status == _lib.DELS_ERR_ALIGNMENT

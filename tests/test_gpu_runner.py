@@ -187,6 +187,60 @@ def test_scorer_with_next_gru_projection(cuda_device, B):
     np.testing.assert_allclose(got, exact, rtol=2 ** -7, atol=1e-3)
 
 
+@pytest.mark.parametrize("B", [1, 3])
+def test_gru_gates_from_packed_keys(cuda_device, B):
+    """The fused GRU-gates entry points take the previous step's packed argmax keys in
+    place of token ids (token_keys): h, s_scaled and the reset keys are bit-identical to
+    the token-id call, and a keys-only scorer call plus one keys decode gives the tokens
+    of the in-kernel decode."""
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(70 + B)
+    dev = cuda_device
+    V, G, r, M = 4099, 256, 64, 96
+    bf = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev).to(torch.bfloat16)  # noqa: E731
+    table = bf(rng.standard_normal((V, 3 * G)) * 0.5)
+    gh = bf(rng.standard_normal((B, 3 * G)) * 0.5)
+    h_in = bf(rng.standard_normal((B, G)))
+    w_rank = bf(rng.standard_normal((r, G)) * 0.05)
+    w_s = bf(rng.standard_normal((M, G)) * 0.05)
+    z = bf(rng.standard_normal((B, M)))
+    alpha = torch.tensor([0.7], device=dev)
+    # keys of a keys-only scorer call over random base logits; the decoded tokens feed the
+    # token-id path
+    base = bf(rng.standard_normal((B, V)))
+    s0 = bf(rng.standard_normal((B, r)) * 0.3)
+    Vr = bf(rng.standard_normal((V, r)) * 0.3)
+    prior = torch.from_numpy(O.bf16_round(O.zipf_log_prior(V).astype(np.float32))).to(dev)
+    beta = torch.tensor([0.2], device=dev)
+    ws = ops.Workspace(1 << 12, dev)
+    ref = ops.fused_argmax_base_bf16(base, s0, Vr, prior, beta, n_pos=1, ws=ws)
+    keys_only = ops.ScoreOut(tokens=None, scores=None, keys=torch.empty(B, dtype=torch.int64, device=dev))
+    ops.fused_argmax_base_bf16(base, s0, Vr, prior, beta, n_pos=1, out=keys_only, ws=ws)
+    tok, _ = ops.keys_decode(keys_only.keys, with_scores=False)
+    assert torch.equal(tok, ref.tokens)
+    assert torch.equal(keys_only.keys, ref.keys)
+    for entry in ("rank", "correction"):
+        outs = []
+        for as_keys in (False, True):
+            h_out = torch.empty(B, G, dtype=torch.bfloat16, device=dev)
+            width = r if entry == "rank" else M
+            s_scaled = torch.empty(B, width, dtype=torch.bfloat16, device=dev)
+            k_reset = torch.zeros(B, dtype=torch.int64, device=dev)
+            src = keys_only.keys if as_keys else ref.tokens
+            if entry == "rank":
+                ops.gru_rank_gemv(src, table, gh, h_in, h_out, w_rank, alpha, s_scaled, keys=k_reset, ws=ws,
+                                  tokens_are_keys=as_keys)
+            else:
+                ops.gru_correction_mid(src, table, gh, h_in, h_out, w_s, z, alpha, s_scaled, keys=k_reset, ws=ws,
+                                       tokens_are_keys=as_keys)
+            outs.append((h_out, s_scaled, k_reset))
+        torch.cuda.synchronize()
+        for a, b in zip(*outs):
+            assert torch.equal(a, b), entry
+    ws.check()
+
+
 @pytest.mark.parametrize("B", [4, 5, 12, 20, 48, 64])
 def test_runner_batches(cuda_device, B):
     """Batch sizes past the fixtures': the plain (<= 4 rows) and staged skinny scorers (16- and
