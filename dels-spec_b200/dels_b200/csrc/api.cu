@@ -37,6 +37,8 @@ bool g_use_pairs = true;
 // (DELS_SCORER_SKINNY=0 in the environment selects the 128-row tile kernel instead).
 bool g_use_skinny = true;
 constexpr int kSkinnyMaxRows = 32;
+// K blocks per pipeline stage of the paired scorer (DELS_PAIR_KGROUP=1 or 2)
+int g_pair_kgroup = 2;
 constexpr int kSkinnyStageRows = 4;
 // Programmatic dependent launch for the kernels of a rollout step (DELS_PDL=0 in the
 // environment turns it off).
@@ -202,6 +204,7 @@ int init_device(int dev) {
   if (const char* env = getenv("DELS_SCORER_PAIRS")) g_use_pairs = env[0] != '0';
   if (const char* env = getenv("DELS_SCORER_SKINNY")) g_use_skinny = env[0] != '0';
   if (const char* env = getenv("DELS_PDL")) g_use_pdl = env[0] != '0';
+  if (const char* env = getenv("DELS_PAIR_KGROUP")) g_pair_kgroup = env[0] == '1' ? 1 : 2;
   int prev = -1;
   cudaError_t e = cudaGetDevice(&prev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -223,9 +226,12 @@ int init_device(int dev) {
     SET((tc_gemm_kernel<64, kStore, false>), TcConfig<64>::kSmemBytes);
     SET((tc_gemm_kernel<32, kStore, false>), TcConfig<32>::kSmemBytes);
     if (rc == DELS_OK && (e = f32_score_setup(kMaxSmem)) != cudaSuccess) rc = cuda_fail(e, "kernel setup: f32_score");
-    SET((tc_scorer_pair_kernel<false>), PairConfig::kSmemBytes);
-    SET((tc_scorer_pair_kernel<true>), PairConfig::kSmemBytes);
-    SET((tc_scorer_pair_kernel<false, true>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<false, false, 1>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<true, false, 1>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<false, true, 1>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<false, false, 2>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<true, false, 2>), PairConfig::kSmemBytes);
+    SET((tc_scorer_pair_kernel<false, true, 2>), PairConfig::kSmemBytes);
     SET((tc_skinny_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_gh_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_staged_kernel<16>), SkinnyConfig<16>::kSmemBytes);
@@ -256,7 +262,7 @@ int init_device(int dev) {
     cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
     cfg.blockDim = dim3(kTcThreads, 1, 1);
     cfg.dynamicSmemBytes = PairConfig::kSmemBytes;
-    e = cudaOccupancyMaxActiveClusters(&pairs, (const void*)tc_scorer_pair_kernel<false>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&pairs, (const void*)tc_scorer_pair_kernel<false, false, 1>, &cfg);
     if (e != cudaSuccess || pairs <= 0) {
       cudaGetLastError();
       pairs = 0;  // the paired scorer is not used on this device
@@ -443,8 +449,13 @@ int launch_scorer_pair(const TcOperands& op, TcArgs args, int max_pairs, cudaStr
   const long long want = tiles < max_pairs ? tiles * (args.tail_split > 1 ? args.tail_split : 1) : tiles;
   const int pairs = (int)(want < max_pairs ? want : max_pairs);
   if (pairs <= 0) return DELS_OK;
-  DELS_CHECK_PDL("tc_scorer_pair_kernel launch", launch_pdl(tc_scorer_pair_kernel<VB, STORE>, dim3(2 * pairs),
-      dim3(kTcThreads), PairConfig::kSmemBytes, st, ma0, mb0, ma1, mb1, mb0t, mb1t, args));
+  if (g_pair_kgroup == 2) {
+    DELS_CHECK_PDL("tc_scorer_pair_kernel launch", launch_pdl(tc_scorer_pair_kernel<VB, STORE, 2>,
+        dim3(2 * pairs), dim3(kTcThreads), PairConfig::kSmemBytes, st, ma0, mb0, ma1, mb1, mb0t, mb1t, args));
+  } else {
+    DELS_CHECK_PDL("tc_scorer_pair_kernel launch", launch_pdl(tc_scorer_pair_kernel<VB, STORE, 1>,
+        dim3(2 * pairs), dim3(kTcThreads), PairConfig::kSmemBytes, st, ma0, mb0, ma1, mb1, mb0t, mb1t, args));
+  }
   return DELS_OK;
 }
 
