@@ -776,8 +776,8 @@ def run_rnn(args, rank, world, dev):
 def runner_launches(runner, steps: int) -> int:
     """Kernels of libdels_b200.so one DeLSGraphRunner call launches (its graph replay)."""
     lm = 1 if hasattr(runner, "_lm_ws") else 0  # the long-logit GEMM of the materialising runner
-    if runner._overlap:  # gates + rank GEMV, scorer (with the next step's W_hh h)
-        return lm + 2 * steps
+    if runner._overlap:  # gates + rank GEMV, scorer (with the next step's W_hh h), keys decode
+        return lm + 2 * steps + 1
     if runner._split_gru:  # gates, rank GEMV, scorer (with the next step's W_hh h)
         return lm + 3 * steps
     if runner._tc:  # gates; per step rank GEMM + finalisation, scorer; W_hh GEMM (+ finalisation)
@@ -1048,7 +1048,8 @@ def run_domino(args, rank, world, dev):
                 "d2h_bytes_per_step": B * steps * 8},
         # z GEMM + finalisation, the prefix GRU steps, per step the correction layer and the
         # scorer, and a GRU update (or its gates alone) between steps unless the gates are fused
-        "gpu_launches": (2 + P + 2 * steps + (0 if runner._overlap else steps - 1)) * args.steps,
+        # (then one keys decode per call)
+        "gpu_launches": (2 + P + 2 * steps + (1 if runner._overlap else steps - 1)) * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
                      "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call},
         "clocks": clk,
