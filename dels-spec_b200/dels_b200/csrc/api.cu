@@ -232,8 +232,11 @@ int init_device(int dev) {
     SET((tc_scorer_pair_kernel<false, false, 2>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<true, false, 2>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<false, true, 2>), PairConfig::kSmemBytes);
+    SET((tc_skinny_kernel<16, 1>), SkinnyConfig<16>::kSmemBytes);
+    SET((tc_skinny_kernel<16, 4>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_kernel<16>), SkinnyConfig<16>::kSmemBytes);
-    SET((tc_skinny_gh_kernel<16>), SkinnyConfig<16>::kSmemBytes);
+    SET((tc_skinny_gh_kernel<16, 1>), SkinnyConfig<16>::kSmemBytes);
+    SET((tc_skinny_gh_kernel<16, kSkinnyGhMaxB>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_staged_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_kernel<32>), SkinnyConfig<32>::kSmemBytes);
     SET((tc_skinny_staged_kernel<32>), SkinnyConfig<32>::kSmemBytes);
@@ -245,8 +248,10 @@ int init_device(int dev) {
     SET(pack_rows_kernel, 0);
     SET(f32_rank_kernel, 0);
     SET(f32_transpose_pass_kernel, 0);
-    SET(gru_step_kernel, kMaxSmem);
-    SET(rank_gemv_kernel, kMaxSmem);
+    for (int rows_per_pass = 1; rows_per_pass <= kRunnerMaxB; rows_per_pass *= 2) {
+      SET(gru_step_kernel_for(rows_per_pass), kMaxSmem);
+      SET(rank_gemv_kernel_for(rows_per_pass), kMaxSmem);
+    }
     SET(linear_finalize_kernel, 0);
     SET(correction_finalize_kernel, 0);
     SET(gather_scaled_kernel, 0);
@@ -403,13 +408,21 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
   const int grid = tiles < sm_count ? tiles : sm_count;
   if (grid <= 0) return DELS_OK;
   if constexpr (GH) {
-    DELS_CHECK_PDL("tc_skinny_gh_kernel launch", launch_pdl(tc_skinny_gh_kernel<NB>, dim3(grid),
-        dim3(kSkinnyGhThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
+    // one-row rollouts get the epilogue and the helper GEMV compiled for one row
+    DELS_CHECK_PDL("tc_skinny_gh_kernel launch",
+        launch_pdl(args.m_rows <= 1 ? tc_skinny_gh_kernel<NB, 1> : tc_skinny_gh_kernel<NB, kSkinnyGhMaxB>, dim3(grid),
+                   dim3(kSkinnyGhThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
   } else if constexpr (SB) {
     DELS_CHECK_PDL("tc_skinny_staged_kernel launch", launch_pdl(tc_skinny_staged_kernel<NB>, dim3(grid),
         dim3(kTcThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, mbase, mprior, args));
   } else {
-    DELS_CHECK_PDL("tc_skinny_kernel launch", launch_pdl(tc_skinny_kernel<NB>, dim3(grid), dim3(kTcThreads),
+    // the 16-column kernel's epilogue compiled for the fewest rows that hold the batch (1, 4, 16)
+    auto kernel = tc_skinny_kernel<NB, NB>;
+    if constexpr (NB == 16) {
+      if (args.m_rows <= 1) kernel = tc_skinny_kernel<NB, 1>;
+      else if (args.m_rows <= 4) kernel = tc_skinny_kernel<NB, 4>;
+    }
+    DELS_CHECK_PDL("tc_skinny_kernel launch", launch_pdl(kernel, dim3(grid), dim3(kTcThreads),
         SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
   }
   return DELS_OK;
@@ -1036,8 +1049,9 @@ int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi
   int rc;
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;
-  DELS_CHECK_PDL("gru_step_kernel launch", launch_pdl(gru_step_kernel, dim3(cdiv(G, kGruCols)),
-      dim3(kGruThreads), gru_smem_bytes(G), reinterpret_cast<cudaStream_t>(stream),
+  const int rows_per_pass = runner_rows_per_pass(B);
+  DELS_CHECK_PDL("gru_step_kernel launch", launch_pdl(gru_step_kernel_for(rows_per_pass), dim3(cdiv(G, kGruCols)),
+      dim3(kGruThreads), gru_smem_bytes(G, rows_per_pass), reinterpret_cast<cudaStream_t>(stream),
       reinterpret_cast<const long long*>(tokens), tok_stride,
       reinterpret_cast<const __nv_bfloat16*>(gi_table), ld_table,
       reinterpret_cast<const __nv_bfloat16*>(w_hh), reinterpret_cast<const __nv_bfloat16*>(b_hh),
@@ -1089,8 +1103,9 @@ static int rank_gemv_common(const void* x, int64_t ld_x, const void* w, int64_t 
   if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
   if (B == 0) return DELS_OK;
   const int grid = cdiv(r, kGemvThreads / 32) < 2 * ds->sm_count ? cdiv(r, kGemvThreads / 32) : 2 * ds->sm_count;
-  DELS_CHECK_PDL("rank_gemv_kernel launch", launch_pdl(rank_gemv_kernel, dim3(grid), dim3(kGemvThreads),
-      rank_gemv_smem_bytes(K), reinterpret_cast<cudaStream_t>(stream),
+  const int rows_per_pass = runner_rows_per_pass(B);
+  DELS_CHECK_PDL("rank_gemv_kernel launch", launch_pdl(rank_gemv_kernel_for(rows_per_pass), dim3(grid),
+      dim3(kGemvThreads), rank_gemv_smem_bytes(K, rows_per_pass), reinterpret_cast<cudaStream_t>(stream),
       reinterpret_cast<const __nv_bfloat16*>(x), ld_x, reinterpret_cast<const __nv_bfloat16*>(w), ld_w,
       reinterpret_cast<const __nv_bfloat16*>(bias), reinterpret_cast<const __nv_bfloat16*>(addend),
       (long long)ld_add, B, K, r, activation, alpha, n_pos, row_pos, reinterpret_cast<__nv_bfloat16*>(s_out),

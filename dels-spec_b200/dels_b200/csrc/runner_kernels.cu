@@ -104,8 +104,9 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 }  // namespace
 
 // One CTA per kGruCols hidden units, one warp per gate row of those units (the CTA has
-// 3 * kGruCols warps); B rows in chunks of kRunnerMaxB.  Each warp loads its W_hh row
-// before h is staged, so the weight stream and the h gather overlap.
+// 3 * kGruCols warps); B rows in chunks of MAXB.  Each warp loads its W_hh row before h is
+// staged, so the weight stream and the h gather overlap.
+template <int MAXB>
 __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long long* __restrict__ tokens,
                                                                long long tok_stride,
                                                                const __nv_bfloat16* __restrict__ table,
@@ -115,8 +116,8 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
                                                                const __nv_bfloat16* h_in, __nv_bfloat16* h_out, int B,
                                                                int G, int V, int* status) {
   extern __shared__ uint4 smem4[];
-  __nv_bfloat16* hs = reinterpret_cast<__nv_bfloat16*>(smem4);     // [kRunnerMaxB][G]
-  float* gh_s = reinterpret_cast<float*>(hs + (size_t)kRunnerMaxB * G);  // [3][kGruCols][kRunnerMaxB]
+  __nv_bfloat16* hs = reinterpret_cast<__nv_bfloat16*>(smem4);  // [MAXB][G]
+  float* gh_s = reinterpret_cast<float*>(hs + (size_t)MAXB * G);  // [3][kGruCols][MAXB]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g0 = blockIdx.x * kGruCols;
   // this warp's gate row: gate = warp / kGruCols, unit g0 + warp % kGruCols
@@ -126,8 +127,8 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
   RowPrefetch pre;
   if (has_row) row_prefetch(wrow, G, lane, pre);  // weights only: safe before the wait
   pdl_wait();
-  for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
-    const int nb = min(kRunnerMaxB, B - b0);
+  for (int b0 = 0; b0 < B; b0 += MAXB) {
+    const int nb = min(MAXB, B - b0);
     __syncthreads();
     // stage h_in rows (zeros when h_in is NULL: the rollout's initial state)
     for (int e = threadIdx.x; e < nb * G / 8; e += blockDim.x) {
@@ -139,12 +140,14 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
     __syncthreads();
     // gh for the gate row {g, G + g, 2G + g} this warp owns
     if (has_row) {
-      float acc[kRunnerMaxB];
-      warp_row_dots<kRunnerMaxB>(pre, wrow, hs, G, nb, G, lane, acc);
+      float acc[MAXB];
+      warp_row_dots<MAXB>(pre, wrow, hs, G, nb, G, lane, acc);
       if (lane == 0) {
         const int g = g0 + c_w;
         const float bias = b_hh != nullptr ? __bfloat162float(b_hh[gate * G + g]) : 0.0f;
-        for (int b = 0; b < nb; ++b) gh_s[(gate * kGruCols + c_w) * kRunnerMaxB + b] = bf16r(acc[b] + bias);
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b)
+          if (b < nb) gh_s[(gate * kGruCols + c_w) * MAXB + b] = bf16r(acc[b] + bias);
       }
     }
     __syncthreads();
@@ -161,9 +164,9 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
       const float gi_r = __bfloat162float(gi[g]);
       const float gi_z = __bfloat162float(gi[G + g]);
       const float gi_n = __bfloat162float(gi[2 * G + g]);
-      const float gh_r = gh_s[(0 * kGruCols + c) * kRunnerMaxB + b];
-      const float gh_z = gh_s[(1 * kGruCols + c) * kRunnerMaxB + b];
-      const float gh_n = gh_s[(2 * kGruCols + c) * kRunnerMaxB + b];
+      const float gh_r = gh_s[(0 * kGruCols + c) * MAXB + b];
+      const float gh_z = gh_s[(1 * kGruCols + c) * MAXB + b];
+      const float gh_n = gh_s[(2 * kGruCols + c) * MAXB + b];
       const float h = __bfloat162float(hs[(size_t)b * G + g]);
       h_out[(long long)(b0 + b) * G + g] = __float2bfloat16_rn(gru_unit(gi_r, gi_z, gi_n, gh_r, gh_z, gh_n, h));
     }
@@ -174,21 +177,22 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
 // One warp per output feature j (grid-stride), all B rows at once.  The warp's first
 // weight row is loaded before x is staged.  With `addend` (the Domino correction MLP)
 // the output is SiLU(addend + bf16(W x)) in fp32 instead of the rank activation.
+template <int MAXB>
 __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
     const __nv_bfloat16* __restrict__ x, long long ld_x, const __nv_bfloat16* __restrict__ w, long long ld_w,
     const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ addend, long long ld_add, int B,
     int K, int r, int activation, const float* __restrict__ alpha, int n_pos, const int* __restrict__ row_pos,
     __nv_bfloat16* s_out, __nv_bfloat16* s_scaled, long long* keys, unsigned* counter, const GruGateSrc gate) {
   extern __shared__ uint4 smem4[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);  // [kRunnerMaxB][K]
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);  // [MAXB][K]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
   const int nwarps = gridDim.x * (blockDim.x >> 5);
   RowPrefetch first;
   if (gwarp < r) row_prefetch(w + (long long)gwarp * ld_w, K, lane, first);  // weights only
   pdl_wait();
-  for (int b0 = 0; b0 < B; b0 += kRunnerMaxB) {
-    const int nb = min(kRunnerMaxB, B - b0);
+  for (int b0 = 0; b0 < B; b0 += MAXB) {
+    const int nb = min(MAXB, B - b0);
     __syncthreads();
     if (gate.table != nullptr) {
       // x = the GRU's new hidden state (K = G units), eight units per thread: every CTA
@@ -242,12 +246,12 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
       } else {
         row_prefetch(wrow, K, lane, pre);
       }
-      float acc[kRunnerMaxB];
-      warp_row_dots<kRunnerMaxB>(pre, wrow, xs, K, nb, K, lane, acc);
+      float acc[MAXB];
+      warp_row_dots<MAXB>(pre, wrow, xs, K, nb, K, lane, acc);
       if (lane < nb) {
         float a = 0.0f;
 #pragma unroll
-        for (int b = 0; b < kRunnerMaxB; ++b)
+        for (int b = 0; b < MAXB; ++b)
           if (b == lane) a = acc[b];
         const int row = b0 + lane;
         const float bj = bias != nullptr ? __bfloat162float(bias[j]) : 0.0f;
@@ -270,6 +274,29 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
   }
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
   pdl_trigger();
+}
+
+// Rows per shared-memory pass: the compile-time row count of the dot-product loops.  Rows
+// past the batch are skipped under a predicate, and predicated-off FMAs still take issue
+// slots, so a batch-1 rollout compiled for 16 rows would issue 16x the arithmetic it needs.
+GruStepKernel gru_step_kernel_for(int rows_per_pass) {
+  switch (rows_per_pass) {
+    case 1: return gru_step_kernel<1>;
+    case 2: return gru_step_kernel<2>;
+    case 4: return gru_step_kernel<4>;
+    case 8: return gru_step_kernel<8>;
+    default: return gru_step_kernel<kRunnerMaxB>;
+  }
+}
+
+RankGemvKernel rank_gemv_kernel_for(int rows_per_pass) {
+  switch (rows_per_pass) {
+    case 1: return rank_gemv_kernel<1>;
+    case 2: return rank_gemv_kernel<2>;
+    case 4: return rank_gemv_kernel<4>;
+    case 8: return rank_gemv_kernel<8>;
+    default: return rank_gemv_kernel<kRunnerMaxB>;
+  }
 }
 
 // The GRU gates for batches where gh = bf16(W_hh h + b_hh) came from the tensor-core

@@ -33,7 +33,7 @@ namespace dels {
 
 constexpr int kSkinnyBM = 128;  // vocab rows per tile (MMA M)
 constexpr int kSkinnyGhThreads = kTcThreads + 64;  // + two helper warps (tc_skinny_gh_kernel)
-constexpr int kSkinnyGhMaxB = 4;                   // rows of the helpers' GEMV
+constexpr int kSkinnyGhMaxB = 4;                   // most rows of the helpers' GEMV
 
 template <int NB>
 struct SkinnyConfig {
@@ -60,8 +60,10 @@ struct SkinnyConfig {
 // `map_base` = base logits [rows, V slice] in 128 x NB boxes (when args.base is set) and
 // `map_prior` = the prior [V slice] fp32 in 128-element boxes (when args.prior is set).
 // GH: warps 6 and 7 compute args.gh_out (the next rollout step's W_hh h), one output row
-// per warp at a time over a grid-wide stride, while warps 0-5 score.
-template <int NB, bool STAGE, bool GH = false>
+// per warp at a time over a grid-wide stride, while warps 0-5 score.  RB (<= NB) bounds
+// the rows the epilogue scores at compile time: the MMA still computes NB columns, but a
+// batch-1 step does not issue (predicated-off) epilogue arithmetic for the other 15.
+template <int NB, bool STAGE, bool GH = false, int GHB = kSkinnyGhMaxB, int RB = NB>
 __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUtensorMap* map_b0,
                                             const CUtensorMap* map_a1, const CUtensorMap* map_b1,
                                             const CUtensorMap* map_base, const CUtensorMap* map_prior,
@@ -293,28 +295,28 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
   } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp can access
-    const int nrows = m_rows < NB ? m_rows : NB;
-    float negb[NB];
+    const int nrows = m_rows < RB ? m_rows : RB;
+    float negb[RB];
 #pragma unroll
-    for (int b = 0; b < NB; ++b)
+    for (int b = 0; b < RB; ++b)
       negb[b] = (b < nrows && args.prior != nullptr) ? -__ldg(&args.beta[row_position(args.row_pos, b, args.n_pos)])
                                                      : 0.0f;
-    long long run[NB];
+    long long run[RB];
 #pragma unroll
-    for (int b = 0; b < NB; ++b) run[b] = kKeyEmpty;
+    for (int b = 0; b < RB; ++b) run[b] = kKeyEmpty;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int vt = quad * 32 + lane;  // this thread's row within the tile
       const int v = t * kSkinnyBM + vt;  // ... and within the vocab slice
       const bool v_ok = v < args.n_cols;
-      float bv[NB];
+      float bv[RB];
       float pv = 0.0f;
       if (!STAGE) {
         // loaded directly, before the accumulator wait so the latency overlaps the MMAs
         pv = (v_ok && args.prior != nullptr) ? __ldg(args.prior + v) : 0.0f;
 #pragma unroll
-        for (int b = 0; b < NB; ++b)
+        for (int b = 0; b < RB; ++b)
           bv[b] = (v_ok && args.base != nullptr && b < nrows)
                       ? __bfloat162float(args.base[(long long)b * args.ld_base + v])
                       : 0.0f;
@@ -324,10 +326,10 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
       if (stage_base) {
         const __nv_bfloat16* bs = reinterpret_cast<const __nv_bfloat16*>(eb);
 #pragma unroll
-        for (int b = 0; b < NB; ++b) bv[b] = __bfloat162float(bs[b * kSkinnyBM + vt]);
+        for (int b = 0; b < RB; ++b) bv[b] = __bfloat162float(bs[b * kSkinnyBM + vt]);
       } else if (STAGE) {
 #pragma unroll
-        for (int b = 0; b < NB; ++b) bv[b] = 0.0f;
+        for (int b = 0; b < RB; ++b) bv[b] = 0.0f;
       }
       if (stage_prior) pv = reinterpret_cast<const float*>(eb + Cfg::kEpiBaseBytes)[vt];
       if (stage_epi) mbar_arrive(eempty_bar(acc));
@@ -346,7 +348,7 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
       if (v_ok) {
         const uint32_t vidx = (uint32_t)(args.v_begin + v);
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
+        for (int b = 0; b < RB; ++b) {
           if (b < nrows) {
             float sc = __uint_as_float(d[b]) + bv[b];
             sc = fmaf(negb[b], pv, sc);
@@ -363,7 +365,7 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
     }
     // Per row: maximum over the warp's lanes, then over the four epilogue warps.
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
+    for (int b = 0; b < RB; ++b) {
       if (b < nrows) {
         long long k = run[b];
 #pragma unroll
@@ -393,18 +395,19 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
     if (args.gh_out != nullptr) {
       // A warp takes rows hw, hw + nhw, ... in groups of kRows; each lane loads its 16-byte
       // pieces of all the group's rows (up to 4 x 32 pieces per row per pass) before any
-      // arithmetic, so a group costs one memory round trip instead of one per row.
+      // arithmetic, so a group costs one memory round trip instead of one per row.  The
+      // row loop is compiled for GHB rows (predicated-off FMAs still take issue slots).
       constexpr int kRows = 4, kPieces = 4;
-      const int nb = args.gh_b < kSkinnyGhMaxB ? args.gh_b : kSkinnyGhMaxB;
+      const int nb = args.gh_b < GHB ? args.gh_b : GHB;
       const int k8n = args.gh_k / 8;
       const int hw = (int)blockIdx.x * 2 + (warp - 6);
       const int nhw = (int)gridDim.x * 2;
       for (int j0 = hw; j0 < args.gh_rows; j0 += nhw * kRows) {
-        float acc[kRows][kSkinnyGhMaxB];
+        float acc[kRows][GHB];
 #pragma unroll
         for (int g = 0; g < kRows; ++g)
 #pragma unroll
-          for (int b = 0; b < kSkinnyGhMaxB; ++b) acc[g][b] = 0.0f;
+          for (int b = 0; b < GHB; ++b) acc[g][b] = 0.0f;
         for (int c0 = 0; c0 < k8n; c0 += 32 * kPieces) {
           uint4 w[kRows][kPieces];
 #pragma unroll
@@ -419,7 +422,7 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
             }
           }
 #pragma unroll
-          for (int b = 0; b < kSkinnyGhMaxB; ++b) {
+          for (int b = 0; b < GHB; ++b) {
             if (b < nb) {
 #pragma unroll
               for (int q = 0; q < kPieces; ++q) {
@@ -449,7 +452,7 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
         for (int g = 0; g < kRows; ++g) {
           const int j = j0 + g * nhw;
 #pragma unroll
-          for (int b = 0; b < kSkinnyGhMaxB; ++b) {
+          for (int b = 0; b < GHB; ++b) {
             float a = acc[g][b];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
@@ -493,21 +496,22 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
 
 // Two entry points over the same body: the staged one takes the two epilogue-operand maps
 // as well; the plain one keeps its parameter block at the four operand maps.
-template <int NB>
+template <int NB, int RB = NB>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_skinny_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                      const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
                      const TcArgs args) {
-  skinny_body<NB, false>(&map_a0, &map_b0, &map_a1, &map_b1, nullptr, nullptr, args);
+  skinny_body<NB, false, false, kSkinnyGhMaxB, RB>(&map_a0, &map_b0, &map_a1, &map_b1, nullptr, nullptr, args);
 }
 
-// The plain scorer plus the helper warps that compute the next rollout step's gh.
-template <int NB>
+// The plain scorer plus the helper warps that compute the next rollout step's gh, both for
+// up to GHB rows.
+template <int NB, int GHB>
 __global__ void __launch_bounds__(kSkinnyGhThreads, 1)
     tc_skinny_gh_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                         const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
                         const TcArgs args) {
-  skinny_body<NB, false, true>(&map_a0, &map_b0, &map_a1, &map_b1, nullptr, nullptr, args);
+  skinny_body<NB, false, true, GHB, GHB>(&map_a0, &map_b0, &map_a1, &map_b1, nullptr, nullptr, args);
 }
 
 template <int NB>
