@@ -232,13 +232,13 @@ int init_device(int dev) {
     SET((tc_scorer_pair_kernel<false, false, 2>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<true, false, 2>), PairConfig::kSmemBytes);
     SET((tc_scorer_pair_kernel<false, true, 2>), PairConfig::kSmemBytes);
-    SET((tc_skinny_kernel<16, 1>), SkinnyConfig<16>::kSmemBytes);
-    SET((tc_skinny_kernel<16, 4>), SkinnyConfig<16>::kSmemBytes);
-    SET((tc_skinny_kernel<16>), SkinnyConfig<16>::kSmemBytes);
-    SET((tc_skinny_gh_kernel<16, 1>), SkinnyConfig<16>::kSmemBytes);
-    SET((tc_skinny_gh_kernel<16, kSkinnyGhMaxB>), SkinnyConfig<16>::kSmemBytes);
+    SET((tc_skinny_kernel<16, 1>), (SkinnyConfig<16, false>::kSmemBytes));
+    SET((tc_skinny_kernel<16, 4>), (SkinnyConfig<16, false>::kSmemBytes));
+    SET((tc_skinny_kernel<16>), (SkinnyConfig<16, false>::kSmemBytes));
+    SET((tc_skinny_gh_kernel<16, 1>), (SkinnyConfig<16, false>::kSmemBytes));
+    SET((tc_skinny_gh_kernel<16, kSkinnyGhMaxB>), (SkinnyConfig<16, false>::kSmemBytes));
     SET((tc_skinny_staged_kernel<16>), SkinnyConfig<16>::kSmemBytes);
-    SET((tc_skinny_kernel<32>), SkinnyConfig<32>::kSmemBytes);
+    SET((tc_skinny_kernel<32>), (SkinnyConfig<32, false>::kSmemBytes));
     SET((tc_skinny_staged_kernel<32>), SkinnyConfig<32>::kSmemBytes);
     SET(rnn_recurrence_kernel, kMaxSmem);
     SET(rank_finalize_kernel, 0);
@@ -411,7 +411,7 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
     // one-row rollouts get the epilogue and the helper GEMV compiled for one row
     DELS_CHECK_PDL("tc_skinny_gh_kernel launch",
         launch_pdl(args.m_rows <= 1 ? tc_skinny_gh_kernel<NB, 1> : tc_skinny_gh_kernel<NB, kSkinnyGhMaxB>, dim3(grid),
-                   dim3(kSkinnyGhThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
+                   dim3(kSkinnyGhThreads), SkinnyConfig<NB, false>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
   } else if constexpr (SB) {
     DELS_CHECK_PDL("tc_skinny_staged_kernel launch", launch_pdl(tc_skinny_staged_kernel<NB>, dim3(grid),
         dim3(kTcThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, mbase, mprior, args));
@@ -423,7 +423,7 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
       else if (args.m_rows <= 4) kernel = tc_skinny_kernel<NB, 4>;
     }
     DELS_CHECK_PDL("tc_skinny_kernel launch", launch_pdl(kernel, dim3(grid), dim3(kTcThreads),
-        SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
+        SkinnyConfig<NB, false>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
   }
   return DELS_OK;
 }

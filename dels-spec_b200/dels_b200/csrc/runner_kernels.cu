@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
   RowPrefetch pre;
   if (has_row) row_prefetch(wrow, G, lane, pre);  // weights only: safe before the wait
   pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
   for (int b0 = 0; b0 < B; b0 += MAXB) {
     const int nb = min(MAXB, B - b0);
     __syncthreads();
@@ -171,7 +172,6 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
       h_out[(long long)(b0 + b) * G + g] = __float2bfloat16_rn(gru_unit(gi_r, gi_z, gi_n, gh_r, gh_z, gh_n, h));
     }
   }
-  pdl_trigger();
 }
 
 // One warp per output feature j (grid-stride), all B rows at once.  The warp's first
@@ -191,6 +191,10 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
   RowPrefetch first;
   if (gwarp < r) row_prefetch(w + (long long)gwarp * ld_w, K, lane, first);  // weights only
   pdl_wait();
+  // The next kernel (the rollout step's scorer) may launch now: its weight prefetch runs
+  // before its own wait, so the Vr stream overlaps the gates and the projection below
+  // (batch-1 runner call -6 %).  It reads what this kernel writes only after that wait.
+  pdl_trigger();
   for (int b0 = 0; b0 < B; b0 += MAXB) {
     const int nb = min(MAXB, B - b0);
     __syncthreads();
@@ -273,7 +277,6 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
     for (int i = threadIdx.x; i < B; i += blockDim.x) keys[i] = kKeyEmpty;
   }
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
-  pdl_trigger();
 }
 
 // Rows per shared-memory pass: the compile-time row count of the dot-product loops.  Rows
@@ -307,6 +310,7 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
                                  const __nv_bfloat16* __restrict__ gh, long long ld_gh, const __nv_bfloat16* h_in,
                                  __nv_bfloat16* h_out, int B, int G, int V, int* status) {
   pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < (long long)B * G;
        e += (long long)gridDim.x * blockDim.x) {
     const int b = (int)(e / G), g = (int)(e % G);
@@ -322,7 +326,6 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
         gru_unit(__bfloat162float(gi[g]), __bfloat162float(gi[G + g]), __bfloat162float(gi[2 * G + g]),
                  __bfloat162float(ghb[g]), __bfloat162float(ghb[G + g]), __bfloat162float(ghb[2 * G + g]), h));
   }
-  pdl_trigger();
 }
 
 __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride,
@@ -330,6 +333,7 @@ __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long 
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter, int* status) {
   pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < B * r; e += gridDim.x * blockDim.x) {
     const int b = e / r, j = e % r;
     long long tok = tokens[(long long)b * tok_stride];
@@ -342,7 +346,6 @@ __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long 
     if (keys != nullptr && j == 0) keys[b] = kKeyEmpty;
   }
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
-  pdl_trigger();
 }
 
 }  // namespace dels

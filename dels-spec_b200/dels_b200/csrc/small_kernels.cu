@@ -23,6 +23,7 @@ __global__ void rank_finalize_kernel(const float* __restrict__ partials, int spl
                                      int n_pos, const int* __restrict__ row_pos, __nv_bfloat16* s_out,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter) {
   pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
   const long long total = (long long)rows * r;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -52,6 +53,7 @@ __global__ void correction_finalize_kernel(const float* __restrict__ partials, i
                                            long long ld_z, const float* __restrict__ alpha, __nv_bfloat16* s_scaled,
                                            long long* keys, unsigned* counter) {
   pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
   const long long total = (long long)rows * m;
   const float a = alpha != nullptr ? alpha[0] : 1.0f;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -66,7 +68,6 @@ __global__ void correction_finalize_kernel(const float* __restrict__ partials, i
     if (keys != nullptr && col == 0) keys[row] = kKeyEmpty;
   }
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;
-  pdl_trigger();
 }
 
 // -----------------------------------------------------------------------------------
@@ -78,6 +79,7 @@ __global__ void linear_finalize_kernel(const float* __restrict__ partials, int s
                                        long long ld_part, int rows, int n, const __nv_bfloat16* __restrict__ bias,
                                        __nv_bfloat16* out, long long ld_out) {
   pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
   const long long total = (long long)rows * n;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -89,11 +91,11 @@ __global__ void linear_finalize_kernel(const float* __restrict__ partials, int s
     if (bias != nullptr) acc += __bfloat162float(bias[col]);
     out[(long long)row * ld_out + col] = __float2bfloat16_rn(acc);
   }
-  pdl_trigger();
 }
 
 __global__ void keys_init_kernel(long long* keys, int rows, unsigned* counter) {
   pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x)
     keys[i] = kKeyEmpty;
   if (counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;

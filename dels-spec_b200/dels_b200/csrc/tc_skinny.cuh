@@ -35,7 +35,9 @@ constexpr int kSkinnyBM = 128;  // vocab rows per tile (MMA M)
 constexpr int kSkinnyGhThreads = kTcThreads + 64;  // + two helper warps (tc_skinny_gh_kernel)
 constexpr int kSkinnyGhMaxB = 4;                   // most rows of the helpers' GEMV
 
-template <int NB>
+// STAGE = false (the plain variant) leaves out the epilogue-operand buffers.  More stages
+// for it (12 at NB = 16) measured slower in the batch-1 rollout.
+template <int NB, bool STAGE = true>
 struct SkinnyConfig {
   static_assert(NB == 16 || NB == 32, "NB is 16 or 32");
   static constexpr int kABytes = kSkinnyBM * kBK * 2;  // vocab tile: 128 x 64 bf16
@@ -47,7 +49,7 @@ struct SkinnyConfig {
   static constexpr int kEpiBaseBytes = NB * kSkinnyBM * 2;
   static constexpr int kEpiPriorBytes = kSkinnyBM * 4;
   static constexpr int kEpiOffset = kStages * (kABytes + kBBytes);
-  static constexpr int kBarOffset = kEpiOffset + kAcc * (kEpiBaseBytes + kEpiPriorBytes);
+  static constexpr int kBarOffset = kEpiOffset + (STAGE ? kAcc * (kEpiBaseBytes + kEpiPriorBytes) : 0);
   static constexpr int kNumBars = 2 * kStages + 4 * kAcc;
   static constexpr int kRedOffset = kBarOffset + kNumBars * 8 + 16;
   static constexpr int kSmemBytes = kRedOffset + 4 * NB * 8 + 1024;
@@ -68,7 +70,7 @@ __device__ __forceinline__ void skinny_body(const CUtensorMap* map_a0, const CUt
                                             const CUtensorMap* map_a1, const CUtensorMap* map_b1,
                                             const CUtensorMap* map_base, const CUtensorMap* map_prior,
                                             const TcArgs& args) {
-  using Cfg = SkinnyConfig<NB>;
+  using Cfg = SkinnyConfig<NB, STAGE>;
   constexpr int S = Cfg::kStages;
   constexpr int NA = Cfg::kAcc;
   extern __shared__ uint8_t smem_raw[];
