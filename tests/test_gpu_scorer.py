@@ -64,6 +64,10 @@ SHAPES = [
     (16, 256, 64, 4099, 16, "identity", True),
     (1, 128, 64, 1000, 1, "identity", True),
     (24, 256, 64, 5003, 8, "silu", True),
+    # at most 4 rows with a long K (17 K blocks) over 157 vocabulary tiles on 148 CTAs:
+    # a partial last wave and a partial last tile
+    (1, 1024, 64, 20000, 1, "identity", True),
+    (3, 1024, 64, 20000, 4, "silu", True),
     # 33..128 rows: one 128-row tile; more: CTA pairs
     (48, 320, 96, 2347, 16, "identity", True),
     (130, 320, 96, 2347, 8, "silu", True),
