@@ -935,7 +935,8 @@ def run_runner(args, rank, world, dev):
         "gpu_launches": runner_launches(runner, steps) * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
                      "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call,
-                     "note": "Vr (77.8 MB) can stay L2-resident across the 14 steps, so this bound can be beaten"},
+                     "note": "every step reads Vr (77.8 MB) and W_hh from HBM: the 126 MB L2 does not keep "
+                             "Vr across steps under any cache policy measured"},
         "clocks": clk,
     }
     if extra:
