@@ -700,7 +700,7 @@ def run_ragged(args, rank, world, dev):
     ms_main = timed(main, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0) / args.steps
     ws.check()
     achieved = flops / (ms_main * 1e-3) / 1e12
-    return {
+    res = {
         "metric": METRIC, "value": total * args.steps / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -715,6 +715,13 @@ def run_ragged(args, rank, world, dev):
                      "frac_of_burst_peak": achieved / pk_tflops, "kernel_ms": ms_main},
         "clocks": clk,
     }
+    if not args.no_cpu_baseline:
+        nrows = 24
+        rps, cores = reference_rows_per_s(*ragged_sample(wl, nrows), reps=2)
+        res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
+                               "sample": f"the first {nrows} accepted rows (acceptance computed on the host) x "
+                                         f"full vocabulary x 2 repetitions, bf16 torch on the host"}
+    return res
 
 
 def run_rnn(args, rank, world, dev):
@@ -757,7 +764,7 @@ def run_rnn(args, rank, world, dev):
     ws.check()
     flops = 2.0 * rows * wl.V * (wl.H + wl.r)
     achieved = flops / (ms_main * 1e-3) / 1e12
-    return {
+    res = {
         "metric": METRIC, "value": rows * args.steps / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -771,6 +778,13 @@ def run_rnn(args, rank, world, dev):
                      "frac_of_burst_peak": achieved / pk_tflops, "kernel_ms": ms_main},
         "clocks": clk,
     }
+    if not args.no_cpu_baseline:
+        sample_t, rnn = rnn_sample(wl, 2)
+        rps, cores = reference_rows_per_s(*sample_t, reps=2, rnn=rnn)
+        res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
+                               "sample": "2 sequences x 16 positions through the RNN head x full vocabulary x 2 "
+                                         "repetitions, bf16 torch on the host"}
+    return res
 
 
 def runner_launches(runner, steps: int) -> int:

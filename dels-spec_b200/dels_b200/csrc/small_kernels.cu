@@ -235,11 +235,26 @@ __global__ void __launch_bounds__(256) rnn_recurrence_kernel(
   const int i = threadIdx.x;
   const int seq0 = blockIdx.x * kRnnSeqs;
 
-  for (int e = threadIdx.x; e < (r / 2) * r; e += blockDim.x) {
-    const int jp = e / r, ii = e % r;
-    const uint16_t lo = reinterpret_cast<const uint16_t*>(w_s)[(long long)ii * r + 2 * jp];
-    const uint16_t hi = reinterpret_cast<const uint16_t*>(w_s)[(long long)ii * r + 2 * jp + 1];
-    wt2[e] = (uint32_t)lo | ((uint32_t)hi << 16);
+  // Thread ii copies row ii of W_s: its (j, j+1) pairs are the row's 32-bit words, read 16
+  // bytes at a time and written to wt2[jp][ii] (consecutive threads, consecutive banks).
+  if ((r % 8) == 0 && (reinterpret_cast<uintptr_t>(w_s) & 15u) == 0) {
+    for (int ii = threadIdx.x; ii < r; ii += blockDim.x) {
+      const uint4* row = reinterpret_cast<const uint4*>(w_s + (long long)ii * r);
+      for (int c = 0; c < r / 8; ++c) {
+        const uint4 v = __ldg(row + c);
+        wt2[(4 * c + 0) * r + ii] = v.x;
+        wt2[(4 * c + 1) * r + ii] = v.y;
+        wt2[(4 * c + 2) * r + ii] = v.z;
+        wt2[(4 * c + 3) * r + ii] = v.w;
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < (r / 2) * r; e += blockDim.x) {
+      const int jp = e / r, ii = e % r;
+      const uint16_t lo = reinterpret_cast<const uint16_t*>(w_s)[(long long)ii * r + 2 * jp];
+      const uint16_t hi = reinterpret_cast<const uint16_t*>(w_s)[(long long)ii * r + 2 * jp + 1];
+      wt2[e] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
   }
   for (int e = threadIdx.x; e < kRnnSeqs * r; e += blockDim.x) state[e] = 0.0f;
   if (keys != nullptr) {
@@ -253,6 +268,21 @@ __global__ void __launch_bounds__(256) rnn_recurrence_kernel(
 
   const float b_i = (bias != nullptr && i < r) ? bias[i] : 0.0f;
   for (int t = 0; t < T; ++t) {
+    // This step's input projection: the first kPreAhead split-K partials of every
+    // sequence are loaded as independent loads before the recurrent dot products and
+    // summed after them (in split order), so one L2 round trip overlaps the dot products
+    // instead of a chain of dependent ones per split.
+    constexpr int kPreAhead = 4;
+    const float a_t = alpha != nullptr ? alpha[t] : 1.0f;
+    float pv[kRnnSeqs][kPreAhead];
+#pragma unroll
+    for (int q = 0; q < kRnnSeqs; ++q) {
+      const int seq = seq0 + q;
+      const bool ok = i < r && seq < n_seq;
+      const long long off = ((long long)seq * T + t) * ld_pre + i;
+#pragma unroll
+      for (int j = 0; j < kPreAhead; ++j) pv[q][j] = (ok && j < splits) ? pre[j * split_stride + off] : 0.0f;
+    }
     float g[kRnnSeqs];
 #pragma unroll
     for (int q = 0; q < kRnnSeqs; ++q) g[q] = 0.0f;
@@ -271,17 +301,19 @@ __global__ void __launch_bounds__(256) rnn_recurrence_kernel(
     }
     __syncthreads();  // everyone has read s_{t-1}
     if (i < r) {
-      const float a = alpha != nullptr ? alpha[t] : 1.0f;
 #pragma unroll
       for (int q = 0; q < kRnnSeqs; ++q) {
         const int seq = seq0 + q;
         if (seq < n_seq) {
           const long long row = (long long)seq * T + t;
           float p = 0.0f;
-          for (int s = 0; s < splits; ++s) p += pre[s * split_stride + row * ld_pre + i];
+#pragma unroll
+          for (int j = 0; j < kPreAhead; ++j)
+            if (j < splits) p += pv[q][j];
+          for (int sp = kPreAhead; sp < splits; ++sp) p += pre[sp * split_stride + row * ld_pre + i];
           const float st = tanhf(p + g[q] + b_i);
           state[q * r + i] = st;
-          s_scaled[row * r + i] = __float2bfloat16_rn(a * st);
+          s_scaled[row * r + i] = __float2bfloat16_rn(a_t * st);
           if (s_out != nullptr) s_out[row * r + i] = __float2bfloat16_rn(st);
         }
       }

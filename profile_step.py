@@ -8,7 +8,9 @@ name it); ``bench.py`` is the timing entry, this one only launches.
 ``--kernel scorer`` launches the fused tcgen05 scorer, each call after a small
 keys-reset kernel (the scorer's epilogue skips chunks below the row's best key so far,
 so every profiled launch starts from empty keys); ``--kernel step`` runs whole draft-scoring steps
-(projection + finalisation + scorer); ``--kernel f32`` runs the fp32 scorer step.
+(projection + finalisation + scorer); ``--kernel f32`` runs the fp32 scorer step;
+``--kernel rnn`` (cfg4) runs the RNN head's rank states alone (input projection +
+recurrence) over a 2048-token vocabulary, so that nothing but the head is resident.
 All inputs are generated and the rank operand computed before the first profiled
 launch, so with ``ncu -k regex:<name> -s <launches-1> -c 1`` the capture is a single
 warm launch of that kernel.
@@ -33,15 +35,17 @@ from dels_b200 import ops, workloads  # noqa: E402
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg5", "cfg4"])
-    ap.add_argument("--kernel", default="scorer", choices=["scorer", "step", "f32"])
+    ap.add_argument("--kernel", default="scorer", choices=["scorer", "step", "f32", "rnn"])
     ap.add_argument("--launches", type=int, default=4)
     ap.add_argument("--rows", type=int, default=0, help="override the row count (cfg5)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     ops.init(dev)
+    if args.kernel == "rnn" and args.workload != "cfg4":
+        raise SystemExit("--kernel rnn needs --workload cfg4")
     if args.workload == "cfg4":
-        wl = workloads.cfg4(device=dev)
+        wl = workloads.cfg4(device=dev, V=2048) if args.kernel == "rnn" else workloads.cfg4(device=dev)
         t = wl.tensors
         s_scaled, _ = ops.rnn_rank_states(t["x"], t["w_in"], t["w_s"], t["bias"], t["alpha"], n_seq=512, T=16)
         h = t["x"]
@@ -62,6 +66,9 @@ def main() -> None:
         if args.kernel == "scorer":
             ops.fused_argmax_bf16(h, t["W"], s_scaled, t["Vr"], t["prior"], t["beta"], n_pos=wl.n_pos,
                                   keys_ready=False, out=out, ws=ws)
+        elif args.kernel == "rnn":
+            ops.rnn_rank_states(t["x"], t["w_in"], t["w_s"], t["bias"], t["alpha"], n_seq=512, T=16,
+                                s_scaled=s_scaled, keys=out.keys, ws=ws)
         elif args.kernel == "step":
             ops.draft_score_bf16(h, t["W"], t["w_rank"], t["Vr"], t["prior"], t["alpha"], t["beta"], n_pos=wl.n_pos,
                                  out=out, ws=ws)

@@ -111,6 +111,23 @@ def test_rnn_states_match_oracle(cuda_device):
     _check(out.tokens.cpu().numpy(), out.scores.cpu().numpy(), sc)
 
 
+@pytest.mark.parametrize("n_seq,T,H,r", [(6, 7, 200, 62), (2, 5, 2048, 64)], ids=["odd_rank", "8_splits"])
+def test_rnn_states_small_shapes_match_oracle(cuda_device, n_seq, T, H, r):
+    """A rank that is not a multiple of 8 (W_s staged by 2-byte loads, not 16-byte rows)
+    with a sequence count that leaves the last CTA partly empty; and 10 rows over a long
+    K, where the input projection runs as 8 split-K partials (more than the recurrence
+    loads ahead of its dot products)."""
+    from dels_b200 import ops, workloads
+
+    wl = workloads.cfg4(device=cuda_device, V=512, n_seq=n_seq, T=T, H=H, r=r)
+    t = wl.tensors
+    s_scaled, s = ops.rnn_rank_states(t["x"], t["w_in"], t["w_s"], t["bias"], t["alpha"], n_seq=n_seq, T=T,
+                                      want_state=True)
+    f = lambda x: x.float().cpu().numpy()  # noqa: E731
+    ref = O.rnn_states(f(t["x"]), f(t["w_in"]), f(t["w_s"]), f(t["bias"]), n_seq, T)
+    np.testing.assert_allclose(f(s), ref, rtol=2 ** -7, atol=2e-3)
+
+
 def _torch_scores(h, W, s_scaled, Vr, prior, beta_rows, chunk=32768):
     """fp32 reference scores on the GPU (TF32 off), chunked over the vocabulary."""
     prev = torch.backends.cuda.matmul.allow_tf32
