@@ -204,6 +204,14 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
       for (int e = threadIdx.x; e < nb * K / 8; e += blockDim.x) {
         const int b = e / (K / 8), k8 = e % (K / 8);
         const int row = b0 + b;
+        const int G8 = K / 8;  // uint4 per gate block
+        // gh and h do not depend on the token: their loads go out together with the token's
+        // (one L2 round trip), ahead of the table row that the token selects
+        const uint4* gh = reinterpret_cast<const uint4*>(gate.gh + (long long)row * gate.ld_gh) + k8;
+        const uint4 hr = gh[0], hz = gh[G8], hn = gh[2 * G8];
+        const uint4 hp = gate.h_in != nullptr
+                             ? *(reinterpret_cast<const uint4*>(gate.h_in + (long long)row * K) + k8)
+                             : make_uint4(0u, 0u, 0u, 0u);
         long long tok = gate.tokens[(long long)row * gate.tok_stride];
         if (gate.token_keys) tok = (long long)key_index(tok);  // the scorer's packed (score, index) key
         if (tok < 0 || tok >= gate.V) {
@@ -211,13 +219,7 @@ __global__ void __launch_bounds__(kGemvThreads) rank_gemv_kernel(
           tok = tok < 0 ? 0 : gate.V - 1;
         }
         const uint4* gi = reinterpret_cast<const uint4*>(gate.table + tok * gate.ld_table) + k8;
-        const uint4* gh = reinterpret_cast<const uint4*>(gate.gh + (long long)row * gate.ld_gh) + k8;
-        const int G8 = K / 8;  // uint4 per gate block
         const uint4 ir = __ldg(gi), iz = __ldg(gi + G8), in = __ldg(gi + 2 * G8);
-        const uint4 hr = gh[0], hz = gh[G8], hn = gh[2 * G8];
-        const uint4 hp = gate.h_in != nullptr
-                             ? *(reinterpret_cast<const uint4*>(gate.h_in + (long long)row * K) + k8)
-                             : make_uint4(0u, 0u, 0u, 0u);
         const uint32_t* a_r = &ir.x; const uint32_t* a_z = &iz.x; const uint32_t* a_n = &in.x;
         const uint32_t* b_r = &hr.x; const uint32_t* b_z = &hz.x; const uint32_t* b_n = &hn.x;
         const uint32_t* c_h = &hp.x;

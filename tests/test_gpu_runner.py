@@ -354,3 +354,43 @@ def test_runners_odd_widths(cuda_device):
     mtoks, mgaps = O.markov_runner_rollout(prefix, base, embedding=emb_r, lm_head=w["Vr"], prior=None, alpha=alpha,
                                            beta=beta)
     assert _compare(mout, mgaps, mtoks, 1e-2) >= 5
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 5, 8, 9, 16, 17, 40])
+def test_small_batch_gemvs_every_rows_per_pass(cuda_device, B):
+    """The GRU step and the rank GEMV at batches that select each of their compiled row
+    counts (1, 2, 4, 8 and 16 rows per shared-memory pass) and the loop over 16-row passes
+    (17, 40), against the oracle: gh = bf16(W_hh h), the gates in fp32, h' in bf16, then
+    s = bf16(SiLU(bf16(W_rank h'))) and bf16(alpha_p s)."""
+    from dels_b200 import ops
+
+    rng = np.random.default_rng(700 + B)
+    V, G, r, n_pos = 301, 256, 96, 5
+    dev = cuda_device
+    table = O.bf16_round((rng.standard_normal((V, 3 * G)) * 0.5).astype(np.float32))
+    w_hh = O.bf16_round((rng.standard_normal((3 * G, G)) * 0.05).astype(np.float32))
+    h_in = O.bf16_round((rng.standard_normal((B, G)) * 0.5).astype(np.float32))
+    w_rank = O.bf16_round((rng.standard_normal((r, G)) * 0.1).astype(np.float32))
+    tokens = rng.integers(0, V, B)
+    alpha = np.linspace(0.9, 0.4, n_pos)
+    bf = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
+
+    h_out = torch.empty(B, G, dtype=torch.bfloat16, device=dev)
+    ops.gru_step(torch.from_numpy(tokens).to(dev), bf(table), bf(w_hh), bf(h_in), h_out)
+    gh = O.bf16_round((h_in.astype(np.float64) @ w_hh.astype(np.float64).T).astype(np.float32))
+    ref_h = O.bf16_round(O.gru_cell(table[tokens], gh, h_in).astype(np.float32))
+    got_h = h_out.float().cpu().numpy()
+    assert np.mean(got_h == ref_h) > 0.98
+    np.testing.assert_allclose(got_h, ref_h, rtol=2 ** -7, atol=2e-3)
+
+    s_scaled = torch.empty(B, r, dtype=torch.bfloat16, device=dev)
+    s_out = torch.empty(B, r, dtype=torch.bfloat16, device=dev)
+    ops.rank_gemv(h_out, bf(w_rank), torch.from_numpy(alpha.astype(np.float32)).to(dev), s_scaled, n_pos=n_pos,
+                  activation="silu", s_out=s_out)
+    got_s = s_out.float().cpu().numpy()
+    ref_s = O.rank_state_bf16(got_h, w_rank, "silu")
+    assert np.mean(got_s == ref_s) > 0.98
+    np.testing.assert_allclose(got_s, ref_s, rtol=2 ** -7, atol=2e-3)
+    pos = np.arange(B) % n_pos
+    ref_scaled = O.bf16_round((alpha[pos][:, None].astype(np.float32) * got_s).astype(np.float32))
+    np.testing.assert_array_equal(s_scaled.float().cpu().numpy(), ref_scaled)
