@@ -89,6 +89,20 @@ class ClockSampler:
         except (OSError, FileNotFoundError):
             self.proc = None
 
+    def ready(self, timeout_s: float = 5.0) -> None:
+        """Wait (host only, bounded) until nvidia-smi has written its first sample: its start-up
+        can outlast a short load phase, which would leave the record empty."""
+        t0 = time.perf_counter()
+        while self.proc is not None and time.perf_counter() - t0 < timeout_s:
+            try:
+                if any(len(line.split(",")) >= 9 for line in self.path.read_text().splitlines()):
+                    return
+            except OSError:
+                pass
+            if self.proc.poll() is not None:
+                return
+            time.sleep(0.02)
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -378,6 +392,7 @@ def timed(fn, steps: int, warmup: int, world: int, stream, dev=None, clocks=None
         hold_steps = int(min(5000, max(1, hold_ms / max(est, 1e-3))))
         if clocks is not None:
             clocks.start()
+            clocks.ready()
         for _ in range(hold_steps):
             fn()
         torch.cuda.synchronize()
