@@ -12,8 +12,8 @@ Workloads (seeded synthetic inputs, see dels_b200.workloads):
   * N > 1 default: the vocab-sharded large batch, 16384 rows, each rank owning a
     contiguous vocabulary slice of W / Vr / prior (strong scaling: total work fixed);
   * ``--workload cfg1|cfg2|cfg3|cfg4|cfg5`` selects any of the five explicitly;
-  * ``--workload runner|domino`` times the drop-in rollout runners (DeLSGraphRunner,
-    DraftCorrectionGraphRunner) call by call, batch ``--runner-batch``.
+  * ``--workload runner|domino|markov`` times the drop-in rollout runners (DeLSGraphRunner,
+    DraftCorrectionGraphRunner, MarkovDeLSGraphRunner) call by call, batch ``--runner-batch``.
 
 ``value`` is device-timed (CUDA events, max over ranks) with inputs resident in HBM;
 ``e2e`` is the same metric through the public API with the step's input rows copied
@@ -199,6 +199,11 @@ def rnn_config(name: str, rows: int, H: int, r: int, V: int) -> dict:
 def runner_config(inp) -> dict:
     return {"workload": inp.name, "V": inp.V, "E": inp.E, "G": inp.G, "r": inp.r,
             "note": "one step = one runner call (14 scored positions per sequence)"}
+
+
+def markov_config(inp) -> dict:
+    return {"workload": inp.name, "V": inp.V, "r": inp.r,
+            "note": "one step = one MarkovDeLSGraphRunner call (14 scored positions per sequence)"}
 
 
 def domino_config(inp) -> dict:
@@ -603,6 +608,8 @@ def run_ours(args, rank, world, dev):
         return run_runner(args, rank, world, dev)
     elif wname == "domino":
         return run_domino(args, rank, world, dev)
+    elif wname == "markov":
+        return run_markov(args, rank, world, dev)
     else:
         raise SystemExit(f"unknown workload {wname}")
 
@@ -875,7 +882,8 @@ def runner_cpu_rate(inp, reps: int = 2) -> tuple[float, int, str]:
         f"one batch-1 rollout of {inp.steps} steps x {reps} repetitions, bf16 torch on the host"
 
 
-def reference_gpu_runner(args, kw, ours, prefix, base, stream, dev) -> dict:
+def reference_gpu_runner(args, kw, ours, prefix, base, stream, dev, module: str = "dels",
+                         cls: str = "DeLSGraphRunner") -> dict:
     """The reference's own DeLSGraphRunner (Triton kernels, code/kernel/dels.py:214-478) on
     this GPU, beside ours: same local head, schedules, prior and call inputs.  The
     reference tree is not part of this repository; ``--reference-runner`` names a copy of
@@ -884,11 +892,11 @@ def reference_gpu_runner(args, kw, ours, prefix, base, stream, dev) -> dict:
     greedy rollout may part ways after a near-tie of the scores)."""
     import importlib.util
 
-    path = Path(args.reference_runner) / "kernel" / "dels.py"
-    spec = importlib.util.spec_from_file_location("dels_reference_kernel_dels", path)
+    path = Path(args.reference_runner) / "kernel" / f"{module}.py"
+    spec = importlib.util.spec_from_file_location(f"dels_reference_kernel_{module}", path)
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
-    ref = mod.DeLSGraphRunner(**kw)
+    ref = getattr(mod, cls)(**kw)
     ms = timed(lambda: ref(prefix, base), args.steps, args.warmup, 1, stream, dev, hold_ms=300.0) / args.steps
     ms_ours = timed(lambda: ours(prefix, base), args.steps, args.warmup, 1, stream, dev, hold_ms=300.0) / args.steps
     t_ref, t_ours = ref(prefix, base), ours(prefix, base)
@@ -898,7 +906,7 @@ def reference_gpu_runner(args, kw, ours, prefix, base, stream, dev) -> dict:
     return {"ms_per_call": ms, "ms_per_call_ours_same_run": ms_ours, "speedup": ms / ms_ours,
             "uses_triton": bool(getattr(ref, "_can_triton_fuse", False)),
             "tokens_identical_frac": float(same.float().mean()), "first_differing_step_per_row": first_diff[:8],
-            "source": "the reference's code/kernel/dels.py, loaded from --reference-runner at run time"}
+            "source": f"the reference's code/kernel/{module}.py, loaded from --reference-runner at run time"}
 
 
 def run_runner(args, rank, world, dev):
@@ -974,6 +982,98 @@ def run_runner(args, rank, world, dev):
         res["reference_gpu_runner"] = reference_gpu_runner(args, kw, runner, prefix, inp.base, stream, dev)
     if not args.no_cpu_baseline:
         rps, cores, sample = runner_cpu_rate(inp)
+        res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample}
+    return res
+
+
+def markov_inputs(args, dev):
+    """The Markov workload's seeded local head (embedding and LM-head factors [V, r], r =
+    256 like the low-rank head), schedules and call inputs (previous token ids, base logits
+    [B, 14, V]), built with torch alone (shared by both arms)."""
+    import types
+
+    import dels as D
+    from dels_b200 import workloads
+
+    V, r, steps, B = workloads.VOCAB, 256, 14, args.runner_batch
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    emb = torch.randn(V, r, generator=g, device=dev) * 0.5
+    lm = torch.randn(V, r, generator=g, device=dev) * 0.05
+    head = D.MarkovDeLSLocalHead(embedding_weight=emb, lm_head_weight=lm, dtype=torch.bfloat16, device=dev)
+    inp = types.SimpleNamespace(V=V, r=r, steps=steps, B=B, head=head, name=f"markov_b{B}_steps{steps}")
+    inp.prior = workloads.zipf_log_prior(V, device=dev).to(torch.bfloat16)
+    inp.alpha = workloads.linspace(0.9, 0.3, steps)
+    inp.beta = workloads.linspace(0.3, 0.1, steps)
+    inp.prev = torch.randint(0, V, (B, 1), generator=g, device=dev)
+    inp.base = torch.randn(B, steps, V, generator=g, device=dev).to(torch.bfloat16)
+    return inp
+
+
+def markov_cpu_rate(inp, reps: int = 2) -> tuple[float, int, str]:
+    """The reference Markov runner's torch path (oracle/reference_torch.markov_rollout) for
+    the first sequence on the host cores; returns (rows/s, threads, sample)."""
+    from oracle.reference_torch import markov_rollout
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_args = (inp.prev[:1].cpu(), inp.base[:1].cpu(), inp.head.embedding_weight.detach().cpu(),
+                inp.head.lm_head_weight.detach().cpu(), inp.prior.cpu(), inp.alpha, inp.beta)
+    markov_rollout(*cpu_args)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        markov_rollout(*cpu_args)
+    dt = (time.perf_counter() - t0) / reps
+    return inp.steps / dt, torch.get_num_threads(), \
+        f"one batch-1 rollout of {inp.steps} steps x {reps} repetitions, bf16 torch on the host"
+
+
+def run_markov(args, rank, world, dev):
+    """The drop-in MarkovDeLSGraphRunner (kernel/markov_dels.py) with a rank-256 Markov head
+    over V = 151936, batch B, 14 suffix steps: one call = copy-in of the previous token ids
+    and base logits, CUDA-graph replay, clone of the tokens (code/kernel/markov_dels.py:303-312)."""
+    from kernel.markov_dels import MarkovDeLSGraphRunner
+
+    if world > 1:
+        raise SystemExit("the markov workload is single-GPU")
+    inp = markov_inputs(args, dev)
+    V, r, steps, B = inp.V, inp.r, inp.steps, inp.B
+    kw = dict(local_head=inp.head, batch_size=B, steps=steps, vocab_size=V, alpha_values=inp.alpha,
+              beta_values=inp.beta, baseline_logits=inp.prior, device=dev)
+    runner = MarkovDeLSGraphRunner(**kw)
+    stream = torch.cuda.current_stream(dev)
+    call = lambda: runner(inp.prev, inp.base)  # noqa: E731
+    clocks = ClockSampler(dev)
+    ms = timed(call, args.steps, args.warmup, 1, stream, dev, clocks, hold_ms=500.0)
+    clk = clocks.stop()
+    host = [t.cpu().pin_memory() for t in (inp.prev, inp.base)]
+    pipe = PipelinedCall(host, runner, dev, stream)
+    ms_e2e = timed(pipe.step, args.steps, args.warmup, 1, stream, dev, hold_ms=500.0, drain=pipe.drain)
+    _, pk_gbs, pk_src = peaks()
+    # per step: the LM-head factor (V x r), the step's base-logit rows, the prior (fp32), the
+    # embedding rows; per call: the copy-in of the base logits (read + write)
+    per_step = r * V * 2 + B * V * 2 + V * 4 + B * r * 2
+    bytes_call = steps * per_step + B * steps * V * 2 * 2
+    achieved = bytes_call / (ms / args.steps * 1e-3) / 1e9
+    rows = B * steps
+    res = {
+        "metric": METRIC, "value": rows * args.steps / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, random-init Markov head at the low-rank head's rank)",
+        "config": markov_config(inp),
+        "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
+                "d2h_bytes_per_step": B * steps * 8},
+        "gpu_launches": 2 * steps * args.steps,  # per step: the embedding gather, the scorer
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
+                     "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call},
+        "clocks": clk,
+    }
+    if args.reference_runner:
+        res["reference_gpu_runner"] = reference_gpu_runner(args, kw, runner, inp.prev, inp.base, stream, dev,
+                                                           module="markov_dels", cls="MarkovDeLSGraphRunner")
+    if not args.no_cpu_baseline:
+        rps, cores, sample = markov_cpu_rate(inp)
         res["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample}
     return res
 
@@ -1100,10 +1200,11 @@ def run_reference(args, dev, world: int = 1):
 
     wname = args.workload if args.workload != "auto" else default_workload(world)
     gdev = dev if torch.cuda.is_available() else torch.device("cpu")
-    if wname in ("runner", "domino"):
-        inp = (runner_inputs if wname == "runner" else domino_inputs)(args, gdev)
-        rate = runner_cpu_rate if wname == "runner" else domino_cpu_rate
-        config = (runner_config if wname == "runner" else domino_config)(inp)
+    if wname in ("runner", "domino", "markov"):
+        inputs = {"runner": runner_inputs, "domino": domino_inputs, "markov": markov_inputs}[wname]
+        rate = {"runner": runner_cpu_rate, "domino": domino_cpu_rate, "markov": markov_cpu_rate}[wname]
+        inp = inputs(args, gdev)
+        config = {"runner": runner_config, "domino": domino_config, "markov": markov_config}[wname](inp)
         rates, cores, sample = [], 0, ""
         for i in range(args.warmup + args.steps):
             rps, cores, sample = rate(inp, reps=1)
@@ -1160,14 +1261,16 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="auto", choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "runner", "domino"])
+    ap.add_argument("--workload", default="auto",
+                    choices=["auto", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "runner", "domino", "markov"])
     ap.add_argument("--runner-batch", type=int, default=1, help="batch of the runner workload")
     ap.add_argument("--runner-hidden", action="store_true",
                     help="runner workload: DeLSFusedGraphRunner fed the draft hidden states")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reference-runner", default="",
-                    help="runner workload: path to a copy of the reference's code/ directory; its Triton "
-                         "DeLSGraphRunner is timed beside ours on the same GPU and inputs")
+                    help="runner / markov workloads: path to a copy of the reference's code/ directory; its "
+                         "Triton DeLSGraphRunner / MarkovDeLSGraphRunner is timed beside ours on the same GPU "
+                         "and inputs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()

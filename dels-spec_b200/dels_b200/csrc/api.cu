@@ -1279,9 +1279,9 @@ int dels_correction_mid_tc_bf16(const void* h, int64_t ld_h, const void* w_s, in
   return DELS_OK;
 }
 
-int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, const void* emb, int64_t ld_emb,
-                                 const float* alpha, int n_pos, int B, int r, int V, void* s_scaled, int64_t* keys,
-                                 void* ws, void* stream) {
+int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* emb,
+                                 int64_t ld_emb, const float* alpha, int n_pos, int B, int r, int V, void* s_scaled,
+                                 int64_t* keys, void* ws, void* stream) {
   if (B < 0 || r <= 0 || V <= 0 || n_pos <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape");
   if (tokens == nullptr || emb == nullptr || s_scaled == nullptr) return fail(DELS_ERR_INVALID_ARG, "NULL argument");
   if (ld_emb < r) return fail(DELS_ERR_INVALID_ARG, "embedding leading dimension < r");
@@ -1293,7 +1293,7 @@ int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, cons
   if (B == 0) return DELS_OK;
   const int grid = cdiv((long long)B * r, 256) < 1024 ? cdiv((long long)B * r, 256) : 1024;
   DELS_CHECK_PDL("gather_scaled_kernel launch", launch_pdl(gather_scaled_kernel, dim3(grid), dim3(256), 0,
-      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<const long long*>(tokens), tok_stride,
+      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<const long long*>(tokens), tok_stride, token_keys,
       reinterpret_cast<const __nv_bfloat16*>(emb), ld_emb, alpha, n_pos, B, r, V,
       reinterpret_cast<__nv_bfloat16*>(s_scaled), reinterpret_cast<long long*>(keys), counter, status));
   return DELS_OK;

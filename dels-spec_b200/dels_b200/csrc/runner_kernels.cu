@@ -330,7 +330,7 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
   }
 }
 
-__global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride,
+__global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride, int token_keys,
                                      const __nv_bfloat16* __restrict__ emb, long long ld_emb,
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter, int* status) {
@@ -339,6 +339,7 @@ __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long 
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < B * r; e += gridDim.x * blockDim.x) {
     const int b = e / r, j = e % r;
     long long tok = tokens[(long long)b * tok_stride];
+    if (token_keys) tok = (long long)key_index(tok);  // the scorer's packed (score, index) key
     if (tok < 0 || tok >= V) {
       if (status != nullptr) atomicCAS(status, 0, DELS_ERR_INVALID_ARG);
       tok = tok < 0 ? 0 : V - 1;

@@ -68,7 +68,7 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
                                  const __nv_bfloat16* __restrict__ gh, long long ld_gh, const __nv_bfloat16* h_in,
                                  __nv_bfloat16* h_out, int B, int G, int V, int* status);
 
-__global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride,
+__global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride, int token_keys,
                                      const __nv_bfloat16* __restrict__ emb, long long ld_emb,
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,
                                      __nv_bfloat16* s_scaled, long long* keys, unsigned* counter, int* status);

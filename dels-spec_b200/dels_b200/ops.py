@@ -709,15 +709,18 @@ def gather_scaled_rows(
     n_pos: int = 1,
     keys: torch.Tensor | None = None,
     ws: Workspace | None = None,
+    tokens_are_keys: bool = False,
 ) -> torch.Tensor:
-    """s_scaled[b] = bf16(alpha * emb[tokens[b]]) (Markov rank state)."""
+    """s_scaled[b] = bf16(alpha * emb[tokens[b]]) (Markov rank state).  With
+    ``tokens_are_keys`` the tokens are the previous step's packed (score, index) keys."""
     _require_cuda("tokens", tokens, torch.int64)
     _require_cuda("emb", emb, torch.bfloat16, 2)
     B, r = s_scaled.shape
     if emb.shape[1] != r or not s_scaled.is_contiguous():
         raise ValueError("embedding / output shapes do not match")
     tok_stride = tokens.stride(0) if tokens.numel() > 1 else 1
-    _lib.call("dels_gather_scaled_rows_bf16", _ptr(tokens), tok_stride, _ptr(emb), _row_major("emb", emb),
+    _lib.call("dels_gather_scaled_rows_bf16", _ptr(tokens), tok_stride, int(bool(tokens_are_keys)), _ptr(emb),
+              _row_major("emb", emb),
               _ptr(alpha), int(n_pos), B, r, emb.shape[0], _ptr(s_scaled), _ptr(keys),
               None if ws is None else ws.ptr, _stream(s_scaled.device))
     return s_scaled

@@ -5,7 +5,10 @@ Drop-in for ``kernel.markov_dels.MarkovDeLSGraphRunner`` of the reference
 checks, ``__call__(prev_token_ids, base_logits) -> LongTensor[B, steps]``.  Each
 captured step is two kernels: the embedding-row gather of the previous token scaled by
 alpha_step (``dels_gather_scaled_rows_bf16``) and the fused tcgen05 scorer over
-base + low-rank - beta * prior (``dels_fused_argmax_base_bf16``).
+base + low-rank - beta * prior (``dels_fused_argmax_base_bf16``).  The scorer of each
+step writes only its packed (score, index) keys; the next step's gather decodes the
+previous key itself, and one ``dels_keys_decode`` per call turns every step's keys into
+the output tokens, so no scorer ends with a completion count and a decode of its own.
 """
 
 from __future__ import annotations
@@ -85,9 +88,9 @@ class MarkovDeLSGraphRunner:
         self._beta = torch.tensor(self.beta_values, dtype=torch.float32, device=device)
         self._tokens = torch.zeros(S, B, dtype=torch.long, device=device)
         self._s_scaled = torch.zeros(B, self._r, dtype=dtype, device=device)
-        self._keys = torch.empty(B, dtype=torch.int64, device=device)
+        self._step_keys = torch.empty(S, B, dtype=torch.int64, device=device)  # one key slot per step
         self._ws = ops.Workspace(1 << 12, device)
-        self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
+        self._key_outs = [ops.ScoreOut(tokens=None, scores=None, keys=self._step_keys[i]) for i in range(S)]
 
         ops.init(device)
         stream = torch.cuda.Stream(device=device)
@@ -104,13 +107,16 @@ class MarkovDeLSGraphRunner:
     def _forward_impl(self):
         current = self.static_prev_ids[:, 0]
         for step in range(self.steps):
+            # the gather resets this step's key slot; from the second step on it reads the
+            # previous step's packed keys
             ops.gather_scaled_rows(current, self.embedding_weight, self._alpha[step : step + 1], self._s_scaled,
-                                   keys=self._keys, ws=self._ws)
+                                   keys=self._step_keys[step], ws=self._ws, tokens_are_keys=step > 0)
             ops.fused_argmax_base_bf16(
                 self.static_base_logits[:, step, :], self._s_scaled, self.lm_head_weight, self._prior_f32,
-                self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step], ws=self._ws,
+                self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._key_outs[step], ws=self._ws,
             )
-            current = self._tokens[step]
+            current = self._step_keys[step]
+        ops.keys_decode(self._step_keys.view(-1), tokens=self._tokens.view(-1), with_scores=False)
         self.static_out.copy_(self._tokens.t())
 
     @torch.inference_mode()

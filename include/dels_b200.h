@@ -280,10 +280,12 @@ DELS_API int dels_gru_correction_mid_bf16(const int64_t* tokens, int64_t tok_str
 
 /* Markov rank state (code/kernel/markov_dels.py:288):
  *   s_scaled[b] = bf16(alpha_p * emb[tokens[b * tok_stride]]),  emb [V, r] bf16,
- * keys[0..B) reset.  Out-of-range ids are clamped and flagged as above. */
-DELS_API int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, const void* emb, int64_t ld_emb,
-                                          const float* alpha, int n_pos, int B, int r, int V, void* s_scaled,
-                                          int64_t* keys, void* ws, void* stream);
+ * keys[0..B) reset.  Out-of-range ids are clamped and flagged as above.  token_keys != 0:
+ * tokens[] holds the previous step's packed (score, index) argmax keys, decoded here (a
+ * keys-only rollout, as in dels_gru_rank_gemv_bf16). */
+DELS_API int dels_gather_scaled_rows_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* emb,
+                                          int64_t ld_emb, const float* alpha, int n_pos, int B, int r, int V,
+                                          void* s_scaled, int64_t* keys, void* ws, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Domino draft-correction rollout (code/kernel/domino.py:232-520).  Per step the

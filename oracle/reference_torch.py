@@ -68,6 +68,23 @@ def runner_rollout(prefix_ids, base_logits, table, w_hh, w_rank, Vr, prior, alph
     return out
 
 
+def markov_rollout(prev_ids, base_logits, emb, lm_head, prior, alpha, beta) -> torch.Tensor:
+    """MarkovDeLSGraphRunner._forward_impl's torch path (code/kernel/markov_dels.py:285-301),
+    on the host: the previous token's embedding row as the rank state, base + alpha *
+    low-rank - beta * prior, argmax, per step."""
+    B, steps, _ = base_logits.shape
+    cur = prev_ids[:, 0]
+    out = torch.empty(B, steps, dtype=torch.long)
+    for step in range(steps):
+        rank_state = F.embedding(cur, emb)
+        logits = base_logits[:, step, :] + alpha[step] * F.linear(rank_state, lm_head)
+        if prior is not None and beta[step] != 0.0:
+            logits = logits - beta[step] * prior.view(1, -1)
+        cur = torch.argmax(logits, dim=-1)
+        out[:, step] = cur
+    return out
+
+
 def domino_rollout(prefix_ids, hiddens, base_logits, table, w_hh, w_z, w_s, fc2, alpha) -> torch.Tensor:
     """DraftCorrectionGraphRunner._forward_impl's torch path (code/kernel/domino.py:399-451,
     bias-free released head: SiLU middle, GRU without biases), on the host."""

@@ -82,3 +82,18 @@ def test_reference_arm_under_torchrun_prints_once():
     assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["scaling"] == "strong"
     assert d["config"]["workload"] == "cfg5_vocab_sharded_16384" and d["value"] > 0
     assert d["config"] == _bench().dense_config("cfg5_vocab_sharded_16384", 16384, 4096, 256, 151936, 2, True)
+
+
+def test_reference_arm_markov_on_the_host():
+    """The Markov runner workload's reference arm: the reference runner's torch rollout on the
+    host, with the config dict our arm prints."""
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "markov",
+                          "--steps", "1", "--warmup", "1"], capture_output=True, text=True, timeout=900, check=True,
+                         cwd=ROOT).stdout
+    lines = [line for line in out.splitlines() if line.startswith("{")]
+    assert len(lines) == 1, out
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "rows/s" and d["value"] > 0
+    assert d["config"] == {"workload": "markov_b1_steps14", "V": 151936, "r": 256,
+                           "note": "one step = one MarkovDeLSGraphRunner call (14 scored positions per sequence)"}
+    assert d["cpu_baseline"]["value"] == d["value"] and "rollout" in d["cpu_baseline"]["sample"]
