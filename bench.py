@@ -816,8 +816,8 @@ def runner_launches(runner, steps: int) -> int:
         return lm + 2 * steps + 1
     if runner._split_gru:  # gates, rank GEMV, scorer (with the next step's W_hh h)
         return lm + 3 * steps
-    if runner._tc:  # gates; per step rank GEMM + finalisation, scorer; W_hh GEMM (+ finalisation)
-        return lm + 1 + 3 * steps + 3 * (steps - 1)
+    if runner._tc:  # gates; per step rank GEMM + finalisation, scorer; W_hh GEMM + gate finalisation
+        return lm + 1 + 3 * steps + (2 if runner._gru_tc_fused else 3) * (steps - 1)
     return lm + 3 * steps  # GRU step, rank GEMV, scorer
 
 
@@ -1064,7 +1064,7 @@ def run_markov(args, rank, world, dev):
         "e2e": {"value": rows * args.steps / (ms_e2e * 1e-3), "unit": "rows/s",
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
                 "d2h_bytes_per_step": B * steps * 8},
-        "gpu_launches": 2 * steps * args.steps,  # per step: the embedding gather, the scorer
+        "gpu_launches": (2 * steps + 1) * args.steps,  # per step the embedding gather and the scorer; keys decode
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
                      "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call},
         "clocks": clk,

@@ -256,6 +256,7 @@ int init_device(int dev) {
     SET(correction_finalize_kernel, 0);
     SET(gather_scaled_kernel, 0);
     SET(gru_gates_kernel, 0);
+    SET(gru_finalize_kernel, 0);
     SET(wait_selftest_kernel, 0);
 #undef SET
   }
@@ -1241,6 +1242,43 @@ int dels_linear_bf16(const void* x, int64_t ld_x, const void* w, int64_t ld_w, c
   DELS_CHECK_PDL("linear_finalize_kernel launch", launch_pdl(linear_finalize_kernel, dim3(grid), dim3(256), 0, st,
       partials, plan.splits, (long long)rows * plan.ld_out, (long long)plan.ld_out, rows, N,
       reinterpret_cast<const __nv_bfloat16*>(bias), reinterpret_cast<__nv_bfloat16*>(out), (long long)ld_out));
+  return DELS_OK;
+}
+
+size_t dels_gru_step_tc_workspace_bytes(int B, int G) {
+  if (B <= 0 || G <= 0) return DELS_WS_HEADER_BYTES;
+  return DELS_WS_HEADER_BYTES + projection_partials_bytes(B, G, 3 * G);
+}
+
+int dels_gru_step_tc_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+                          const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G, int V,
+                          void* ws, size_t ws_bytes, void* stream) {
+  int rc;
+  if (B < 0 || G <= 0 || V <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d V=%d", B, G, V);
+  if (tokens == nullptr || gi_table == nullptr || h_in == nullptr || h_out == nullptr)
+    return fail(DELS_ERR_INVALID_ARG, "NULL argument");
+  if (ld_table < 3LL * G) return fail(DELS_ERR_INVALID_ARG, "gi table leading dimension < 3G");
+  if ((rc = check_bf16_matrix("h_in", h_in, G, G)) != DELS_OK) return rc;
+  if ((rc = check_bf16_matrix("w_hh", w_hh, G, G)) != DELS_OK) return rc;
+  WsHeader hdr;
+  if ((rc = ws_header(ws, ws_bytes, dels_gru_step_tc_workspace_bytes(B, G), &hdr)) != DELS_OK) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = current_device_state(&ds)) != DELS_OK) return rc;
+  if (B == 0) return DELS_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + DELS_WS_HEADER_BYTES);
+  SplitPlan plan;
+  if ((rc = launch_projection(h_in, G, w_hh, G, B, G, 3 * G, partials, hdr.status, ds->sm_count, st, &plan)) !=
+      DELS_OK)
+    return rc;
+  const long long total = (long long)B * G;
+  const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
+  DELS_CHECK_PDL("gru_finalize_kernel launch", launch_pdl(gru_finalize_kernel, dim3(grid), dim3(256), 0, st,
+      partials, plan.splits, (long long)B * plan.ld_out, (long long)plan.ld_out,
+      reinterpret_cast<const long long*>(tokens), (long long)tok_stride,
+      reinterpret_cast<const __nv_bfloat16*>(gi_table), (long long)ld_table,
+      reinterpret_cast<const __nv_bfloat16*>(b_hh), reinterpret_cast<const __nv_bfloat16*>(h_in),
+      reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V, hdr.status));
   return DELS_OK;
 }
 

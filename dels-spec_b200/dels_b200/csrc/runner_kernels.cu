@@ -330,6 +330,55 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
   }
 }
 
+// The GRU step after a tensor-core split-K projection of W_hh h_in: per (row, unit) the
+// three gate columns' partial sums are added in split order, the bias joins the fp32 sum
+// and the result is rounded to bf16 once (as dels_linear_bf16's finalisation writes gh),
+// then the gates as gru_gates_kernel evaluates them.  The partials of a split group are
+// loaded together, ahead of the sums.
+__global__ void gru_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
+                                    long long ld_part, const long long* __restrict__ tokens, long long tok_stride,
+                                    const __nv_bfloat16* __restrict__ table, long long ld_table,
+                                    const __nv_bfloat16* __restrict__ b_hh, const __nv_bfloat16* h_in,
+                                    __nv_bfloat16* h_out, int B, int G, int V, int* status) {
+  constexpr int kAhead = 4;
+  pdl_wait();
+  pdl_trigger();  // the next kernel reads our output only after its own wait
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < (long long)B * G;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(e / G), g = (int)(e % G);
+    long long tok = tokens[(long long)b * tok_stride];
+    const float h = h_in != nullptr ? __bfloat162float(h_in[(long long)b * G + g]) : 0.0f;
+    float acc[3] = {0.0f, 0.0f, 0.0f};
+    for (int s0 = 0; s0 < splits; s0 += kAhead) {
+      float v[3][kAhead];
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int q = 0; q < kAhead; ++q)
+          v[j][q] = s0 + q < splits ? partials[(s0 + q) * split_stride + (long long)b * ld_part + j * G + g] : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int q = 0; q < kAhead; ++q)
+          if (s0 + q < splits) acc[j] += v[j][q];
+    }
+    float gh[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      float a = acc[j];
+      if (b_hh != nullptr) a += __bfloat162float(b_hh[j * G + g]);
+      gh[j] = __bfloat162float(__float2bfloat16_rn(a));
+    }
+    if (tok < 0 || tok >= V) {
+      if (status != nullptr) atomicCAS(status, 0, DELS_ERR_INVALID_ARG);
+      tok = tok < 0 ? 0 : V - 1;
+    }
+    const __nv_bfloat16* gi = table + tok * ld_table;
+    h_out[(long long)b * G + g] = __float2bfloat16_rn(gru_unit(__bfloat162float(gi[g]), __bfloat162float(gi[G + g]),
+                                                               __bfloat162float(gi[2 * G + g]), gh[0], gh[1], gh[2], h));
+  }
+}
+
 __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride, int token_keys,
                                      const __nv_bfloat16* __restrict__ emb, long long ld_emb,
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,

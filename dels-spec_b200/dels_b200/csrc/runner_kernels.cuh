@@ -68,6 +68,12 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
                                  const __nv_bfloat16* __restrict__ gh, long long ld_gh, const __nv_bfloat16* h_in,
                                  __nv_bfloat16* h_out, int B, int G, int V, int* status);
 
+__global__ void gru_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
+                                    long long ld_part, const long long* __restrict__ tokens, long long tok_stride,
+                                    const __nv_bfloat16* __restrict__ table, long long ld_table,
+                                    const __nv_bfloat16* __restrict__ b_hh, const __nv_bfloat16* h_in,
+                                    __nv_bfloat16* h_out, int B, int G, int V, int* status);
+
 __global__ void gather_scaled_kernel(const long long* __restrict__ tokens, long long tok_stride, int token_keys,
                                      const __nv_bfloat16* __restrict__ emb, long long ld_emb,
                                      const float* __restrict__ alpha, int n_pos, int B, int r, int V,

@@ -591,6 +591,38 @@ def gru_gates(
     return h_out
 
 
+def gru_step_tc(
+    tokens: torch.Tensor,
+    gi_table: torch.Tensor,
+    w_hh: torch.Tensor,
+    h_in: torch.Tensor,
+    h_out: torch.Tensor,
+    *,
+    b_hh: torch.Tensor | None = None,
+    ws: Workspace | None = None,
+) -> torch.Tensor:
+    """h_out = GRU(gi_table[tokens], h_in) with gh = bf16(W_hh h_in + b_hh) from a tensor-core
+    split-K GEMM whose finalisation evaluates the gates (bit-identical to linear_bf16 followed
+    by gru_gates)."""
+    _require_cuda("tokens", tokens, torch.int64)
+    _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
+    _require_cuda("w_hh", w_hh, torch.bfloat16, 2)
+    _require_cuda("h_in", h_in, torch.bfloat16, 2)
+    _require_cuda("h_out", h_out, torch.bfloat16, 2)
+    B, G = h_out.shape
+    V = gi_table.shape[0]
+    if w_hh.shape != (3 * G, G) or not w_hh.is_contiguous() or gi_table.shape[1] != 3 * G:
+        raise ValueError("GRU weights do not match the hidden size")
+    if h_in.shape != (B, G) or not h_in.is_contiguous() or not h_out.is_contiguous():
+        raise ValueError("h_in / h_out must be contiguous [B, G] tensors")
+    need = _lib.query("dels_gru_step_tc_workspace_bytes", B, G)
+    ws = workspace(need, h_out.device) if ws is None else ws.ensure(need)
+    tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
+    _lib.call("dels_gru_step_tc_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+              _ptr(w_hh), _ptr(b_hh), _ptr(h_in), _ptr(h_out), B, G, V, ws.ptr, ws.nbytes, _stream(h_out.device))
+    return h_out
+
+
 def gru_rank_gemv(
     tokens: torch.Tensor,
     gi_table: torch.Tensor,

@@ -166,7 +166,11 @@ class DeLSGraphRunner:
                            and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0"
                            and self._scorer_computes_next_gh())
         if self._tc:
-            need = max(ops.linear_workspace_bytes(B, G, 3 * G), ops.rank_workspace_bytes(B, G, r))
+            # the GRU's split-K finalisation evaluates the gates itself (dels_gru_step_tc_bf16;
+            # DELS_RUNNER_GRU_TC_FUSED=0 runs dels_linear_bf16 then dels_gru_gates_bf16)
+            self._gru_tc_fused = os.environ.get("DELS_RUNNER_GRU_TC_FUSED", "1") != "0"
+            need = max(ops.linear_workspace_bytes(B, G, 3 * G), ops.rank_workspace_bytes(B, G, r),
+                       int(ops._lib.query("dels_gru_step_tc_workspace_bytes", B, G)))
             self._tc_ws = ops.Workspace(need, device)
         if self._overlap:
             # Per-step packed argmax keys: each step's scorer only writes keys (no in-kernel
@@ -199,9 +203,12 @@ class DeLSGraphRunner:
             return ops.gru_step(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out, b_hh=self.gru_b_hh,
                                 ws=self._ws)
         if h_in is None:
-            gh = self._gh0
-        else:
-            gh = ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh, ws=self._tc_ws)
+            return ops.gru_gates(tokens, self._gru_input_proj_table, self._gh0, h_in, h_out, ws=self._ws)
+        if self._gru_tc_fused:
+            # W_hh h as a split-K GEMM whose finalisation evaluates the gates (one kernel less)
+            return ops.gru_step_tc(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out,
+                                   b_hh=self.gru_b_hh, ws=self._tc_ws)
+        gh = ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh, ws=self._tc_ws)
         return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws)
 
     def _rank(self, h_cur, step: int):

@@ -169,8 +169,12 @@ class DraftCorrectionGraphRunner:
         # the SiLU epilogue (as in kernel/dels.py).
         self._tc = B >= int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
         if self._tc:
+            # the GRU's split-K finalisation evaluates the gates itself (dels_gru_step_tc_bf16;
+            # DELS_RUNNER_GRU_TC_FUSED=0 runs dels_linear_bf16 then dels_gru_gates_bf16)
+            self._gru_tc_fused = os.environ.get("DELS_RUNNER_GRU_TC_FUSED", "1") != "0"
             self._tc_ws = ops.Workspace(max(ops.linear_workspace_bytes(B, G, 3 * G),
-                                            ops.correction_mid_tc_workspace_bytes(B, G, M)), device)
+                                            ops.correction_mid_tc_workspace_bytes(B, G, M),
+                                            int(ops._lib.query("dels_gru_step_tc_workspace_bytes", B, G))), device)
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
             if self.gru_b_hh is not None:
                 self._gh0.copy_(self.gru_b_hh[None, :].expand(B, -1))
@@ -207,6 +211,10 @@ class DraftCorrectionGraphRunner:
         if not self._tc:
             return ops.gru_step(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out, b_hh=self.gru_b_hh,
                                 ws=self._ws)
+        if h_in is not None and self._gru_tc_fused:
+            # W_hh h as a split-K GEMM whose finalisation evaluates the gates (one kernel less)
+            return ops.gru_step_tc(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out,
+                                   b_hh=self.gru_b_hh, ws=self._tc_ws)
         gh = self._gh0 if h_in is None else ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh,
                                                            ws=self._tc_ws)
         return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws)

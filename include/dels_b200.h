@@ -224,6 +224,17 @@ DELS_API int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, cons
                                  const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V,
                                  void* ws, void* stream);
 
+/* The same GRU step for larger batches in two launches: gh = W_hh . h_in as a tensor-core
+ * split-K GEMM into fp32 partials (the workspace), then one kernel that sums each unit's
+ * three gate columns in split order, adds b_hh (NULL = none) and rounds to bf16 exactly as
+ * dels_linear_bf16 writes gh, and evaluates the gates as dels_gru_gates_bf16 does:
+ * h_out bit-identical to dels_linear_bf16 followed by dels_gru_gates_bf16.  h_in and w_hh
+ * row-major with row stride G (16-byte rows, G % 8 == 0); h_in must not be NULL. */
+DELS_API size_t dels_gru_step_tc_workspace_bytes(int B, int G);
+DELS_API int dels_gru_step_tc_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+                                   const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G,
+                                   int V, void* ws, size_t ws_bytes, void* stream);
+
 /* Rank projection for small batches (code/kernel/dels.py:437-443):
  *   s = bf16(act(bf16(x . w^T + bias))), s_scaled = bf16(alpha_p * s), keys[0..B) reset,
  * one warp per output feature.  K % 8 == 0.  ws (optional) supplies the counter that

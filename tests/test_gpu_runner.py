@@ -394,3 +394,33 @@ def test_small_batch_gemvs_every_rows_per_pass(cuda_device, B):
     pos = np.arange(B) % n_pos
     ref_scaled = O.bf16_round((alpha[pos][:, None].astype(np.float32) * got_s).astype(np.float32))
     np.testing.assert_array_equal(s_scaled.float().cpu().numpy(), ref_scaled)
+
+
+@pytest.mark.parametrize("B", [12, 33, 64])
+def test_gru_step_tc_matches_linear_then_gates(cuda_device, B):
+    """The tensor-core GRU step whose split-K finalisation evaluates the gates gives h_out
+    bit-identical to dels_linear_bf16 followed by dels_gru_gates_bf16 (with and without
+    b_hh), and matches the oracle cell."""
+    from dels_b200 import ops
+
+    dev = cuda_device
+    rng = np.random.default_rng(1200 + B)
+    V, G = 503, 256
+    bf = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev).to(torch.bfloat16)  # noqa: E731
+    table = bf(rng.standard_normal((V, 3 * G)) * 0.5)
+    w_hh = bf(rng.standard_normal((3 * G, G)) * 0.05)
+    b_hh = bf(rng.standard_normal(3 * G) * 0.1)
+    h_in = bf(rng.standard_normal((B, G)) * 0.5)
+    tokens = torch.from_numpy(rng.integers(0, V, B)).to(dev)
+    for bias in (None, b_hh):
+        ref = torch.empty(B, G, dtype=torch.bfloat16, device=dev)
+        gh = ops.linear_bf16(h_in, w_hh, bias)
+        ops.gru_gates(tokens, table, gh, h_in, ref)
+        out = torch.empty(B, G, dtype=torch.bfloat16, device=dev)
+        ops.gru_step_tc(tokens, table, w_hh, h_in, out, b_hh=bias)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    gh_ref = O.bf16_round((f(h_in).astype(np.float64) @ f(w_hh).astype(np.float64).T + f(b_hh)).astype(np.float32))
+    cell = O.bf16_round(O.gru_cell(f(table)[tokens.cpu().numpy()], gh_ref, f(h_in)).astype(np.float32))
+    np.testing.assert_allclose(f(out), cell, rtol=2 ** -7, atol=2e-3)
