@@ -131,6 +131,15 @@ def test_argument_errors_are_reported_before_device_work(lib):
         _lib.call("dels_fused_argmax_base_gru_bf16", p, 1000, p, 64, p, 64, None, None, 1, 5, 64, 1000, 0, None,
                   None, p, 256, p, None, p, 1024, p, None)
     assert ei.value.status == _lib.DELS_ERR_UNSUPPORTED
+    # the tensor-core GRU step: NULL operands, then a misaligned h_in, before any device work
+    with pytest.raises(_lib.DelsArgumentError) as ei:
+        _lib.call("dels_gru_step_tc_bf16", None, 1, None, 3072, None, None, None, None, 16, 1024, 100, None, 0, None)
+    assert ei.value.status == _lib.DELS_ERR_INVALID_ARG
+    with pytest.raises(_lib.DelsArgumentError) as ei:
+        _lib.call("dels_gru_step_tc_bf16", p, 1, p, 3072, p, None, ctypes.c_void_p(addr), p, 16, 1024, 100, None, 0,
+                  None)
+    assert ei.value.status == _lib.DELS_ERR_ALIGNMENT
+    assert _lib.query("dels_gru_step_tc_workspace_bytes", 16, 1024) > _lib.DELS_WS_HEADER_BYTES
     # fp32 scorer needs H % 4 == 0
     with pytest.raises(_lib.DelsError):
         _lib.call("dels_draft_score_f32", None, 0, None, 0, None, 0, None, 0, None, None, None, 1, None, 1, 6, 4, 10,
