@@ -151,12 +151,12 @@ class DeLSGraphRunner:
         # finalisation); below it one warp per weight row does each in a single launch.
         tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "12"))
         self._tc = B >= tc_rows and self.rank_bias is None
-        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 3, at most 4; 0 turns it off) a step is
+        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 2, at most 4; 0 turns it off) a step is
         # two kernels: the GRU gates fused into the rank projection (dels_gru_rank_gemv_bf16),
         # then the scorer, whose two helper warps per CTA compute the next step's W_hh h
         # (which needs h but not the token) while the others score
         # (dels_fused_argmax_base_gru_bf16).
-        self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "3"))) and not self._tc
+        self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "2"))) and not self._tc
                          and self._scorer_computes_next_gh())
         # The other batches of at most 4 rows (DELS_RUNNER_SPLIT_GRU=0 turns it off): the
         # scorer's helper warps still compute the next W_hh h, and the step's GRU update
