@@ -146,10 +146,10 @@ class DeLSGraphRunner:
         self._keys = torch.empty(B, dtype=torch.int64, device=device)
         self._ws = ops.Workspace(1 << 12, device)
         self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
-        # From DELS_RUNNER_TC_ROWS rows up (default 12) the GRU's W_hh product and the rank
+        # From DELS_RUNNER_TC_ROWS rows up (default 9) the GRU's W_hh product and the rank
         # projection run as tensor-core split-K GEMMs (then the gates / the rank
         # finalisation); below it one warp per weight row does each in a single launch.
-        tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "12"))
+        tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "9"))
         self._tc = B >= tc_rows and self.rank_bias is None
         # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 2, at most 4; 0 turns it off) a step is
         # two kernels: the GRU gates fused into the rank projection (dels_gru_rank_gemv_bf16),

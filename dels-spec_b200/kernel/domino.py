@@ -164,10 +164,10 @@ class DraftCorrectionGraphRunner:
         self._ws = ops.Workspace(1 << 12, device)
         self._ws_lin = ops.Workspace(1 << 12, device)
         self._outs = [ops.ScoreOut(tokens=self._tokens[i], scores=None, keys=self._keys) for i in range(S)]
-        # From DELS_RUNNER_TC_ROWS rows up (default 16) the GRU's W_hh product and the
+        # From DELS_RUNNER_TC_ROWS rows up (default 9) the GRU's W_hh product and the
         # correction MLP's W_s product run as tensor-core split-K GEMMs, then the gates /
         # the SiLU epilogue (as in kernel/dels.py).
-        self._tc = B >= int(os.environ.get("DELS_RUNNER_TC_ROWS", "16"))
+        self._tc = B >= int(os.environ.get("DELS_RUNNER_TC_ROWS", "9"))
         if self._tc:
             # the GRU's split-K finalisation evaluates the gates itself (dels_gru_step_tc_bf16;
             # DELS_RUNNER_GRU_TC_FUSED=0 runs dels_linear_bf16 then dels_gru_gates_bf16)
