@@ -4,21 +4,21 @@ Drop-in for ``kernel.dels.DeLSGraphRunner`` of the reference (code/kernel/dels.p
 same constructor keywords, same ``ValueError`` checks, same ``__call__(prefix_ids,
 base_logits) -> LongTensor[B, steps]`` returning a fresh tensor, same static buffers
 (``static_prefix_ids``, ``static_base_logits``, ``static_out``), warm-up on a side
-stream and capture into ``self.graph``.  At 1-3 rows each captured step is two
+stream and capture into ``self.graph``.  At 1-2 rows each captured step is two
 ``libdels_b200.so`` kernels:
 
   1. the GRU gates of the previous token (input-table row, gh, h) fused into the rank
      projection + activation + alpha_step scaling, keys reset (``dels_gru_rank_gemv_bf16``);
   2. the fused scorer on tcgen05 tensor cores: base logits + low-rank logits - beta *
-     prior, argmax with the lowest index on ties, written straight into the step's token
-     slot, while two helper warps per CTA compute the next step's gh = bf16(W_hh h +
-     b_hh), which needs h but not the token (``dels_fused_argmax_base_gru_bf16``).
+     prior, argmax with the lowest index on ties, as the step's packed key, while two
+     helper warps per CTA compute the next step's gh = bf16(W_hh h + b_hh), which needs
+     h but not the token (``dels_fused_argmax_base_gru_bf16``).
 
-At 4 rows the gates run as their own kernel before the rank GEMV (``dels_gru_gates_bf16``,
-``dels_rank_gemv_bf16``), with the same scorer.  At 5-11 rows a step is the GRU step
+At 3-4 rows the gates run as their own kernel before the rank GEMV (``dels_gru_gates_bf16``,
+``dels_rank_gemv_bf16``), with the same scorer.  At 5-8 rows a step is the GRU step
 kernel (``dels_gru_step_bf16``), the rank GEMV and the scorer; from ``DELS_RUNNER_TC_ROWS``
-rows up W_hh h and the rank projection run as tensor-core GEMMs (``dels_linear_bf16`` +
-``dels_gru_gates_bf16``, ``dels_rank_project_bf16``).
+(9) rows up W_hh h and the rank projection run as tensor-core GEMMs
+(``dels_gru_step_tc_bf16``, ``dels_rank_project_bf16``).
 
 alpha / beta live in device arrays indexed by step, so one graph serves a schedule;
 the reference instead bakes them into the Triton kernels as constexprs (:404-409).

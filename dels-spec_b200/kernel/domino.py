@@ -19,10 +19,10 @@ Per call (all on ``libdels_b200.so``):
 
 At 1-4 rows W_hh h of the GRU update moves onto two helper warps per CTA of the scorer
 (``dels_fused_argmax_base_gru_bf16``: it needs h but not the token) and only the gates
-stay between steps: fused into the next step's correction layer at 1-3 rows
-(``dels_gru_correction_mid_bf16``), as their own kernel at 4 (``dels_gru_gates_bf16``).
-From ``DELS_RUNNER_TC_ROWS`` rows up W_hh h and W_s h run on the tensor-core GEMMs
-(``dels_linear_bf16`` + ``dels_gru_gates_bf16``, ``dels_correction_mid_tc_bf16``).
+stay between steps: fused into the next step's correction layer at 1-2 rows
+(``dels_gru_correction_mid_bf16``), as their own kernel at 3-4 (``dels_gru_gates_bf16``).
+From ``DELS_RUNNER_TC_ROWS`` (9) rows up W_hh h and W_s h run on the tensor-core GEMMs
+(``dels_gru_step_tc_bf16``, ``dels_correction_mid_tc_bf16``).
 
 The correction MLP must be Linear -> SiLU -> Linear (the released Domino head,
 code/dflash.py:271-276, and the only form the reference fuses, :283-291); its weights
