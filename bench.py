@@ -814,8 +814,8 @@ def runner_launches(runner, steps: int) -> int:
     lm = 1 if hasattr(runner, "_lm_ws") else 0  # the long-logit GEMM of the materialising runner
     if runner._overlap:  # gates + rank GEMV, scorer (with the next step's W_hh h), keys decode
         return lm + 2 * steps + 1
-    if runner._split_gru:  # gates, rank GEMV, scorer (with the next step's W_hh h)
-        return lm + 3 * steps
+    if runner._split_gru:  # gates, rank GEMV, scorer (with the next step's W_hh h); keys decode
+        return lm + 3 * steps + (1 if runner._keys_only else 0)
     if runner._tc:  # gates; per step rank GEMM + finalisation, scorer; W_hh GEMM + gate finalisation
         return lm + 1 + 3 * steps + (2 if runner._gru_tc_fused else 3) * (steps - 1)
     return lm + 3 * steps  # GRU step, rank GEMV, scorer
@@ -1179,7 +1179,8 @@ def run_domino(args, rank, world, dev):
         # z GEMM + finalisation, the prefix GRU steps, per step the correction layer and the
         # scorer, and a GRU update (or its gates alone) between steps unless the gates are fused
         # (then one keys decode per call)
-        "gpu_launches": (2 + P + 2 * steps + (1 if runner._overlap else steps - 1)) * args.steps,
+        "gpu_launches": (2 + P + 2 * steps + (0 if runner._overlap else steps - 1)
+                         + (1 if runner._keys_only else 0)) * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk_gbs, "unit": "GB/s", "frac": achieved / pk_gbs,
                      "traffic": None, "peak_source": f"{pk_src} (copy)", "algorithmic": bytes_call},
         "clocks": clk,

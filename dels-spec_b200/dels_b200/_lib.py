@@ -82,7 +82,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                           _I, _P, _P, _P, _P, _P]),
     "dels_gru_rank_gemv_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _I64, _P, _I, _I, _P,
                                      _P, _P, _P, _P]),
-    "dels_gru_gates_bf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _P]),
+    "dels_gru_gates_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _P]),
     "dels_rank_gemv_bf16": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "dels_gather_scaled_rows_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "dels_gru_step_tc_workspace_bytes": (_SZ, [_I, _I]),

@@ -1061,9 +1061,9 @@ int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi
   return DELS_OK;
 }
 
-int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
-                        const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V, void* ws,
-                        void* stream) {
+int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
+                        int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G,
+                        int V, void* ws, void* stream) {
   if (B < 0 || G <= 0 || V <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d V=%d", B, G, V);
   if (tokens == nullptr || gi_table == nullptr || gh == nullptr || h_out == nullptr)
     return fail(DELS_ERR_INVALID_ARG, "NULL argument");
@@ -1077,7 +1077,7 @@ int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, const void* g
   const long long total = (long long)B * G;
   const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
   DELS_CHECK_PDL("gru_gates_kernel launch", launch_pdl(gru_gates_kernel, dim3(grid), dim3(256), 0,
-      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<const long long*>(tokens), tok_stride,
+      reinterpret_cast<cudaStream_t>(stream), reinterpret_cast<const long long*>(tokens), tok_stride, token_keys,
       reinterpret_cast<const __nv_bfloat16*>(gi_table), ld_table, reinterpret_cast<const __nv_bfloat16*>(gh),
       (long long)ld_gh, reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G,
       V, status));

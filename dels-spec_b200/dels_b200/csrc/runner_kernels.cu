@@ -307,7 +307,7 @@ RankGemvKernel rank_gemv_kernel_for(int rows_per_pass) {
 // The GRU gates for batches where gh = bf16(W_hh h + b_hh) came from the tensor-core
 // projection (dels_linear_bf16): one thread per (row, unit), the same gate arithmetic as
 // gru_step_kernel.
-__global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long tok_stride,
+__global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long tok_stride, int token_keys,
                                  const __nv_bfloat16* __restrict__ table, long long ld_table,
                                  const __nv_bfloat16* __restrict__ gh, long long ld_gh, const __nv_bfloat16* h_in,
                                  __nv_bfloat16* h_out, int B, int G, int V, int* status) {
@@ -317,6 +317,7 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
        e += (long long)gridDim.x * blockDim.x) {
     const int b = (int)(e / G), g = (int)(e % G);
     long long tok = tokens[(long long)b * tok_stride];
+    if (token_keys) tok = (long long)key_index(tok);  // the scorer's packed (score, index) key
     if (tok < 0 || tok >= V) {
       if (status != nullptr) atomicCAS(status, 0, DELS_ERR_INVALID_ARG);
       tok = tok < 0 ? 0 : V - 1;

@@ -63,7 +63,7 @@ using RankGemvKernel = void (*)(const __nv_bfloat16* x, long long ld_x, const __
 GruStepKernel gru_step_kernel_for(int rows_per_pass);
 RankGemvKernel rank_gemv_kernel_for(int rows_per_pass);
 
-__global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long tok_stride,
+__global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long tok_stride, int token_keys,
                                  const __nv_bfloat16* __restrict__ table, long long ld_table,
                                  const __nv_bfloat16* __restrict__ gh, long long ld_gh, const __nv_bfloat16* h_in,
                                  __nv_bfloat16* h_out, int B, int G, int V, int* status);

@@ -572,8 +572,10 @@ def gru_gates(
     h_out: torch.Tensor,
     *,
     ws: Workspace | None = None,
+    tokens_are_keys: bool = False,
 ) -> torch.Tensor:
-    """h_out = GRU gates(gi_table[tokens], gh, h_in) for a precomputed gh = bf16(W_hh h + b_hh)."""
+    """h_out = GRU gates(gi_table[tokens], gh, h_in) for a precomputed gh = bf16(W_hh h + b_hh).
+    With ``tokens_are_keys`` the tokens are the previous step's packed (score, index) keys."""
     _require_cuda("tokens", tokens, torch.int64)
     _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
     _require_cuda("gh", gh, torch.bfloat16, 2)
@@ -585,7 +587,8 @@ def gru_gates(
     if h_in is not None and (h_in.shape != (B, G) or not h_in.is_contiguous()):
         raise ValueError("h_in must be a contiguous [B, G] tensor")
     tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
-    _lib.call("dels_gru_gates_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+    _lib.call("dels_gru_gates_bf16", _ptr(tokens), tok_stride, int(bool(tokens_are_keys)), _ptr(gi_table),
+              _row_major("gi_table", gi_table),
               _ptr(gh), gh.stride(0), _ptr(h_in), _ptr(h_out), B, G, V, None if ws is None else ws.ptr,
               _stream(h_out.device))
     return h_out

@@ -172,11 +172,15 @@ class DeLSGraphRunner:
             need = max(ops.linear_workspace_bytes(B, G, 3 * G), ops.rank_workspace_bytes(B, G, r),
                        int(ops._lib.query("dels_gru_step_tc_workspace_bytes", B, G)))
             self._tc_ws = ops.Workspace(need, device)
-        if self._overlap:
+        # The split schedule reads the previous step's packed keys in its gates kernel too
+        # (DELS_RUNNER_SPLIT_KEYS=0: each scorer decodes its own tokens).
+        self._split_keys = self._split_gru and os.environ.get("DELS_RUNNER_SPLIT_KEYS", "1") != "0"
+        self._keys_only = self._overlap or self._split_keys
+        if self._keys_only:
             # Per-step packed argmax keys: each step's scorer only writes keys (no in-kernel
             # decode: no last-CTA count, fence or decode at the end of every step), the next
-            # step's fused GRU-gates + rank GEMV decodes the token it needs, and one decode
-            # per call fills the token slots.
+            # step's GRU gates (fused into the rank GEMV, or their own kernel) decode the
+            # token they need, and one decode per call fills the token slots.
             self._step_keys = torch.empty(S, B, dtype=torch.int64, device=device)
             self._key_outs = [ops.ScoreOut(tokens=None, scores=None, keys=self._step_keys[i]) for i in range(S)]
         if self._tc or self._overlap or self._split_gru:
@@ -211,10 +215,11 @@ class DeLSGraphRunner:
         gh = ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh, ws=self._tc_ws)
         return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws)
 
-    def _rank(self, h_cur, step: int):
+    def _rank(self, h_cur, step: int, keys=None):
+        keys = self._keys if keys is None else keys
         if not self._tc:
             ops.rank_gemv(h_cur, self.rank_weight, self._alpha[step : step + 1], self._s_scaled,
-                          bias=self.rank_bias, activation=self._activation, keys=self._keys, ws=self._ws)
+                          bias=self.rank_bias, activation=self._activation, keys=keys, ws=self._ws)
         else:
             ops.rank_project_bf16(h_cur, self.rank_weight, self._alpha[step : step + 1], n_pos=1,
                                   activation=self._activation, s_scaled=self._s_scaled, keys=self._keys,
@@ -230,19 +235,20 @@ class DeLSGraphRunner:
                                   activation=self._activation, keys=self._step_keys[step], ws=self._ws,
                                   tokens_are_keys=step > 0)
             else:
-                ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_prev, h_new, ws=self._ws)
-                self._rank(h_new, step)
+                ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_prev, h_new, ws=self._ws,
+                              tokens_are_keys=self._split_keys and step > 0)
+                self._rank(h_new, step, keys=self._step_keys[step] if self._split_keys else None)
             if step + 1 < self.steps:
                 # the scorer's helper warps compute the next step's gh = bf16(W_hh h_new + b_hh)
                 self._score(step, next_gh=(h_new, self._gh))
             else:
                 self._score(step)
-            if self._overlap:
+            if self._keys_only:
                 tokens = self._step_keys[step]
             else:
                 tokens = self._tokens[step]
             h_prev, gh, cur = h_new, self._gh, cur ^ 1
-        if self._overlap:
+        if self._keys_only:
             ops.keys_decode(self._step_keys.view(-1), tokens=self._tokens.view(-1), with_scores=False)
         self.static_out.copy_(self._tokens.t())
 
@@ -269,7 +275,7 @@ class DeLSGraphRunner:
         return True
 
     def _score(self, step: int, next_gh=None):
-        out = self._key_outs[step] if self._overlap else self._outs[step]
+        out = self._key_outs[step] if self._keys_only else self._outs[step]
         if next_gh is not None:
             h, gh_out = next_gh
             ops.fused_argmax_base_gru_bf16(

@@ -189,9 +189,14 @@ class DraftCorrectionGraphRunner:
                            and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0")
         if self._tc or self._overlap or self._split_gru:
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
-        if self._overlap:
-            # per-step packed argmax keys: keys-only scorer calls, the next step's fused gates
-            # decode the token they need, one decode per call fills the token slots
+        # the split schedule reads the previous step's packed keys in its gates kernel too
+        # (DELS_RUNNER_SPLIT_KEYS=0: each scorer decodes its own tokens)
+        self._split_keys = self._split_gru and os.environ.get("DELS_RUNNER_SPLIT_KEYS", "1") != "0"
+        self._keys_only = self._overlap or self._split_keys
+        if self._keys_only:
+            # per-step packed argmax keys: keys-only scorer calls, the next step's gates (fused
+            # or their own kernel) decode the token they need, one decode per call fills the
+            # token slots
             self._step_keys = torch.empty(max(S, 1), B, dtype=torch.int64, device=device)
             self._key_outs = [ops.ScoreOut(tokens=None, scores=None, keys=self._step_keys[i]) for i in range(S)]
 
@@ -233,8 +238,8 @@ class DraftCorrectionGraphRunner:
         gh_on_scorer = self._overlap or self._split_gru
         for t in range(S):
             last = t + 1 == S
-            keys = self._step_keys[t] if self._overlap else self._keys
-            out = self._key_outs[t] if self._overlap else self._outs[t]
+            keys = self._step_keys[t] if self._keys_only else self._keys
+            out = self._key_outs[t] if self._keys_only else self._outs[t]
             if self._overlap and t > 0:
                 # the previous token's GRU gates fused into this step's correction layer; the
                 # token comes from the previous step's packed key
@@ -246,9 +251,10 @@ class DraftCorrectionGraphRunner:
             elif self._split_gru and t > 0:
                 h_prev, h = h, self._h[cur]
                 cur ^= 1
-                ops.gru_gates(self._tokens[t - 1], self._gru_input_proj_table, self._gh, h_prev, h, ws=self._ws)
-                ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
-                                   ws=self._ws)
+                prev = self._step_keys[t - 1] if self._split_keys else self._tokens[t - 1]
+                ops.gru_gates(prev, self._gru_input_proj_table, self._gh, h_prev, h, ws=self._ws,
+                              tokens_are_keys=self._split_keys)
+                ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=keys, ws=self._ws)
             elif self._tc:
                 ops.correction_mid_tc(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
                                       ws=self._tc_ws)
@@ -267,7 +273,7 @@ class DraftCorrectionGraphRunner:
                 h = self._gru(self._tokens[t], h, self._h[cur])
                 cur ^= 1
         if S > 0:
-            if self._overlap:
+            if self._keys_only:
                 ops.keys_decode(self._step_keys[:S].reshape(-1), tokens=self._tokens[:S].view(-1), with_scores=False)
             self.static_out.copy_(self._tokens[:S].t())
 

@@ -219,10 +219,11 @@ DELS_API int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const
  * tensor-core projection beats one warp per gate row (code/kernel/dels.py:368-373):
  *   r, z = sigmoid(gi + gh), n = tanh(gi_n + r * gh_n), h_out[b] = bf16((1 - z) n + z h_in[b]),
  * gi = gi_table[tokens[b * tok_stride]], h_in NULL = zero state.  Out-of-range ids are
- * clamped and flagged as in dels_gru_step_bf16. */
-DELS_API int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
-                                 const void* gh, int64_t ld_gh, const void* h_in, void* h_out, int B, int G, int V,
-                                 void* ws, void* stream);
+ * clamped and flagged as in dels_gru_step_bf16.  token_keys != 0: tokens[] holds the
+ * previous step's packed (score, index) argmax keys, decoded here. */
+DELS_API int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
+                                 int64_t ld_table, const void* gh, int64_t ld_gh, const void* h_in, void* h_out,
+                                 int B, int G, int V, void* ws, void* stream);
 
 /* The same GRU step for larger batches in two launches: gh = W_hh . h_in as a tensor-core
  * split-K GEMM into fp32 partials (the workspace), then one kernel that sums each unit's
