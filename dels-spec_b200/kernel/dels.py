@@ -4,18 +4,21 @@ Drop-in for ``kernel.dels.DeLSGraphRunner`` of the reference (code/kernel/dels.p
 same constructor keywords, same ``ValueError`` checks, same ``__call__(prefix_ids,
 base_logits) -> LongTensor[B, steps]`` returning a fresh tensor, same static buffers
 (``static_prefix_ids``, ``static_base_logits``, ``static_out``), warm-up on a side
-stream and capture into ``self.graph``.  At 1-2 rows each captured step is two
+stream and capture into ``self.graph``.  At 1-4 rows each captured step is three
 ``libdels_b200.so`` kernels:
 
-  1. the GRU gates of the previous token (input-table row, gh, h) fused into the rank
-     projection + activation + alpha_step scaling, keys reset (``dels_gru_rank_gemv_bf16``);
-  2. the fused scorer on tcgen05 tensor cores: base logits + low-rank logits - beta *
+  1. the GRU gates of the previous token (input-table row, gh, h), the token decoded from
+     the previous step's packed key (``dels_gru_gates_bf16``);
+  2. the rank projection + activation + alpha_step scaling, the step's key slot reset
+     (``dels_rank_gemv_bf16``);
+  3. the fused scorer on tcgen05 tensor cores: base logits + low-rank logits - beta *
      prior, argmax with the lowest index on ties, as the step's packed key, while two
      helper warps per CTA compute the next step's gh = bf16(W_hh h + b_hh), which needs
-     h but not the token (``dels_fused_argmax_base_gru_bf16``).
+     h but not the token (``dels_fused_argmax_base_gru_bf16``);
 
-At 3-4 rows the gates run as their own kernel before the rank GEMV (``dels_gru_gates_bf16``,
-``dels_rank_gemv_bf16``), with the same scorer.  At 5-8 rows a step is the GRU step
+and one keys decode per call fills the tokens.  With ``DELS_RUNNER_OVERLAP_ROWS`` the
+gates of up to that many rows are fused into the rank GEMV instead
+(``dels_gru_rank_gemv_bf16``, two kernels per step; measured slower).  At 5-8 rows a step is the GRU step
 kernel (``dels_gru_step_bf16``), the rank GEMV and the scorer; from ``DELS_RUNNER_TC_ROWS``
 (9) rows up W_hh h and the rank projection run as tensor-core GEMMs
 (``dels_gru_step_tc_bf16``, ``dels_rank_project_bf16``).
@@ -151,12 +154,12 @@ class DeLSGraphRunner:
         # finalisation); below it one warp per weight row does each in a single launch.
         tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "9"))
         self._tc = B >= tc_rows and self.rank_bias is None
-        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 2, at most 4; 0 turns it off) a step is
+        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 0, at most 4) a step is
         # two kernels: the GRU gates fused into the rank projection (dels_gru_rank_gemv_bf16),
         # then the scorer, whose two helper warps per CTA compute the next step's W_hh h
         # (which needs h but not the token) while the others score
         # (dels_fused_argmax_base_gru_bf16).
-        self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "2"))) and not self._tc
+        self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "0"))) and not self._tc
                          and self._scorer_computes_next_gh())
         # The other batches of at most 4 rows (DELS_RUNNER_SPLIT_GRU=0 turns it off): the
         # scorer's helper warps still compute the next W_hh h, and the step's GRU update

@@ -19,8 +19,9 @@ Per call (all on ``libdels_b200.so``):
 
 At 1-4 rows W_hh h of the GRU update moves onto two helper warps per CTA of the scorer
 (``dels_fused_argmax_base_gru_bf16``: it needs h but not the token) and only the gates
-stay between steps: fused into the next step's correction layer at 1-2 rows
-(``dels_gru_correction_mid_bf16``), as their own kernel at 3-4 (``dels_gru_gates_bf16``).
+stay between steps, as their own kernel decoding the previous step's packed key
+(``dels_gru_gates_bf16``; with ``DELS_RUNNER_OVERLAP_ROWS`` fused into the next step's
+correction layer, ``dels_gru_correction_mid_bf16``, measured slower).
 From ``DELS_RUNNER_TC_ROWS`` (9) rows up W_hh h and W_s h run on the tensor-core GEMMs
 (``dels_gru_step_tc_bf16``, ``dels_correction_mid_tc_bf16``).
 
@@ -178,11 +179,11 @@ class DraftCorrectionGraphRunner:
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
             if self.gru_b_hh is not None:
                 self._gh0.copy_(self.gru_b_hh[None, :].expand(B, -1))
-        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 2, at most 4; 0 turns it off) a step
+        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 0, at most 4) a step
         # after the first is two kernels: the previous token's GRU gates fused into the
         # correction layer (dels_gru_correction_mid_bf16), then the scorer, whose helper
         # warps compute the next update's W_hh h (dels_fused_argmax_base_gru_bf16).
-        self._overlap = B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "2"))) and not self._tc
+        self._overlap = B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "0"))) and not self._tc
         # The other batches of at most 4 rows (DELS_RUNNER_SPLIT_GRU=0 turns it off): the same
         # helper warps, with the GRU update reduced to its gates (dels_gru_gates_bf16).
         self._split_gru = (not self._tc and not self._overlap and B <= 4
