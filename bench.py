@@ -816,9 +816,10 @@ def runner_launches(runner, steps: int) -> int:
         return lm + 2 * steps + 1
     if runner._split_gru:  # gates, rank GEMV, scorer (with the next step's W_hh h); keys decode
         return lm + 3 * steps + (1 if runner._keys_only else 0)
+    dec = 1 if getattr(runner, "_keys_only", False) else 0  # one keys decode per call
     if runner._tc:  # gates; per step rank GEMM + finalisation, scorer; W_hh GEMM + gate finalisation
-        return lm + 1 + 3 * steps + (2 if runner._gru_tc_fused else 3) * (steps - 1)
-    return lm + 3 * steps  # GRU step, rank GEMV, scorer
+        return lm + 1 + 3 * steps + (2 if runner._gru_tc_fused else 3) * (steps - 1) + dec
+    return lm + 3 * steps + dec  # GRU step, rank GEMV, scorer
 
 
 def runner_inputs(args, dev):

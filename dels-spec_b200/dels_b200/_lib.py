@@ -75,7 +75,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I,
         [_P, _I64, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P],
     ),
-    "dels_gru_step_bf16": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "dels_gru_step_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "dels_fused_argmax_base_gru_bf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _I, _U32, _P, _P,
                                              _P, _SZ, _P, _P, _P, _I, _P, _P]),
     "dels_gru_correction_mid_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _I64, _P, _P, _I, _I, _I, _P, _I64, _P, _I64,
@@ -86,7 +86,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dels_rank_gemv_bf16": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "dels_gather_scaled_rows_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "dels_gru_step_tc_workspace_bytes": (_SZ, [_I, _I]),
-    "dels_gru_step_tc_bf16": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
+    "dels_gru_step_tc_bf16": (_I, [_P, _I64, _I, _P, _I64, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "dels_linear_workspace_bytes": (_SZ, [_I, _I, _I]),
     "dels_correction_mid_tc_workspace_bytes": (_SZ, [_I, _I, _I]),
     "dels_linear_bf16": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _P, _I64, _P, _SZ, _P]),

@@ -1034,7 +1034,7 @@ int dels_rnn_rank_states_bf16(const void* x, int64_t ld_x, const void* w_in, int
   return DELS_OK;
 }
 
-int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table, int64_t ld_table,
                        const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G, int V,
                        void* ws, void* stream) {
   if (B < 0 || G <= 0 || V <= 0) return fail(DELS_ERR_INVALID_ARG, "bad shape B=%d G=%d V=%d", B, G, V);
@@ -1053,7 +1053,7 @@ int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi
   const int rows_per_pass = runner_rows_per_pass(B);
   DELS_CHECK_PDL("gru_step_kernel launch", launch_pdl(gru_step_kernel_for(rows_per_pass), dim3(cdiv(G, kGruCols)),
       dim3(kGruThreads), gru_smem_bytes(G, rows_per_pass), reinterpret_cast<cudaStream_t>(stream),
-      reinterpret_cast<const long long*>(tokens), tok_stride,
+      reinterpret_cast<const long long*>(tokens), tok_stride, token_keys,
       reinterpret_cast<const __nv_bfloat16*>(gi_table), ld_table,
       reinterpret_cast<const __nv_bfloat16*>(w_hh), reinterpret_cast<const __nv_bfloat16*>(b_hh),
       reinterpret_cast<const __nv_bfloat16*>(h_in), reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V,
@@ -1250,7 +1250,8 @@ size_t dels_gru_step_tc_workspace_bytes(int B, int G) {
   return DELS_WS_HEADER_BYTES + projection_partials_bytes(B, G, 3 * G);
 }
 
-int dels_gru_step_tc_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
+int dels_gru_step_tc_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
+                          int64_t ld_table,
                           const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G, int V,
                           void* ws, size_t ws_bytes, void* stream) {
   int rc;
@@ -1275,7 +1276,7 @@ int dels_gru_step_tc_bf16(const int64_t* tokens, int64_t tok_stride, const void*
   const int grid = (int)(cdiv(total, 256) < 4 * ds->sm_count ? cdiv(total, 256) : 4 * ds->sm_count);
   DELS_CHECK_PDL("gru_finalize_kernel launch", launch_pdl(gru_finalize_kernel, dim3(grid), dim3(256), 0, st,
       partials, plan.splits, (long long)B * plan.ld_out, (long long)plan.ld_out,
-      reinterpret_cast<const long long*>(tokens), (long long)tok_stride,
+      reinterpret_cast<const long long*>(tokens), (long long)tok_stride, token_keys,
       reinterpret_cast<const __nv_bfloat16*>(gi_table), (long long)ld_table,
       reinterpret_cast<const __nv_bfloat16*>(b_hh), reinterpret_cast<const __nv_bfloat16*>(h_in),
       reinterpret_cast<__nv_bfloat16*>(h_out), B, G, V, hdr.status));

@@ -108,7 +108,7 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 // staged, so the weight stream and the h gather overlap.
 template <int MAXB>
 __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long long* __restrict__ tokens,
-                                                               long long tok_stride,
+                                                               long long tok_stride, int token_keys,
                                                                const __nv_bfloat16* __restrict__ table,
                                                                long long ld_table,
                                                                const __nv_bfloat16* __restrict__ w_hh,
@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kGruThreads, 2) gru_step_kernel(const long lon
       const int g = g0 + c;
       if (g >= G) continue;
       long long tok = tokens[(long long)(b0 + b) * tok_stride];
+      if (token_keys) tok = (long long)key_index(tok);  // the scorer's packed (score, index) key
       if (tok < 0 || tok >= V) {
         if (status != nullptr) atomicCAS(status, 0, DELS_ERR_INVALID_ARG);
         tok = tok < 0 ? 0 : V - 1;
@@ -338,7 +339,7 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
 // loaded together, ahead of the sums.
 __global__ void gru_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
                                     long long ld_part, const long long* __restrict__ tokens, long long tok_stride,
-                                    const __nv_bfloat16* __restrict__ table, long long ld_table,
+                                    int token_keys, const __nv_bfloat16* __restrict__ table, long long ld_table,
                                     const __nv_bfloat16* __restrict__ b_hh, const __nv_bfloat16* h_in,
                                     __nv_bfloat16* h_out, int B, int G, int V, int* status) {
   constexpr int kAhead = 4;
@@ -348,6 +349,7 @@ __global__ void gru_finalize_kernel(const float* __restrict__ partials, int spli
        e += (long long)gridDim.x * blockDim.x) {
     const int b = (int)(e / G), g = (int)(e % G);
     long long tok = tokens[(long long)b * tok_stride];
+    if (token_keys) tok = (long long)key_index(tok);  // the scorer's packed (score, index) key
     const float h = h_in != nullptr ? __bfloat162float(h_in[(long long)b * G + g]) : 0.0f;
     float acc[3] = {0.0f, 0.0f, 0.0f};
     for (int s0 = 0; s0 < splits; s0 += kAhead) {

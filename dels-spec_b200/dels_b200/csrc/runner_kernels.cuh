@@ -52,7 +52,7 @@ __device__ __forceinline__ float gru_unit(float gi_r, float gi_z, float gi_n, fl
 
 // gru_step_kernel and rank_gemv_kernel, compiled for 1, 2, 4, 8 or kRunnerMaxB rows per
 // pass (pick with runner_rows_per_pass; other values give the kRunnerMaxB build).
-using GruStepKernel = void (*)(const long long* tokens, long long tok_stride, const __nv_bfloat16* table,
+using GruStepKernel = void (*)(const long long* tokens, long long tok_stride, int token_keys, const __nv_bfloat16* table,
                                long long ld_table, const __nv_bfloat16* w_hh, const __nv_bfloat16* b_hh,
                                const __nv_bfloat16* h_in, __nv_bfloat16* h_out, int B, int G, int V, int* status);
 using RankGemvKernel = void (*)(const __nv_bfloat16* x, long long ld_x, const __nv_bfloat16* w, long long ld_w,
@@ -70,7 +70,7 @@ __global__ void gru_gates_kernel(const long long* __restrict__ tokens, long long
 
 __global__ void gru_finalize_kernel(const float* __restrict__ partials, int splits, long long split_stride,
                                     long long ld_part, const long long* __restrict__ tokens, long long tok_stride,
-                                    const __nv_bfloat16* __restrict__ table, long long ld_table,
+                                    int token_keys, const __nv_bfloat16* __restrict__ table, long long ld_table,
                                     const __nv_bfloat16* __restrict__ b_hh, const __nv_bfloat16* h_in,
                                     __nv_bfloat16* h_out, int B, int G, int V, int* status);
 

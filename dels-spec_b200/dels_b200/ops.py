@@ -543,8 +543,10 @@ def gru_step(
     *,
     b_hh: torch.Tensor | None = None,
     ws: Workspace | None = None,
+    tokens_are_keys: bool = False,
 ) -> torch.Tensor:
-    """h_out = GRU(gi_table[tokens], h_in) with gh = W_hh h_in (+ b_hh); h_in None = zeros."""
+    """h_out = GRU(gi_table[tokens], h_in) with gh = W_hh h_in (+ b_hh); h_in None = zeros.
+    With ``tokens_are_keys`` the tokens are the previous step's packed (score, index) keys."""
     _require_cuda("tokens", tokens, torch.int64)
     _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
     _require_cuda("w_hh", w_hh, torch.bfloat16, 2)
@@ -558,7 +560,8 @@ def gru_step(
     if not h_out.is_contiguous():
         raise ValueError("h_out must be contiguous")
     tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
-    _lib.call("dels_gru_step_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+    _lib.call("dels_gru_step_bf16", _ptr(tokens), tok_stride, int(bool(tokens_are_keys)), _ptr(gi_table),
+              _row_major("gi_table", gi_table),
               _ptr(w_hh), _ptr(b_hh), _ptr(h_in), _ptr(h_out), B, G, V, None if ws is None else ws.ptr,
               _stream(h_out.device))
     return h_out
@@ -603,10 +606,11 @@ def gru_step_tc(
     *,
     b_hh: torch.Tensor | None = None,
     ws: Workspace | None = None,
+    tokens_are_keys: bool = False,
 ) -> torch.Tensor:
     """h_out = GRU(gi_table[tokens], h_in) with gh = bf16(W_hh h_in + b_hh) from a tensor-core
     split-K GEMM whose finalisation evaluates the gates (bit-identical to linear_bf16 followed
-    by gru_gates)."""
+    by gru_gates).  With ``tokens_are_keys`` the tokens are packed (score, index) keys."""
     _require_cuda("tokens", tokens, torch.int64)
     _require_cuda("gi_table", gi_table, torch.bfloat16, 2)
     _require_cuda("w_hh", w_hh, torch.bfloat16, 2)
@@ -621,7 +625,8 @@ def gru_step_tc(
     need = _lib.query("dels_gru_step_tc_workspace_bytes", B, G)
     ws = workspace(need, h_out.device) if ws is None else ws.ensure(need)
     tok_stride = tokens.stride(0) if tokens.dim() >= 1 and tokens.numel() > 1 else 1
-    _lib.call("dels_gru_step_tc_bf16", _ptr(tokens), tok_stride, _ptr(gi_table), _row_major("gi_table", gi_table),
+    _lib.call("dels_gru_step_tc_bf16", _ptr(tokens), tok_stride, int(bool(tokens_are_keys)), _ptr(gi_table),
+              _row_major("gi_table", gi_table),
               _ptr(w_hh), _ptr(b_hh), _ptr(h_in), _ptr(h_out), B, G, V, ws.ptr, ws.nbytes, _stream(h_out.device))
     return h_out
 

@@ -178,7 +178,12 @@ class DeLSGraphRunner:
         # The split schedule reads the previous step's packed keys in its gates kernel too
         # (DELS_RUNNER_SPLIT_KEYS=0: each scorer decodes its own tokens).
         self._split_keys = self._split_gru and os.environ.get("DELS_RUNNER_SPLIT_KEYS", "1") != "0"
-        self._keys_only = self._overlap or self._split_keys
+        # From 5 rows (GRU step kernel or tensor-core GRU, rank projection, scorer) the GRU
+        # reads the previous step's packed keys as well (DELS_RUNNER_PLAIN_KEYS=0: each
+        # scorer decodes its own tokens)
+        self._plain_keys = (not self._overlap and not self._split_gru and self._scorer_computes_next_gh()
+                            and os.environ.get("DELS_RUNNER_PLAIN_KEYS", "1") != "0")
+        self._keys_only = self._overlap or self._split_keys or self._plain_keys
         if self._keys_only:
             # Per-step packed argmax keys: each step's scorer only writes keys (no in-kernel
             # decode: no last-CTA count, fence or decode at the end of every step), the next
@@ -205,18 +210,20 @@ class DeLSGraphRunner:
         with torch.inference_mode(), torch.cuda.graph(self.graph):
             self._forward_impl()
 
-    def _gru(self, tokens, h_in, h_out):
+    def _gru(self, tokens, h_in, h_out, keys: bool = False):
+        # keys: `tokens` holds the previous step's packed argmax keys
         if not self._tc:
             return ops.gru_step(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out, b_hh=self.gru_b_hh,
-                                ws=self._ws)
+                                ws=self._ws, tokens_are_keys=keys)
         if h_in is None:
-            return ops.gru_gates(tokens, self._gru_input_proj_table, self._gh0, h_in, h_out, ws=self._ws)
+            return ops.gru_gates(tokens, self._gru_input_proj_table, self._gh0, h_in, h_out, ws=self._ws,
+                                 tokens_are_keys=keys)
         if self._gru_tc_fused:
             # W_hh h as a split-K GEMM whose finalisation evaluates the gates (one kernel less)
             return ops.gru_step_tc(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out,
-                                   b_hh=self.gru_b_hh, ws=self._tc_ws)
+                                   b_hh=self.gru_b_hh, ws=self._tc_ws, tokens_are_keys=keys)
         gh = ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh, ws=self._tc_ws)
-        return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws)
+        return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws, tokens_are_keys=keys)
 
     def _rank(self, h_cur, step: int, keys=None):
         keys = self._keys if keys is None else keys
@@ -225,7 +232,7 @@ class DeLSGraphRunner:
                           bias=self.rank_bias, activation=self._activation, keys=keys, ws=self._ws)
         else:
             ops.rank_project_bf16(h_cur, self.rank_weight, self._alpha[step : step + 1], n_pos=1,
-                                  activation=self._activation, s_scaled=self._s_scaled, keys=self._keys,
+                                  activation=self._activation, s_scaled=self._s_scaled, keys=keys,
                                   want_state=False, ws=self._tc_ws)
 
     def _forward_gh_on_scorer(self):
@@ -261,12 +268,16 @@ class DeLSGraphRunner:
         prefix = self.static_prefix_ids[:, 0]
         h_cur = self._gru(prefix, None, self._h[0])
         nxt = 1
+        keys = self._plain_keys
         for step in range(self.steps):
-            self._rank(h_cur, step)
+            self._rank(h_cur, step, keys=self._step_keys[step] if keys else None)
             self._score(step)
             if step + 1 < self.steps:
-                h_cur = self._gru(self._tokens[step], h_cur, self._h[nxt])
+                prev = self._step_keys[step] if keys else self._tokens[step]
+                h_cur = self._gru(prev, h_cur, self._h[nxt], keys=keys)
                 nxt ^= 1
+        if keys:
+            ops.keys_decode(self._step_keys.view(-1), tokens=self._tokens.view(-1), with_scores=False)
         self.static_out.copy_(self._tokens.t())
 
     # -- the per-step inputs and scorer; DeLSFusedGraphRunner overrides these ----------

@@ -193,7 +193,11 @@ class DraftCorrectionGraphRunner:
         # the split schedule reads the previous step's packed keys in its gates kernel too
         # (DELS_RUNNER_SPLIT_KEYS=0: each scorer decodes its own tokens)
         self._split_keys = self._split_gru and os.environ.get("DELS_RUNNER_SPLIT_KEYS", "1") != "0"
-        self._keys_only = self._overlap or self._split_keys
+        # from 5 rows the GRU update between steps reads the previous step's packed keys as
+        # well (DELS_RUNNER_PLAIN_KEYS=0: each scorer decodes its own tokens)
+        self._plain_keys = (not self._overlap and not self._split_gru
+                            and os.environ.get("DELS_RUNNER_PLAIN_KEYS", "1") != "0")
+        self._keys_only = self._overlap or self._split_keys or self._plain_keys
         if self._keys_only:
             # per-step packed argmax keys: keys-only scorer calls, the next step's gates (fused
             # or their own kernel) decode the token they need, one decode per call fills the
@@ -213,17 +217,18 @@ class DraftCorrectionGraphRunner:
         with torch.inference_mode(), torch.cuda.graph(self.graph):
             self._forward_impl()
 
-    def _gru(self, tokens, h_in, h_out):
+    def _gru(self, tokens, h_in, h_out, keys: bool = False):
+        # keys: `tokens` holds the previous step's packed argmax keys
         if not self._tc:
             return ops.gru_step(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out, b_hh=self.gru_b_hh,
-                                ws=self._ws)
+                                ws=self._ws, tokens_are_keys=keys)
         if h_in is not None and self._gru_tc_fused:
             # W_hh h as a split-K GEMM whose finalisation evaluates the gates (one kernel less)
             return ops.gru_step_tc(tokens, self._gru_input_proj_table, self.gru_w_hh, h_in, h_out,
-                                   b_hh=self.gru_b_hh, ws=self._tc_ws)
+                                   b_hh=self.gru_b_hh, ws=self._tc_ws, tokens_are_keys=keys)
         gh = self._gh0 if h_in is None else ops.linear_bf16(h_in, self.gru_w_hh, self.gru_b_hh, out=self._gh,
                                                            ws=self._tc_ws)
-        return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws)
+        return ops.gru_gates(tokens, self._gru_input_proj_table, gh, h_in, h_out, ws=self._ws, tokens_are_keys=keys)
 
     def _forward_impl(self):
         B, S, H, M = self.batch_size, self.steps, self.hidden_dim, self._m
@@ -257,7 +262,7 @@ class DraftCorrectionGraphRunner:
                               tokens_are_keys=self._split_keys)
                 ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=keys, ws=self._ws)
             elif self._tc:
-                ops.correction_mid_tc(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=self._keys,
+                ops.correction_mid_tc(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=keys,
                                       ws=self._tc_ws)
             else:
                 ops.correction_mid(h, self.w_s, z[:, t, :], self._alpha, self._s_scaled, keys=keys, ws=self._ws)
@@ -271,7 +276,8 @@ class DraftCorrectionGraphRunner:
                 ops.fused_argmax_base_bf16(base_t, self._s_scaled, self.fc2_weight, self._prior_f32, self._beta,
                                            n_pos=1, keys_ready=True, out=out, ws=self._ws)
             if not last and not gh_on_scorer:
-                h = self._gru(self._tokens[t], h, self._h[cur])
+                prev = self._step_keys[t] if self._plain_keys else self._tokens[t]
+                h = self._gru(prev, h, self._h[cur], keys=self._plain_keys)
                 cur ^= 1
         if S > 0:
             if self._keys_only:

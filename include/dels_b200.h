@@ -209,10 +209,11 @@ DELS_API int dels_rnn_rank_states_bf16(const void* x, int64_t ld_x, const void* 
  *   r, z = sigmoid(gi + gh) (first two G-blocks), n = tanh(gi_n + r * gh_n)
  *   h_out[b] = bf16((1 - z) * n + z * h_in[b])      (h_in NULL = zero state)
  * G % 8 == 0.  Out-of-range token ids are clamped and flagged in the ws status word
- * (DELS_ERR_INVALID_ARG) when ws is given. */
-DELS_API int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
-                                const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G,
-                                int V, void* ws, void* stream);
+ * (DELS_ERR_INVALID_ARG) when ws is given.  token_keys != 0: tokens[] holds the previous
+ * step's packed (score, index) argmax keys, decoded here. */
+DELS_API int dels_gru_step_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
+                                int64_t ld_table, const void* w_hh, const void* b_hh, const void* h_in, void* h_out,
+                                int B, int G, int V, void* ws, void* stream);
 
 /* The gates of the same GRU step when gh = bf16(W_hh . h_in + b_hh) [B, 3G] (row stride
  * ld_gh) was computed separately, e.g. by dels_linear_bf16 for larger batches, where the
@@ -230,11 +231,12 @@ DELS_API int dels_gru_gates_bf16(const int64_t* tokens, int64_t tok_stride, int 
  * three gate columns in split order, adds b_hh (NULL = none) and rounds to bf16 exactly as
  * dels_linear_bf16 writes gh, and evaluates the gates as dels_gru_gates_bf16 does:
  * h_out bit-identical to dels_linear_bf16 followed by dels_gru_gates_bf16.  h_in and w_hh
- * row-major with row stride G (16-byte rows, G % 8 == 0); h_in must not be NULL. */
+ * row-major with row stride G (16-byte rows, G % 8 == 0); h_in must not be NULL;
+ * token_keys as in dels_gru_gates_bf16. */
 DELS_API size_t dels_gru_step_tc_workspace_bytes(int B, int G);
-DELS_API int dels_gru_step_tc_bf16(const int64_t* tokens, int64_t tok_stride, const void* gi_table, int64_t ld_table,
-                                   const void* w_hh, const void* b_hh, const void* h_in, void* h_out, int B, int G,
-                                   int V, void* ws, size_t ws_bytes, void* stream);
+DELS_API int dels_gru_step_tc_bf16(const int64_t* tokens, int64_t tok_stride, int token_keys, const void* gi_table,
+                                   int64_t ld_table, const void* w_hh, const void* b_hh, const void* h_in, void* h_out,
+                                   int B, int G, int V, void* ws, size_t ws_bytes, void* stream);
 
 /* Rank projection for small batches (code/kernel/dels.py:437-443):
  *   s = bf16(act(bf16(x . w^T + bias))), s_scaled = bf16(alpha_p * s), keys[0..B) reset,

@@ -133,11 +133,12 @@ def test_argument_errors_are_reported_before_device_work(lib):
     assert ei.value.status == _lib.DELS_ERR_UNSUPPORTED
     # the tensor-core GRU step: NULL operands, then a misaligned h_in, before any device work
     with pytest.raises(_lib.DelsArgumentError) as ei:
-        _lib.call("dels_gru_step_tc_bf16", None, 1, None, 3072, None, None, None, None, 16, 1024, 100, None, 0, None)
+        _lib.call("dels_gru_step_tc_bf16", None, 1, 0, None, 3072, None, None, None, None, 16, 1024, 100, None, 0,
+                  None)
     assert ei.value.status == _lib.DELS_ERR_INVALID_ARG
     with pytest.raises(_lib.DelsArgumentError) as ei:
-        _lib.call("dels_gru_step_tc_bf16", p, 1, p, 3072, p, None, ctypes.c_void_p(addr), p, 16, 1024, 100, None, 0,
-                  None)
+        _lib.call("dels_gru_step_tc_bf16", p, 1, 0, p, 3072, p, None, ctypes.c_void_p(addr), p, 16, 1024, 100, None,
+                  0, None)
     assert ei.value.status == _lib.DELS_ERR_ALIGNMENT
     assert _lib.query("dels_gru_step_tc_workspace_bytes", 16, 1024) > _lib.DELS_WS_HEADER_BYTES
     # fp32 scorer needs H % 4 == 0

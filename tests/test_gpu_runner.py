@@ -424,3 +424,30 @@ def test_gru_step_tc_matches_linear_then_gates(cuda_device, B):
     gh_ref = O.bf16_round((f(h_in).astype(np.float64) @ f(w_hh).astype(np.float64).T + f(b_hh)).astype(np.float32))
     cell = O.bf16_round(O.gru_cell(f(table)[tokens.cpu().numpy()], gh_ref, f(h_in)).astype(np.float32))
     np.testing.assert_allclose(f(out), cell, rtol=2 ** -7, atol=2e-3)
+
+
+def test_gru_entry_points_read_packed_keys(cuda_device):
+    """The GRU step, the tensor-core GRU step and the gates kernel give the same h whether
+    the previous tokens come as ids or as the scorer's packed (score, index) keys."""
+    from dels_b200 import ops
+
+    dev = cuda_device
+    rng = np.random.default_rng(1300)
+    B, V, G = 10, 503, 128
+    bf = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev).to(torch.bfloat16)  # noqa: E731
+    table = bf(rng.standard_normal((V, 3 * G)) * 0.5)
+    w_hh = bf(rng.standard_normal((3 * G, G)) * 0.05)
+    h_in = bf(rng.standard_normal((B, G)) * 0.5)
+    gh = bf(rng.standard_normal((B, 3 * G)) * 0.5)
+    tok = rng.integers(0, V, B)
+    ids = torch.from_numpy(tok).to(dev)
+    keys = torch.from_numpy(O.pack_keys(rng.standard_normal(B).astype(np.float32), tok)).to(dev)
+    for run in (lambda t, o, k: ops.gru_step(t, table, w_hh, h_in, o, tokens_are_keys=k),
+                lambda t, o, k: ops.gru_step_tc(t, table, w_hh, h_in, o, tokens_are_keys=k),
+                lambda t, o, k: ops.gru_gates(t, table, gh, h_in, o, tokens_are_keys=k)):
+        a = torch.empty(B, G, dtype=torch.bfloat16, device=dev)
+        b = torch.empty(B, G, dtype=torch.bfloat16, device=dev)
+        run(ids, a, False)
+        run(keys, b, True)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
