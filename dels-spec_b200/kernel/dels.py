@@ -154,16 +154,17 @@ class DeLSGraphRunner:
         # finalisation); below it one warp per weight row does each in a single launch.
         tc_rows = int(os.environ.get("DELS_RUNNER_TC_ROWS", "9"))
         self._tc = B >= tc_rows and self.rank_bias is None
-        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 0, at most 4) a step is
-        # two kernels: the GRU gates fused into the rank projection (dels_gru_rank_gemv_bf16),
+        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 0: off; at most 4) a step is two
+        # kernels: the GRU gates fused into the rank projection (dels_gru_rank_gemv_bf16),
         # then the scorer, whose two helper warps per CTA compute the next step's W_hh h
         # (which needs h but not the token) while the others score
-        # (dels_fused_argmax_base_gru_bf16).
+        # (dels_fused_argmax_base_gru_bf16).  Measured slower than the split schedule below
+        # once that one was keys-only.
         self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "0"))) and not self._tc
                          and self._scorer_computes_next_gh())
-        # The other batches of at most 4 rows (DELS_RUNNER_SPLIT_GRU=0 turns it off): the
-        # scorer's helper warps still compute the next W_hh h, and the step's GRU update
-        # shrinks to the gates (dels_gru_gates_bf16) before the rank GEMV, three kernels.
+        # Batches of at most 4 rows by default (DELS_RUNNER_SPLIT_GRU=0 turns it off): the
+        # scorer's helper warps compute the next W_hh h, and the step's GRU update shrinks
+        # to the gates (dels_gru_gates_bf16) before the rank GEMV, three kernels.
         # Above 4 rows the helpers' work, which grows with the rows, outlasts the scorer.
         self._split_gru = (not self._tc and not self._overlap and B <= 4
                            and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0"
