@@ -179,12 +179,12 @@ class DraftCorrectionGraphRunner:
             self._gh0 = torch.zeros(B, 3 * G, dtype=dtype, device=device)
             if self.gru_b_hh is not None:
                 self._gh0.copy_(self.gru_b_hh[None, :].expand(B, -1))
-        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 0, at most 4) a step
+        # Up to DELS_RUNNER_OVERLAP_ROWS rows (default 0: off; at most 4) a step
         # after the first is two kernels: the previous token's GRU gates fused into the
         # correction layer (dels_gru_correction_mid_bf16), then the scorer, whose helper
         # warps compute the next update's W_hh h (dels_fused_argmax_base_gru_bf16).
         self._overlap = B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "0"))) and not self._tc
-        # The other batches of at most 4 rows (DELS_RUNNER_SPLIT_GRU=0 turns it off): the same
+        # Batches of at most 4 rows by default (DELS_RUNNER_SPLIT_GRU=0 turns it off): the same
         # helper warps, with the GRU update reduced to its gates (dels_gru_gates_bf16).
         self._split_gru = (not self._tc and not self._overlap and B <= 4
                            and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0")
