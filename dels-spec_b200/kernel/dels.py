@@ -179,10 +179,10 @@ class DeLSGraphRunner:
         # The split schedule reads the previous step's packed keys in its gates kernel too
         # (DELS_RUNNER_SPLIT_KEYS=0: each scorer decodes its own tokens).
         self._split_keys = self._split_gru and os.environ.get("DELS_RUNNER_SPLIT_KEYS", "1") != "0"
-        # From 5 rows (GRU step kernel or tensor-core GRU, rank projection, scorer) the GRU
-        # reads the previous step's packed keys as well (DELS_RUNNER_PLAIN_KEYS=0: each
-        # scorer decodes its own tokens)
-        self._plain_keys = (not self._overlap and not self._split_gru and self._scorer_computes_next_gh()
+        # From 5 rows (GRU step kernel or tensor-core GRU, rank projection, scorer), and in
+        # DeLSFusedGraphRunner at every batch, the GRU reads the previous step's packed keys
+        # as well (DELS_RUNNER_PLAIN_KEYS=0: each scorer decodes its own tokens)
+        self._plain_keys = (not self._overlap and not self._split_gru
                             and os.environ.get("DELS_RUNNER_PLAIN_KEYS", "1") != "0")
         self._keys_only = self._overlap or self._split_keys or self._plain_keys
         if self._keys_only:
@@ -375,8 +375,8 @@ class DeLSFusedGraphRunner(DeLSGraphRunner):
             raise RuntimeError("the per-step fused scorer does not compute the GRU projection")
         ops.fused_argmax_bf16(
             self.static_parallel_hiddens[:, step, :], self._lm_weight, self._s_scaled, self.lm_head_weight,
-            self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True, out=self._outs[step],
-            ws=self._ws,
+            self._prior_f32, self._beta[step : step + 1], n_pos=1, keys_ready=True,
+            out=self._key_outs[step] if self._keys_only else self._outs[step], ws=self._ws,
         )
 
     @torch.inference_mode()
