@@ -237,6 +237,7 @@ int init_device(int dev) {
     SET((tc_skinny_kernel<16>), (SkinnyConfig<16, false>::kSmemBytes));
     SET((tc_skinny_gh_kernel<16, 1>), (SkinnyConfig<16, false>::kSmemBytes));
     SET((tc_skinny_gh_kernel<16, kSkinnyGhMaxB>), (SkinnyConfig<16, false>::kSmemBytes));
+    SET((tc_skinny_gh_kernel<16, kSkinnyGhRows>), (SkinnyConfig<16, false>::kSmemBytes));
     SET((tc_skinny_staged_kernel<16>), SkinnyConfig<16>::kSmemBytes);
     SET((tc_skinny_kernel<32>), (SkinnyConfig<32, false>::kSmemBytes));
     SET((tc_skinny_staged_kernel<32>), SkinnyConfig<32>::kSmemBytes);
@@ -409,10 +410,12 @@ int launch_skinny(const TcOperands& op, TcArgs args, int sm_count, cudaStream_t 
   const int grid = tiles < sm_count ? tiles : sm_count;
   if (grid <= 0) return DELS_OK;
   if constexpr (GH) {
-    // one-row rollouts get the epilogue and the helper GEMV compiled for one row
-    DELS_CHECK_PDL("tc_skinny_gh_kernel launch",
-        launch_pdl(args.m_rows <= 1 ? tc_skinny_gh_kernel<NB, 1> : tc_skinny_gh_kernel<NB, kSkinnyGhMaxB>, dim3(grid),
-                   dim3(kSkinnyGhThreads), SkinnyConfig<NB, false>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
+    // the epilogue and the helper GEMV compiled for the fewest rows that hold the batch
+    auto kernel = args.m_rows <= 1 ? tc_skinny_gh_kernel<NB, 1>
+                  : (args.m_rows <= kSkinnyGhMaxB ? tc_skinny_gh_kernel<NB, kSkinnyGhMaxB>
+                                                  : tc_skinny_gh_kernel<NB, kSkinnyGhRows>);
+    DELS_CHECK_PDL("tc_skinny_gh_kernel launch", launch_pdl(kernel, dim3(grid), dim3(kSkinnyGhThreads),
+        SkinnyConfig<NB, false>::kSmemBytes, st, wa0, rb0, wa1, rb1, args));
   } else if constexpr (SB) {
     DELS_CHECK_PDL("tc_skinny_staged_kernel launch", launch_pdl(tc_skinny_staged_kernel<NB>, dim3(grid),
         dim3(kTcThreads), SkinnyConfig<NB>::kSmemBytes, st, wa0, rb0, wa1, rb1, mbase, mprior, args));
@@ -638,9 +641,9 @@ int fused_argmax_common(const void* h, long long ld_h, const void* W, long long 
   const bool vec_base = base != nullptr && aligned16(base) && (ld_base % 8) == 0;
   if (gh != nullptr) {
     // the next step's W_hh h on the plain skinny scorer's helper warps
-    if (!(rows <= kSkinnyStageRows && g_use_skinny))
+    if (!(rows <= kSkinnyGhRows && g_use_skinny))
       return fail(DELS_ERR_UNSUPPORTED, "the fused gh projection needs at most %d rows and the skinny scorer",
-                  kSkinnyStageRows);
+                  kSkinnyGhRows);
     a.gh_w = gh->gh_w;
     a.gh_bias = gh->gh_bias;
     a.gh_x = gh->gh_x;
@@ -771,8 +774,7 @@ int dels_fused_argmax_base_gru_bf16(const void* base, int64_t ld_base, const voi
   if (w_hh == nullptr || h == nullptr || gh_out == nullptr) return fail(DELS_ERR_INVALID_ARG, "NULL GRU operand");
   if (G <= 0 || (G % 8) != 0 || !aligned16(w_hh) || !aligned16(h))
     return fail(DELS_ERR_ALIGNMENT, "GRU hidden size %d must be a multiple of 8, w_hh and h 16-byte aligned", G);
-  if (rows > kSkinnyStageRows)
-    return fail(DELS_ERR_UNSUPPORTED, "at most %d rows (got %d)", kSkinnyStageRows, rows);
+  if (rows > kSkinnyGhRows) return fail(DELS_ERR_UNSUPPORTED, "at most %d rows (got %d)", kSkinnyGhRows, rows);
   TcArgs gh;
   std::memset(&gh, 0, sizeof(gh));
   gh.gh_w = reinterpret_cast<const __nv_bfloat16*>(w_hh);

@@ -33,7 +33,8 @@ namespace dels {
 
 constexpr int kSkinnyBM = 128;  // vocab rows per tile (MMA M)
 constexpr int kSkinnyGhThreads = kTcThreads + 64;  // + two helper warps (tc_skinny_gh_kernel)
-constexpr int kSkinnyGhMaxB = 4;                   // most rows of the helpers' GEMV
+constexpr int kSkinnyGhMaxB = 4;                   // rows of the helpers' 4-row GEMV build
+constexpr int kSkinnyGhRows = 8;                   // most rows of the scorer with helpers
 
 // STAGE = false (the plain variant) leaves out the epilogue-operand buffers.  More stages
 // for it (12 at NB = 16) measured slower in the batch-1 rollout.

@@ -162,11 +162,13 @@ class DeLSGraphRunner:
         # once that one was keys-only.
         self._overlap = (B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "0"))) and not self._tc
                          and self._scorer_computes_next_gh())
-        # Batches of at most 4 rows by default (DELS_RUNNER_SPLIT_GRU=0 turns it off): the
-        # scorer's helper warps compute the next W_hh h, and the step's GRU update shrinks
-        # to the gates (dels_gru_gates_bf16) before the rank GEMV, three kernels.
-        # Above 4 rows the helpers' work, which grows with the rows, outlasts the scorer.
-        self._split_gru = (not self._tc and not self._overlap and B <= 4
+        # Batches of at most DELS_RUNNER_SPLIT_ROWS rows (default 4, at most 8;
+        # DELS_RUNNER_SPLIT_GRU=0 turns it off): the scorer's helper warps compute the next
+        # W_hh h, and the step's GRU update shrinks to the gates (dels_gru_gates_bf16)
+        # before the rank GEMV, three kernels.  From 5 rows the helpers' work, which grows
+        # with the rows, outlasts this runner's scorer (Vr, 78 MB per step).
+        self._split_gru = (not self._tc and not self._overlap
+                           and B <= min(8, int(os.environ.get("DELS_RUNNER_SPLIT_ROWS", "4")))
                            and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0"
                            and self._scorer_computes_next_gh())
         if self._tc:

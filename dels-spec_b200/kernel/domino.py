@@ -17,7 +17,7 @@ Per call (all on ``libdels_b200.so``):
                                                      (prior = b2, beta = -alpha)
     h = GRUCell(table[tok], h)                       ``dels_gru_step_bf16``
 
-At 1-4 rows W_hh h of the GRU update moves onto two helper warps per CTA of the scorer
+At 1-8 rows W_hh h of the GRU update moves onto two helper warps per CTA of the scorer
 (``dels_fused_argmax_base_gru_bf16``: it needs h but not the token) and only the gates
 stay between steps, as their own kernel decoding the previous step's packed key
 (``dels_gru_gates_bf16``; with ``DELS_RUNNER_OVERLAP_ROWS`` fused into the next step's
@@ -184,17 +184,20 @@ class DraftCorrectionGraphRunner:
         # correction layer (dels_gru_correction_mid_bf16), then the scorer, whose helper
         # warps compute the next update's W_hh h (dels_fused_argmax_base_gru_bf16).
         self._overlap = B <= min(4, int(os.environ.get("DELS_RUNNER_OVERLAP_ROWS", "0"))) and not self._tc
-        # Batches of at most 4 rows by default (DELS_RUNNER_SPLIT_GRU=0 turns it off): the same
-        # helper warps, with the GRU update reduced to its gates (dels_gru_gates_bf16).
-        self._split_gru = (not self._tc and not self._overlap and B <= 4
+        # Batches of at most DELS_RUNNER_SPLIT_ROWS rows (default 8, at most 8;
+        # DELS_RUNNER_SPLIT_GRU=0 turns it off): the same helper warps, with the GRU update
+        # reduced to its gates (dels_gru_gates_bf16).  This scorer streams fc2 (311 MB per
+        # step), long enough to hide the helpers' W_hh h at 5-8 rows too.
+        self._split_gru = (not self._tc and not self._overlap
+                           and B <= min(8, int(os.environ.get("DELS_RUNNER_SPLIT_ROWS", "8")))
                            and os.environ.get("DELS_RUNNER_SPLIT_GRU", "1") != "0")
         if self._tc or self._overlap or self._split_gru:
             self._gh = torch.empty(B, 3 * G, dtype=dtype, device=device)
         # the split schedule reads the previous step's packed keys in its gates kernel too
         # (DELS_RUNNER_SPLIT_KEYS=0: each scorer decodes its own tokens)
         self._split_keys = self._split_gru and os.environ.get("DELS_RUNNER_SPLIT_KEYS", "1") != "0"
-        # from 5 rows the GRU update between steps reads the previous step's packed keys as
-        # well (DELS_RUNNER_PLAIN_KEYS=0: each scorer decodes its own tokens)
+        # outside the split schedule the GRU update between steps reads the previous step's
+        # packed keys as well (DELS_RUNNER_PLAIN_KEYS=0: each scorer decodes its own tokens)
         self._plain_keys = (not self._overlap and not self._split_gru
                             and os.environ.get("DELS_RUNNER_PLAIN_KEYS", "1") != "0")
         self._keys_only = self._overlap or self._split_keys or self._plain_keys

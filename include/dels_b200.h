@@ -252,8 +252,8 @@ DELS_API int dels_rank_gemv_bf16(const void* x, int64_t ld_x, const void* w, int
  * same launch: gh_out[b] = bf16(w_hh . h[b] + b_hh), w_hh [3G, G], h [rows, G] (the
  * state after this step's GRU update), gh_out [rows, 3G] (code/kernel/dels.py:366,
  * F.linear(h_state, W_hh, b_hh)).  It needs h but not this step's token, so two extra
- * warps per CTA compute it while the others score, and the next step's
- * dels_gru_rank_gemv_bf16 starts from it.  At most 4 rows; G % 8 == 0. */
+ * warps per CTA compute it while the others score, and the next step's GRU gates
+ * (dels_gru_gates_bf16 or dels_gru_rank_gemv_bf16) start from it.  At most 8 rows; G % 8 == 0. */
 DELS_API int dels_fused_argmax_base_gru_bf16(const void* base, int64_t ld_base, const void* s_scaled, int64_t ld_s,
                                              const void* Vr, int64_t ld_vr, const float* prior, const float* beta,
                                              int n_pos, int rows, int r, int V, uint32_t flags, int64_t* keys,

@@ -124,11 +124,11 @@ def test_argument_errors_are_reported_before_device_work(lib):
                   ctypes.c_void_p(addr), 3072, None, ctypes.c_void_p(addr), 1, 1024, 100, None, 1024,
                   ctypes.c_void_p(addr), 1024, 1024, None, None, None, None, None)
     assert ei.value.status == _lib.DELS_ERR_ALIGNMENT
-    # the scorer with the next GRU projection takes at most 4 rows
+    # the scorer with the next GRU projection takes at most 8 rows
     ok = (ctypes.c_char * 256)()
     p = ctypes.c_void_p((ctypes.addressof(ok) + 15) & ~15)
     with pytest.raises(_lib.DelsError) as ei:
-        _lib.call("dels_fused_argmax_base_gru_bf16", p, 1000, p, 64, p, 64, None, None, 1, 5, 64, 1000, 0, None,
+        _lib.call("dels_fused_argmax_base_gru_bf16", p, 1000, p, 64, p, 64, None, None, 1, 9, 64, 1000, 0, None,
                   None, p, 256, p, None, p, 1024, p, None)
     assert ei.value.status == _lib.DELS_ERR_UNSUPPORTED
     # the tensor-core GRU step: NULL operands, then a misaligned h_in, before any device work

@@ -272,3 +272,37 @@ def test_domino_runner_batch20_with_biases(cuda_device):
         b2=prm["embed_proj_2_bias"],
     )
     assert _compare(out, gaps, toks, 1e-2) >= B * S // 2
+
+
+@pytest.mark.parametrize("B", [6, 8])
+def test_domino_runner_split_schedule_5_to_8_rows(cuda_device, B):
+    """5-8 rows: the gates kernel, the correction layer and the scorer whose helper warps
+    (built for 8 rows) compute the next W_hh h, every bias present, against the oracle."""
+    from kernel.domino import DraftCorrectionGraphRunner
+
+    V, H, G, M, S, P, alpha = 3001, 64, 48, 40, 4, 2, 0.8
+    gen = torch.Generator(device="cpu").manual_seed(47 + B)
+    draft = _Draft(H, G, M, V, True)
+    with torch.no_grad():
+        for prm in draft.parameters():
+            prm.copy_((torch.randn(prm.shape, generator=gen) * 0.2).to(torch.bfloat16).float())
+    embed = (torch.randn(V, H, generator=gen) * 0.5).to(torch.bfloat16).float().numpy()
+    hiddens = (torch.randn(B, S, H, generator=gen)).to(torch.bfloat16).float().numpy()
+    base = (torch.randn(B, S, V, generator=gen)).to(torch.bfloat16).float().numpy()
+    prefix = torch.randint(0, V, (B, P), generator=gen).numpy()
+    prm = {k.replace(".", "_"): p.detach().numpy().copy() for k, p in draft.named_parameters()}
+    runner = DraftCorrectionGraphRunner(
+        draft_model=draft.to(cuda_device, torch.bfloat16), target_model=_target(embed, cuda_device), batch_size=B,
+        steps=S, hidden_dim=H, gru_hidden_dim=G, vocab_size=V, prefix_token_count=P, device=cuda_device,
+        guidance_alpha=alpha,
+    )
+    assert runner._split_gru and runner._keys_only and not runner._tc
+    out = runner(torch.from_numpy(prefix).to(cuda_device), _bf16(hiddens, cuda_device),
+                 _bf16(base, cuda_device)).cpu().numpy()
+    toks, gaps = O.domino_runner_rollout(
+        prefix, hiddens, base, alpha=alpha, bf16=True, embed=embed, w_ih=prm["prefix_gru_weight_ih_l0"],
+        w_hh=prm["prefix_gru_weight_hh_l0"], b_ih=prm["prefix_gru_bias_ih_l0"], b_hh=prm["prefix_gru_bias_hh_l0"],
+        w1=prm["embed_proj_0_weight"], b1=prm["embed_proj_0_bias"], fc2=prm["embed_proj_2_weight"],
+        b2=prm["embed_proj_2_bias"],
+    )
+    assert _compare(out, gaps, toks, 1e-2) >= B * S // 2

@@ -154,7 +154,7 @@ def test_runner_full_vocab_b1(cuda_device):
     assert _compare(out.cpu().numpy(), gaps, toks, 1e-2) >= 3
 
 
-@pytest.mark.parametrize("B", [1, 3, 4])
+@pytest.mark.parametrize("B", [1, 3, 4, 5, 8])
 def test_scorer_with_next_gru_projection(cuda_device, B):
     """dels_fused_argmax_base_gru_bf16: the same tokens as the plain base-logit scorer, and
     gh_out within one bf16 rounding of bf16(W_hh h + b_hh) (helper warps' fp32 sums)."""
@@ -239,6 +239,41 @@ def test_gru_gates_from_packed_keys(cuda_device, B):
         for a, b in zip(*outs):
             assert torch.equal(a, b), entry
     ws.check()
+
+
+@pytest.mark.parametrize("B", [5, 8])
+def test_runner_split_schedule_up_to_8_rows(cuda_device, monkeypatch, B):
+    """The split schedule (gates kernel, rank GEMV, scorer whose helper warps compute the
+    next W_hh h) at 5-8 rows, where the scorer stages its epilogue operands: tokens against
+    the oracle rollout."""
+    from kernel.dels import DeLSGraphRunner
+
+    monkeypatch.setenv("DELS_RUNNER_SPLIT_ROWS", "8")
+    rng = np.random.default_rng(120 + B)
+    V, E, G, r, steps = 2003, 40, 64, 32, 4
+    w = {
+        "embed": O.bf16_round((rng.standard_normal((V, E)) * 0.5).astype(np.float32)),
+        "w_ih": O.bf16_round((rng.standard_normal((3 * G, E)) * 0.2).astype(np.float32)),
+        "w_hh": O.bf16_round((rng.standard_normal((3 * G, G)) * 0.2).astype(np.float32)),
+        "w_rank": O.bf16_round((rng.standard_normal((r, G)) * 0.3).astype(np.float32)),
+        "Vr": O.bf16_round((rng.standard_normal((V, r)) * 0.3).astype(np.float32)),
+    }
+    head = _head(cuda_device, V, E, G, r, "identity", w)
+    prior = O.bf16_round(O.zipf_log_prior(V).astype(np.float32))
+    alpha = list(np.linspace(0.9, 0.5, steps))
+    beta = list(np.linspace(0.3, 0.1, steps))
+    runner = DeLSGraphRunner(local_head=head, batch_size=B, steps=steps, vocab_size=V, alpha_values=alpha,
+                             beta_values=beta, baseline_logits=torch.from_numpy(prior).to(cuda_device),
+                             device=cuda_device)
+    assert runner._split_gru and runner._keys_only
+    base = O.bf16_round(rng.standard_normal((B, steps, V)).astype(np.float32))
+    prefix = rng.integers(0, V, (B, 1))
+    out = runner(torch.from_numpy(prefix).to(cuda_device),
+                 torch.from_numpy(base).to(cuda_device).to(torch.bfloat16)).cpu().numpy()
+    toks, gaps = O.dels_runner_rollout(prefix, base, embed=w["embed"], w_ih=w["w_ih"], w_hh=w["w_hh"],
+                                       w_rank=w["w_rank"], Vr=w["Vr"], prior=prior, alpha=alpha, beta=beta,
+                                       bf16=True)
+    assert _compare(out, gaps, toks, 1e-2) >= B * steps // 2
 
 
 @pytest.mark.parametrize("B", [4, 5, 12, 20, 48, 64])
