@@ -62,8 +62,9 @@ struct SkinnyConfig {
 // the K blocks of the two segments (kb0 = 0 for the base-logit variant).  With STAGE:
 // `map_base` = base logits [rows, V slice] in 128 x NB boxes (when args.base is set) and
 // `map_prior` = the prior [V slice] fp32 in 128-element boxes (when args.prior is set).
-// GH: warps 6 and 7 compute args.gh_out (the next rollout step's W_hh h), one output row
-// per warp at a time over a grid-wide stride, while warps 0-5 score.  RB (<= NB) bounds
+// GH: warps 6 and 7 compute args.gh_out (the next rollout step's W_hh h) for up to GHB
+// rows, four output rows per warp at a time over a grid-wide stride, while warps 0-5
+// score.  RB (<= NB) bounds
 // the rows the epilogue scores at compile time: the MMA still computes NB columns, but a
 // batch-1 step does not issue (predicated-off) epilogue arithmetic for the other 15.
 template <int NB, bool STAGE, bool GH = false, int GHB = kSkinnyGhMaxB, int RB = NB>
